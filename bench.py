@@ -1,0 +1,319 @@
+"""Benchmark: Q16.48 matvec microbench (config 1) on B200 through libiq.so.
+
+A step = one pass of matmul_vec over the five config-1 shapes
+(K x N = 2048x2048, 2048x256, 2048x5632, 5632x2048, 2048x32000), weights and
+activations already resident in HBM (712 MiB of int64 weights per step: the
+working set exceeds the 126 MB L2, so each shape is read cold from HBM).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun: every rank runs the whole workload on its own GPU
+(independent matvecs, no data-path collective: weak scaling); time is the max
+over ranks. `--impl reference` times the reference's own CPU matmul_vec
+(oracle/_ref, llama_int.c:1014) on the host cores, rows split across threads.
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(ROOT, "int-llm_b200")]
+import configs  # noqa: E402
+
+METRIC = "Q16.48 matvec throughput, config 1 (M=1, 5 TinyLlama shapes), bit-exact"
+UNIT = "GMAC/s"
+SHAPES = configs.CFG1_SHAPES
+MACS_PER_STEP = sum(K * N for K, N in SHAPES)
+BYTES_PER_STEP = sum(8 * (K * N + K + N) for K, N in SHAPES)
+
+
+def env_int(k, d):
+    return int(os.environ.get(k, d))
+
+
+def workload_config():
+    return {"workload": "config1_matvec_M1",
+            "shapes_KxN": [f"{K}x{N}" for K, N in SHAPES],
+            "weights": "bf16-representable N(0,0.02) in Q16.48 (seeded)",
+            "activations": "uniform [-8,8) Q16.48 (seeded)",
+            "l2": "inputs larger than L2: 712 MiB of weights cycled per step",
+            "parallelism": "independent replicas per GPU (weak scaling)"}
+
+
+def synth_inputs():
+    """Seeded config-1 inputs from the library's own generator (iq_synth_*)."""
+    import iq
+    return [(iq.synth_weights(1, configs.matvec_names(K, N)[0], (N, K)),
+             iq.synth_acts(1, configs.matvec_names(K, N)[1], (K,))) for K, N in SHAPES]
+
+
+class Clocks:
+    """nvidia-smi sampler running during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.Q,
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        out, _ = self.p.communicate(timeout=10)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def load_traffic():
+    """dram bytes per launch of the dominant kernel from the committed ncu summary."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get("k_matvec_per_step_bytes")
+    except Exception:
+        return None
+
+
+# ------------------------------------------------------------------ CPU legs
+
+def cpu_reference_lib():
+    """The reference's own matmul_vec compiled from source (oracle/_ref), else
+    the oracle's C restatement. Returns (callable(out,w,x,M,N,threads), kind)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    R = orc.ref()
+    if R is not None:
+        return (lambda o, w, x, M, N, t: R.ref_matmul_vec_mt(orc.p(o), orc.p(w), orc.p(x), M, N, t)), "reference"
+    return (lambda o, w, x, M, N, t: orc.O.iqo_matmul_vec(orc.p(o), orc.p(w), orc.p(x), M, N)), "port"
+
+
+def cpu_step(fn, ins, outs, threads):
+    for (w, x), o, (K, N) in zip(ins, outs, SHAPES):
+        fn(o, w, x, N, K, threads)
+
+
+def cpu_baseline(ins, budget_s=10.0):
+    """Single-thread reference matmul_vec over whole config-1 steps, ~budget_s."""
+    fn, kind = cpu_reference_lib()
+    outs = [np.empty(N, np.int64) for K, N in SHAPES]
+    cpu_step(fn, ins, outs, 1)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s:
+        cpu_step(fn, ins, outs, 1)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": MACS_PER_STEP * n / dt / 1e9, "unit": UNIT, "cores": 1, "kind": kind,
+            "sample": f"{n} whole config-1 steps ({MACS_PER_STEP} MAC each), single thread, "
+                      f"{dt:.1f} s; host {os.cpu_count()} cpus"}
+
+
+def run_reference(args):
+    rank = env_int("RANK", 0)
+    if rank != 0:
+        return
+    ins = synth_inputs()
+    fn, kind = cpu_reference_lib()
+    threads = os.cpu_count() or 1
+    outs = [np.empty(N, np.int64) for K, N in SHAPES]
+    for _ in range(args.warmup):
+        cpu_step(fn, ins, outs, threads)
+    t0 = time.perf_counter()
+    done = 0
+    for _ in range(args.steps):   # bounded: stops early after 60 s of CPU work
+        cpu_step(fn, ins, outs, threads)
+        done += 1
+        if time.perf_counter() - t0 > 60.0:
+            break
+    dt = time.perf_counter() - t0
+    v = MACS_PER_STEP * done / dt / 1e9
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": done, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int64",
+        "data": "synthetic", "config": workload_config(),
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": f"{args.steps} whole config-1 steps, rows split over {threads} threads"},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+
+
+# ------------------------------------------------------------------ GPU leg
+
+def run_ours(args):
+    import torch
+    import iq
+    rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    iq.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    ins = synth_inputs()
+    dev = [(torch.from_numpy(w).cuda(), torch.from_numpy(x).cuda()) for w, x in ins]
+    outs = [torch.empty(N, dtype=torch.int64, device="cuda") for K, N in SHAPES]
+    s = torch.cuda.Stream()
+    L = iq.lib()
+    sp = ctypes.c_void_p(s.cuda_stream)
+    ptrs = [(ctypes.c_void_p(o.data_ptr()), ctypes.c_void_p(w.data_ptr()), ctypes.c_void_p(x.data_ptr()))
+            for o, (w, x) in zip(outs, dev)]
+
+    def step(evs=None):
+        for i, ((po, pw, px), (K, N)) in enumerate(zip(ptrs, SHAPES)):
+            if evs is not None:
+                evs[i][0].record(s)
+            rc = L.iq_matvec_dev(po, pw, px, N, K, sp)
+            if rc:
+                raise iq.IQError("iq_matvec_dev", rc, L)
+            if evs is not None:
+                evs[i][1].record(s)
+
+    # warm-up (the device results are compared with the drop-in path's below)
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+
+    # timed region: K steps, CUDA events on the launching stream, per-launch events
+    nev = args.steps * len(SHAPES)
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            for _ in SHAPES] for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = Clocks(local)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk.start()
+    time.sleep(0.3)
+    t_start.record(s)
+    for k in range(args.steps):
+        step(evs[k])
+    t_end.record(s)
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    if dist:
+        dist.barrier()
+    ms_total = t_start.elapsed_time(t_end)
+    per_shape_ms = [0.0] * len(SHAPES)
+    for k in range(args.steps):
+        for i in range(len(SHAPES)):
+            per_shape_ms[i] += evs[k][i][0].elapsed_time(evs[k][i][1])
+    kern_ms = sum(per_shape_ms)
+    if dist:
+        t = torch.tensor([ms_total, kern_ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total, kern_ms = t.tolist()
+
+    # e2e: the public host-pointer drop-in iq_matmul_vec, pinned host buffers,
+    # H2D of x and D2H of out inside the timed region every call
+    hx = [torch.from_numpy(x).pin_memory().numpy() for w, x in ins]
+    ho = [torch.empty(N, dtype=torch.int64).pin_memory().numpy() for K, N in SHAPES]
+    for (w, x), (K, N) in zip(ins, SHAPES):
+        iq.weight_register(w, N, K)
+    e2e_steps = max(10, args.steps // 10)
+
+    def e2e_step():
+        for (w, x), hxx, hoo, (K, N) in zip(ins, hx, ho, SHAPES):
+            iq.matmul_vec(hoo, w, hxx, N, K)
+    for _ in range(3):
+        e2e_step()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = t.item()
+    # the drop-in result must equal the device path's (same inputs)
+    for o, hoo in zip(outs, ho):
+        assert (o.cpu().numpy() == hoo).all(), "drop-in and device path disagree"
+
+    if rank != 0:
+        if dist:
+            dist.destroy_process_group()
+        return
+    peak, peak_kind = measured_peak()
+    achieved = BYTES_PER_STEP * args.steps / (kern_ms / 1e3) / 1e9
+    traffic = load_traffic()
+    line = {
+        "metric": METRIC, "value": MACS_PER_STEP * args.steps * world / (ms_total / 1e3) / 1e9,
+        "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_total / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int64", "data": "synthetic", "config": workload_config(),
+        "gb_per_s_per_gpu": BYTES_PER_STEP * args.steps / (ms_total / 1e3) / 1e9,
+        "per_shape_gbs": {f"{K}x{N}": 8 * (K * N + K + N) * args.steps / (t / 1e3) / 1e9
+                          for (K, N), t in zip(SHAPES, per_shape_ms)},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_source": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)",
+                     "kernel": "k_matvec", "traffic": traffic},
+        "e2e": {"value": MACS_PER_STEP * e2e_steps * world / e2e_s / 1e9, "unit": UNIT,
+                "h2d_bytes_per_step": sum(8 * K for K, N in SHAPES),
+                "d2h_bytes_per_step": sum(8 * N for K, N in SHAPES),
+                "api": "iq_matmul_vec (host pointers, weights registered)"},
+        "gpu_launches": nev,
+        "clocks": clocks,
+    }
+    if world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(ins)
+    print(json.dumps(line))
+    if dist:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,281 @@
+// iq_api.cu -- the C ABI of libiq.so (declared in include/iq.h).
+// Single translation unit: the kernel headers are included here.
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+#include <cstring>
+#include "iq_common.cuh"
+#include "iq_fpmath.cuh"
+#include "iq_matvec.cuh"
+#include "iq_gemm.cuh"
+#include "iq_elem.cuh"
+
+namespace iq {
+
+static int g_last_cuda = 0;
+
+int cuda_fail(cudaError_t e) {
+    g_last_cuda = (int)e;
+    if (e == cudaErrorMemoryAllocation) return IQ_ERR_OOM;
+    if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver ||
+        e == cudaErrorNoKernelImageForDevice || e == cudaErrorInvalidDevice)
+        return IQ_ERR_UNSUPPORTED;
+    return IQ_ERR_CUDA;
+}
+
+struct DevState {
+    bool ready = false;
+    DevInfo info;
+    cudaStream_t stream = nullptr;
+};
+static std::mutex g_mu;
+static DevState g_dev[64];
+static int g_host_device = 0;
+
+static int ensure_device(int dev) {
+    if (dev < 0 || dev >= 64) return IQ_ERR_ARG;
+    std::lock_guard<std::mutex> lk(g_mu);
+    DevState &d = g_dev[dev];
+    if (d.ready) return IQ_OK;
+    cudaDeviceProp p;
+    IQ_CUDA(cudaGetDeviceProperties(&p, dev));
+    d.info.sms = p.multiProcessorCount;
+    d.info.smem_optin = (int)p.sharedMemPerBlockOptin;
+    d.info.cc_major = p.major;
+    d.info.cc_minor = p.minor;
+    if (p.major != 10) return IQ_ERR_UNSUPPORTED;  // built for sm_100a only
+    IQ_CUDA(cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking));
+    k_cordic_init<<<1, 1, 0, d.stream>>>();
+    IQ_CHECK_LAUNCH();
+    IQ_CUDA(cudaStreamSynchronize(d.stream));
+    d.ready = true;
+    return IQ_OK;
+}
+
+static int cur_device(int *dev) {
+    IQ_CUDA(cudaGetDevice(dev));
+    return ensure_device(*dev);
+}
+
+const DevInfo &dev_info() {
+    int d = 0;
+    cudaGetDevice(&d);
+    return g_dev[d].info;
+}
+cudaStream_t lib_stream() {
+    int d = 0;
+    cudaGetDevice(&d);
+    return g_dev[d].stream;
+}
+
+// ------------------------------------------------------------ launchers
+
+template <int ROWS, int UNROLL, bool VEC, bool XSMEM>
+static int launch_mv_t(int64_t *out, const int64_t *W, const int64_t *x, int M, int N, cudaStream_t s) {
+    auto kern = k_matvec<ROWS, UNROLL, VEC, XSMEM>;
+    size_t smem = XSMEM ? (size_t)N * sizeof(int64_t) : 0;
+    if (smem > 48 * 1024) IQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int occ = 0;
+    IQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 256, smem));
+    if (occ < 1) occ = 1;
+    int groups = (M + ROWS - 1) / ROWS;
+    int ctas_needed = (groups + 7) / 8;
+    int grid = dev_info().sms * occ;
+    if (grid > ctas_needed) grid = ctas_needed;
+    kern<<<grid, 256, smem, s>>>(out, W, x, M, N);
+    IQ_CHECK_LAUNCH();
+    return IQ_OK;
+}
+
+int launch_matvec(int64_t *out, const int64_t *W, const int64_t *x, int M, int N, cudaStream_t s) {
+    bool vec = ((N & 1) == 0) && (((uintptr_t)W & 15) == 0);
+    bool xsmem = (size_t)N * 8 <= 96 * 1024 && (((uintptr_t)x & 7) == 0);
+    if (vec && xsmem) return launch_mv_t<1, 8, true, true>(out, W, x, M, N, s);
+    if (vec) return launch_mv_t<1, 8, true, false>(out, W, x, M, N, s);
+    if (xsmem) return launch_mv_t<1, 8, false, true>(out, W, x, M, N, s);
+    return launch_mv_t<1, 8, false, false>(out, W, x, M, N, s);
+}
+
+int launch_gemm(int64_t *out, const int64_t *W, const int64_t *X, int rows, int M, int N, cudaStream_t s) {
+    constexpr int BM = 64, BR = 32, BK = 32, TM = 4, TR = 2;
+    dim3 grid((M + BM - 1) / BM, (rows + BR - 1) / BR);
+    k_gemm<BM, BR, BK, TM, TR><<<grid, (BM / TM) * (BR / TR), 0, s>>>(out, W, X, rows, M, N);
+    IQ_CHECK_LAUNCH();
+    return IQ_OK;
+}
+
+// ------------------------------------------------------- weight cache
+
+struct WEntry { int64_t *d = nullptr; int M = 0, N = 0; int dev = 0; };
+static std::mutex g_wmu;
+static std::unordered_map<const void *, WEntry> g_wcache;
+
+static int weight_lookup(const int64_t *w, int M, int N, int dev, bool create, int64_t **dptr) {
+    std::lock_guard<std::mutex> lk(g_wmu);
+    auto it = g_wcache.find(w);
+    if (it != g_wcache.end()) {
+        if (it->second.M == M && it->second.N == N && it->second.dev == dev) {
+            *dptr = it->second.d;
+            return IQ_OK;
+        }
+        cudaFree(it->second.d);
+        g_wcache.erase(it);
+    }
+    if (!create) { *dptr = nullptr; return IQ_OK; }
+    size_t bytes = (size_t)M * N * sizeof(int64_t);
+    int64_t *d = nullptr;
+    IQ_CUDA(cudaMalloc(&d, bytes));
+    cudaError_t e = cudaMemcpy(d, w, bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) { cudaFree(d); return cuda_fail(e); }
+    WEntry en; en.d = d; en.M = M; en.N = N; en.dev = dev;
+    g_wcache[w] = en;
+    *dptr = d;
+    return IQ_OK;
+}
+
+}  // namespace iq
+
+using namespace iq;
+
+// ------------------------------------------------------------ C ABI
+
+extern "C" {
+
+IQ_API const char *iq_status_str(int s) {
+    switch (s) {
+    case IQ_OK: return "ok";
+    case IQ_ERR_ARG: return "invalid argument";
+    case IQ_ERR_CUDA: return "CUDA error";
+    case IQ_ERR_OOM: return "out of memory";
+    case IQ_ERR_NCCL: return "NCCL error";
+    case IQ_ERR_TIMEOUT: return "timeout";
+    case IQ_ERR_RANGE: return "out of range";
+    case IQ_ERR_STATE: return "invalid state";
+    case IQ_ERR_UNSUPPORTED: return "unsupported device";
+    default: return "unknown status";
+    }
+}
+
+IQ_API int iq_last_cuda_error(void) { return g_last_cuda; }
+IQ_API int iq_version(void) { return 100; }
+
+IQ_API int iq_set_device(int device) {
+    int n = 0;
+    IQ_CUDA(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) return IQ_ERR_ARG;
+    g_host_device = device;
+    IQ_CUDA(cudaSetDevice(device));
+    return ensure_device(device);
+}
+
+IQ_API int iq_weight_register(const int64_t *weight, int M, int N) {
+    if (!weight || M <= 0 || N <= 0) return IQ_ERR_ARG;
+    IQ_CUDA(cudaSetDevice(g_host_device));
+    int rc = ensure_device(g_host_device);
+    if (rc) return rc;
+    int64_t *d;
+    return weight_lookup(weight, M, N, g_host_device, true, &d);
+}
+
+IQ_API int iq_weight_unregister(const int64_t *weight) {
+    std::lock_guard<std::mutex> lk(g_wmu);
+    auto it = g_wcache.find(weight);
+    if (it == g_wcache.end()) return IQ_ERR_STATE;
+    cudaFree(it->second.d);
+    g_wcache.erase(it);
+    return IQ_OK;
+}
+
+IQ_API int iq_weight_cache_clear(void) {
+    std::lock_guard<std::mutex> lk(g_wmu);
+    for (auto &kv : g_wcache) cudaFree(kv.second.d);
+    g_wcache.clear();
+    return IQ_OK;
+}
+
+namespace iq {
+// Per-device staging buffers for the host-pointer drop-in (grown on demand).
+struct Staging { int64_t *d_in = nullptr, *d_out = nullptr; size_t cap_in = 0, cap_out = 0; };
+static Staging g_stage[64];
+static std::mutex g_stage_mu;
+
+static int stage_grow(int64_t **p, size_t *cap, size_t need) {
+    if (*cap >= need) return IQ_OK;
+    if (*p) cudaFree(*p);
+    *p = nullptr; *cap = 0;
+    size_t n = need < 4096 ? 4096 : need;
+    IQ_CUDA(cudaMalloc(p, n * sizeof(int64_t)));
+    *cap = n;
+    return IQ_OK;
+}
+}  // namespace iq
+
+IQ_API int iq_matmul_vec(int64_t *out, const int64_t *weight, const int64_t *in, int M, int N) {
+    if (!out || !weight || !in || M <= 0 || N <= 0) return IQ_ERR_ARG;
+    int dev = g_host_device;
+    IQ_CUDA(cudaSetDevice(dev));
+    int rc = ensure_device(dev);
+    if (rc) return rc;
+    int64_t *dw = nullptr;
+    rc = weight_lookup(weight, M, N, dev, true, &dw);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(g_stage_mu);
+    Staging &st = g_stage[dev];
+    if ((rc = stage_grow(&st.d_in, &st.cap_in, (size_t)N))) return rc;
+    if ((rc = stage_grow(&st.d_out, &st.cap_out, (size_t)M))) return rc;
+    cudaStream_t s = g_dev[dev].stream;
+    IQ_CUDA(cudaMemcpyAsync(st.d_in, in, (size_t)N * 8, cudaMemcpyHostToDevice, s));
+    if ((rc = launch_matvec(st.d_out, dw, st.d_in, M, N, s))) return rc;
+    IQ_CUDA(cudaMemcpyAsync(out, st.d_out, (size_t)M * 8, cudaMemcpyDeviceToHost, s));
+    IQ_CUDA(cudaStreamSynchronize(s));
+    return IQ_OK;
+}
+
+IQ_API int iq_matvec_dev(int64_t *d_out, const int64_t *d_w, const int64_t *d_in, int M, int N, void *stream) {
+    if (!d_out || !d_w || !d_in || M <= 0 || N <= 0) return IQ_ERR_ARG;
+    if (d_out == d_in) return IQ_ERR_ARG;
+    int dev, rc;
+    if ((rc = cur_device(&dev))) return rc;
+    return launch_matvec(d_out, d_w, d_in, M, N, pick(stream));
+}
+
+IQ_API int iq_gemm_dev(int64_t *d_out, const int64_t *d_w, const int64_t *d_X, int rows, int M, int N, void *stream) {
+    if (!d_out || !d_w || !d_X || rows <= 0 || M <= 0 || N <= 0) return IQ_ERR_ARG;
+    int dev, rc;
+    if ((rc = cur_device(&dev))) return rc;
+    if (rows == 1) return launch_matvec(d_out, d_w, d_X, M, N, pick(stream));
+    return launch_gemm(d_out, d_w, d_X, rows, M, N, pick(stream));
+}
+
+IQ_API int iq_fp_dev(int fn, const int64_t *d_x, const int64_t *d_y, int64_t *d_out, int64_t n, void *stream) {
+    if (!d_x || !d_out || n < 0 || fn < 0 || fn > IQ_FN_EXP_DYADIC) return IQ_ERR_ARG;
+    if ((fn == IQ_FN_MUL || fn == IQ_FN_DIV || fn == IQ_FN_EXP_DYADIC) && !d_y) return IQ_ERR_ARG;
+    if (n == 0) return IQ_OK;
+    int dev, rc;
+    if ((rc = cur_device(&dev))) return rc;
+    int64_t blocks = (n + 255) / 256;
+    int cap = dev_info().sms * 8;
+    k_fp_eval<<<(int)(blocks < cap ? blocks : cap), 256, 0, pick(stream)>>>(fn, d_x, d_y, d_out, n);
+    IQ_CHECK_LAUNCH();
+    return IQ_OK;
+}
+
+IQ_API int iq_rmsnorm_dev(int64_t *d_out, const int64_t *d_x, const int64_t *d_w, int rows, int dim, void *stream) {
+    if (!d_out || !d_x || !d_w || rows <= 0 || dim <= 0) return IQ_ERR_ARG;
+    int dev, rc;
+    if ((rc = cur_device(&dev))) return rc;
+    k_rmsnorm<<<rows, 256, 0, pick(stream)>>>(d_out, d_x, d_w, dim);
+    IQ_CHECK_LAUNCH();
+    return IQ_OK;
+}
+
+IQ_API int iq_softmax_dev(int64_t *d_x, int rows, int n, void *stream) {
+    if (!d_x || rows <= 0 || n <= 0) return IQ_ERR_ARG;
+    int dev, rc;
+    if ((rc = cur_device(&dev))) return rc;
+    k_softmax<<<rows, 256, 0, pick(stream)>>>(d_x, n);
+    IQ_CHECK_LAUNCH();
+    return IQ_OK;
+}
+
+}  // extern "C"

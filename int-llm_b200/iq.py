@@ -1,0 +1,165 @@
+"""Python host-side binding of libiq.so (the C ABI in include/iq.h).
+
+This is a thin ctypes mirror of the reference's operator surface: ``matmul_vec``
+(llama_int.c:1014) with its argument order ``(out, weight, in, M, N)``, where M
+is the number of output rows and N the input length. Host arrays are numpy
+int64; device arrays are anything exposing ``data_ptr()`` (torch tensors are
+used only as device-memory plumbing). Every call raises ``IQError`` on a
+non-zero status; there is no CPU fallback: if libiq.so is missing or no B200
+is present, calls fail loudly.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libiq.so")
+
+IQ_FN = dict(mul=0, div=1, sqrt=2, sqrt_fast=3, inv_sqrt=4, exp=5, log=6, cos=7, sin=8,
+             sigmoid=9, silu=10, safe_exp=11, exp_dyadic=12)
+
+# every symbol include/iq.h declares, with (restype, argtypes)
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_I64 = ctypes.c_int64
+SIGNATURES = {
+    "iq_status_str": (ctypes.c_char_p, [_I]),
+    "iq_last_cuda_error": (_I, []),
+    "iq_version": (_I, []),
+    "iq_set_device": (_I, [_I]),
+    "iq_matmul_vec": (_I, [_P, _P, _P, _I, _I]),
+    "iq_weight_register": (_I, [_P, _I, _I]),
+    "iq_weight_unregister": (_I, [_P]),
+    "iq_weight_cache_clear": (_I, []),
+    "iq_matvec_dev": (_I, [_P, _P, _P, _I, _I, _P]),
+    "iq_gemm_dev": (_I, [_P, _P, _P, _I, _I, _I, _P]),
+    "iq_fp_dev": (_I, [_I, _P, _P, _P, _I64, _P]),
+    "iq_rmsnorm_dev": (_I, [_P, _P, _P, _I, _I, _P]),
+    "iq_softmax_dev": (_I, [_P, _I, _I, _P]),
+    "iq_tensor_seed": (ctypes.c_uint64, [_I, ctypes.c_char_p]),
+    "iq_synth_weights": (_I, [ctypes.c_uint64, _P, _I64]),
+    "iq_synth_acts": (_I, [ctypes.c_uint64, _P, _I64]),
+    "iq_synth_tokens": (_I, [ctypes.c_uint64, _P, _I, _I]),
+    "iq_bf16_to_q1648": (_I64, [ctypes.c_uint16]),
+    "iq_q1648_to_bf16": (ctypes.c_uint16, [_I64]),
+}
+
+
+class IQError(RuntimeError):
+    def __init__(self, fn, status, lib):
+        self.status = status
+        msg = lib.iq_status_str(status).decode()
+        cuda = lib.iq_last_cuda_error()
+        super().__init__(f"{fn} failed: {msg} (status {status}, last cudaError {cuda})")
+
+
+_lib = None
+
+
+def lib():
+    """Load libiq.so (built in-tree by the package Makefile)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"libiq.so not built at {LIB_PATH}; run __graft_entry__.build()")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _call(name, *args):
+    L = lib()
+    rc = getattr(L, name)(*args)
+    if rc != 0:
+        raise IQError(name, rc, L)
+    return rc
+
+
+def _hp(a):
+    assert isinstance(a, np.ndarray) and a.flags.c_contiguous
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _dp(t):
+    if t is None:
+        return None
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _sp(stream):
+    if stream is None:
+        return None
+    return ctypes.c_void_p(getattr(stream, "cuda_stream", stream))
+
+
+# ---------------------------------------------------------------- host API
+
+def matmul_vec(out, weight, inp, M, N):
+    """Drop-in for matmul_vec(out, weight, in, M, N) on host int64 arrays."""
+    assert out.dtype == weight.dtype == inp.dtype == np.int64
+    assert out.size >= M and inp.size >= N and weight.size >= M * N
+    _call("iq_matmul_vec", _hp(out), _hp(weight), _hp(inp), M, N)
+
+
+def weight_register(weight, M, N):
+    _call("iq_weight_register", _hp(weight), M, N)
+
+
+def weight_unregister(weight):
+    _call("iq_weight_unregister", _hp(weight))
+
+
+def weight_cache_clear():
+    _call("iq_weight_cache_clear")
+
+
+def set_device(d):
+    _call("iq_set_device", d)
+
+
+# -------------------------------------------------------------- device API
+
+def matvec_dev(out, w, x, M, N, stream=None):
+    _call("iq_matvec_dev", _dp(out), _dp(w), _dp(x), M, N, _sp(stream))
+
+
+def gemm_dev(out, w, X, rows, M, N, stream=None):
+    _call("iq_gemm_dev", _dp(out), _dp(w), _dp(X), rows, M, N, _sp(stream))
+
+
+def fp_dev(fn, x, y, out, n, stream=None):
+    code = IQ_FN[fn] if isinstance(fn, str) else fn
+    _call("iq_fp_dev", code, _dp(x), _dp(y), _dp(out), n, _sp(stream))
+
+
+def rmsnorm_dev(out, x, w, rows, dim, stream=None):
+    _call("iq_rmsnorm_dev", _dp(out), _dp(x), _dp(w), rows, dim, _sp(stream))
+
+
+def softmax_dev(x, rows, n, stream=None):
+    _call("iq_softmax_dev", _dp(x), rows, n, _sp(stream))
+
+
+# --------------------------------------------------------- synthetic inputs
+
+def synth_weights(cfg, name, shape):
+    a = np.empty(shape, dtype=np.int64)
+    _call("iq_synth_weights", lib().iq_tensor_seed(cfg, name.encode()), _hp(a), a.size)
+    return a
+
+
+def synth_acts(cfg, name, shape):
+    a = np.empty(shape, dtype=np.int64)
+    _call("iq_synth_acts", lib().iq_tensor_seed(cfg, name.encode()), _hp(a), a.size)
+    return a
+
+
+def synth_tokens(cfg, name, n, vocab):
+    a = np.empty(n, dtype=np.int32)
+    _call("iq_synth_tokens", lib().iq_tensor_seed(cfg, name.encode()), _hp(a), n, vocab)
+    return a

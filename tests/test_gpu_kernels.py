@@ -1,0 +1,204 @@
+"""GPU parity tests: every kernel, through the C ABI, bit-exact against the
+oracle (C restatement) on the same seeded inputs, plus the reference goldens."""
+import ctypes
+import json
+import os
+
+import numpy as np
+import pytest
+
+import configs
+import iq
+import oracle as orc
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+ONE = 1 << 48
+
+
+def dev(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    import torch
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def rand_full(rng, shape):
+    return rng.integers(-2 ** 63, 2 ** 63 - 1, shape, dtype=np.int64)
+
+
+# ------------------------------------------------------------------ matvec
+
+@pytest.mark.parametrize("M,N", [(1, 1), (1, 2), (3, 17), (5, 64), (7, 65), (64, 1000), (33, 2048),
+                                 (1000, 63), (129, 4097), (17, 40000)])
+@pytest.mark.parametrize("dist", ["full", "cfg"])
+def test_matvec_dev_edges(M, N, dist):
+    import torch
+    rng = np.random.default_rng(M * 7919 + N)
+    if dist == "full":
+        w, x = rand_full(rng, (M, N)), rand_full(rng, (N,))
+    else:
+        w = orc.synth_weights(1, f"w:{M}x{N}", (M, N))
+        x = orc.synth_acts(1, f"x:{M}x{N}", (N,))
+    want = orc.matmul_vec(w, x)
+    dw, dx = dev(w), dev(x)
+    do = torch.empty(M, dtype=torch.int64, device="cuda")
+    iq.matvec_dev(do, dw, dx, M, N)
+    assert (host(do) == want).all()
+
+
+def test_matvec_unaligned_weight_pointer():
+    """A weight base that is 8- but not 16-byte aligned takes the scalar-load path."""
+    import torch
+    rng = np.random.default_rng(5)
+    M, N = 37, 300
+    w, x = rand_full(rng, (M, N)), rand_full(rng, (N,))
+    buf = dev(np.concatenate([np.zeros(1, np.int64), w.ravel()]))
+    dx = dev(x)
+    do = torch.empty(M, dtype=torch.int64, device="cuda")
+    lib = iq.lib()
+    rc = lib.iq_matvec_dev(ctypes.c_void_p(do.data_ptr()), ctypes.c_void_p(buf.data_ptr() + 8),
+                           ctypes.c_void_p(dx.data_ptr()), M, N, None)
+    assert rc == 0
+    assert (host(do) == orc.matmul_vec(w, x)).all()
+
+
+def test_matvec_cfg1_golden_and_dropin():
+    """Config-1 shapes through the drop-in matmul_vec(out, weight, in, M, N) on host
+    pointers, checked against the reference's own outputs (golden hash)."""
+    for g in json.load(open(os.path.join(GOLD, "matvec_cfg1.json"))):
+        K, N = g["K"], g["N"]
+        w = orc.synth_weights(1, g["weight"], (N, K))
+        x = orc.synth_acts(1, g["act"], (K,))
+        out = np.empty(N, dtype=np.int64)
+        iq.matmul_vec(out, w, x, N, K)
+        assert orc.fnv_hash(out) == g["out_hash"], (K, N)
+        out2 = np.zeros(N, dtype=np.int64)
+        iq.matmul_vec(out2, w, x, N, K)   # second call: cached weights
+        assert (out2 == out).all()
+        iq.weight_unregister(w)
+
+
+def test_dropin_weight_cache_rekeys_on_shape():
+    rng = np.random.default_rng(11)
+    w = rand_full(rng, (64 * 64,))
+    x = rand_full(rng, (64,))
+    o1 = np.empty(64, np.int64)
+    iq.matmul_vec(o1, w, x, 64, 64)
+    assert (o1 == orc.matmul_vec(w.reshape(64, 64), x)).all()
+    o2 = np.empty(128, np.int64)
+    iq.matmul_vec(o2, w, x[:32].copy(), 128, 32)   # same pointer, new shape
+    assert (o2 == orc.matmul_vec(w.reshape(128, 32), x[:32].copy())).all()
+    iq.weight_cache_clear()
+
+
+# ------------------------------------------------------------------ gemm
+
+@pytest.mark.parametrize("rows,M,N", [(2, 5, 7), (31, 64, 129), (33, 65, 1000), (64, 256, 2048),
+                                      (100, 300, 5632)])
+def test_gemm_dev_vs_oracle(rows, M, N):
+    import torch
+    rng = np.random.default_rng(rows + M + N)
+    w, X = rand_full(rng, (M, N)), rand_full(rng, (rows, N))
+    want = orc.matmul_rows(w, X)
+    do = torch.empty((rows, M), dtype=torch.int64, device="cuda")
+    iq.gemm_dev(do, dev(w), dev(X), rows, M, N)
+    assert (host(do) == want).all()
+
+
+# ------------------------------------------------------------------ fp_math
+
+def det_grid():
+    """The determinism gate's input grid (fp_determinism.c:101-137)."""
+    g = [0, ONE, -ONE, ONE // 2, -(ONE // 2), 1, -1, ONE + 1, ONE - 1, 32000 * ONE, -32000 * ONE,
+         181 * ONE, 7 * ONE, -7 * ONE, 2 * ONE, 10 * ONE]
+    for e in range(-44, 15):
+        p = ONE << e if e >= 0 else ONE >> -e
+        g += [p, -p]
+    st = 0x9E3779B97F4A7C15
+    M64 = (1 << 64) - 1
+    span = 32000 * ONE
+    for _ in range(4096):
+        st ^= (st << 13) & M64
+        st ^= st >> 7
+        st ^= (st << 17) & M64
+        mag = st % span
+        g.append(mag if st & 1 else -mag)
+    return np.array(g, dtype=np.int64)
+
+
+def test_fp_ports_reproduce_determinism_subhashes():
+    """Device ports of fp_mul/div/sqrt/sqrt_fast/inv_sqrt/exp/log/sincos/sigmoid/silu
+    over the gate's grid give the reference's golden sub-hashes."""
+    import torch
+    gd = json.load(open(os.path.join(GOLD, "determinism.json")))
+    g = det_grid()
+    n = len(g)
+    assert n == 4230
+    y = g[(np.arange(n) * 7 + 3) % n]
+    xp = np.abs(g)
+    xp = np.where(xp < 1024, xp + 1024, xp)
+    forty, twenty = 40 * ONE, 20 * ONE
+    ea = (g.view(np.uint64) % np.uint64(forty)).astype(np.int64) - twenty
+
+    def run(fn, x, yy=None):
+        do = torch.empty(len(x), dtype=torch.int64, device="cuda")
+        iq.fp_dev(fn, dev(x), dev(yy) if yy is not None else None, do, len(x))
+        return host(do)
+
+    assert f"{orc.fnv_hash(run('mul', g, y)):016x}" == gd["sub:fp_mul"]
+    nz = y != 0
+    assert f"{orc.fnv_hash(run('div', g[nz], y[nz])):016x}" == gd["sub:fp_div"]
+    assert f"{orc.fnv_hash(run('sqrt', xp)):016x}" == gd["sub:fp_sqrt"]
+    assert f"{orc.fnv_hash(run('sqrt_fast', xp)):016x}" == gd["sub:fp_sqrt_fast"]
+    assert f"{orc.fnv_hash(run('inv_sqrt', xp)):016x}" == gd["sub:fp_inv_sqrt"]
+    assert f"{orc.fnv_hash(run('log', xp)):016x}" == gd["sub:fp_log"]
+    assert f"{orc.fnv_hash(run('exp', ea)):016x}" == gd["sub:fp_exp"]
+    assert f"{orc.fnv_hash(run('cos', g)):016x}" == gd["sub:fp_sincos_cos"]
+    assert f"{orc.fnv_hash(run('sin', g)):016x}" == gd["sub:fp_sincos_sin"]
+    assert f"{orc.fnv_hash(run('sigmoid', g)):016x}" == gd["sub:fp_sigmoid"]
+    assert f"{orc.fnv_hash(run('silu', g)):016x}" == gd["sub:fp_silu"]
+
+
+@pytest.mark.parametrize("fn", list(range(13)))
+def test_fp_ports_random_vs_oracle(fn):
+    import torch
+    rng = np.random.default_rng(fn)
+    x = np.concatenate([rand_full(rng, 3000), rng.integers(-50 * ONE, 50 * ONE, 3000)]).astype(np.int64)
+    y = np.roll(x, 5)
+    if fn == 1:
+        y[y == 0] = 1
+    if fn == 12:
+        x = rng.integers(-3 * ONE, 3 * ONE, x.size).astype(np.int64)
+        y = rng.integers(0, 20, x.size).astype(np.int64)
+    want = orc.fp_vec(fn, x, y)
+    do = torch.empty(x.size, dtype=torch.int64, device="cuda")
+    iq.fp_dev(fn, dev(x), dev(y), do, x.size)
+    assert (host(do) == want).all()
+
+
+def test_rmsnorm_softmax_vs_oracle():
+    import torch
+    rng = np.random.default_rng(1)
+    for rows, dim in ((1, 1), (3, 7), (4, 2048), (2, 5632)):
+        x = rng.integers(-8 * ONE, 8 * ONE, (rows, dim)).astype(np.int64)
+        w = rng.integers(-2 * ONE, 2 * ONE, dim).astype(np.int64)
+        want = np.empty_like(x)
+        for r in range(rows):
+            orc.O.iqo_rmsnorm(orc.p(want[r]), orc.p(np.ascontiguousarray(x[r])), orc.p(w), dim)
+        do = torch.empty((rows, dim), dtype=torch.int64, device="cuda")
+        iq.rmsnorm_dev(do, dev(x), dev(w), rows, dim)
+        assert (host(do) == want).all()
+        s = rng.integers(-30 * ONE, 30 * ONE, (rows, dim)).astype(np.int64)
+        want = s.copy()
+        for r in range(rows):
+            row = np.ascontiguousarray(want[r])
+            orc.O.iqo_softmax(orc.p(row), dim)
+            want[r] = row
+        ds = dev(s)
+        iq.softmax_dev(ds, rows, dim)
+        assert (host(ds) == want).all()
