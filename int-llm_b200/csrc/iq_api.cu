@@ -4,6 +4,7 @@
 #include <unordered_map>
 #include <vector>
 #include <cstring>
+#include <cstdlib>
 #include "iq_common.cuh"
 #include "iq_fpmath.cuh"
 #include "iq_matvec.cuh"
@@ -70,30 +71,48 @@ cudaStream_t lib_stream() {
 
 // ------------------------------------------------------------ launchers
 
-template <int ROWS, int UNROLL, bool VEC, bool XSMEM>
-static int launch_mv_t(int64_t *out, const int64_t *W, const int64_t *x, int M, int N, cudaStream_t s) {
-    auto kern = k_matvec<ROWS, UNROLL, VEC, XSMEM>;
+template <int WPR, int UNROLL, bool VEC, bool XSMEM>
+static int launch_mv_t(int64_t *out, const int64_t *W, const int64_t *x, int M, int N, int add, cudaStream_t s) {
+    auto kern = k_matvec<WPR, UNROLL, VEC, XSMEM>;
     size_t smem = XSMEM ? (size_t)N * sizeof(int64_t) : 0;
     if (smem > 48 * 1024) IQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int occ = 0;
     IQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 256, smem));
     if (occ < 1) occ = 1;
-    int groups = (M + ROWS - 1) / ROWS;
-    int ctas_needed = (groups + 7) / 8;
+    int rpc = 8 / WPR;
+    int ctas_needed = (M + rpc - 1) / rpc;
     int grid = dev_info().sms * occ;
     if (grid > ctas_needed) grid = ctas_needed;
-    kern<<<grid, 256, smem, s>>>(out, W, x, M, N);
+    kern<<<grid, 256, smem, s>>>(out, W, x, M, N, add);
     IQ_CHECK_LAUNCH();
     return IQ_OK;
 }
 
-int launch_matvec(int64_t *out, const int64_t *W, const int64_t *x, int M, int N, cudaStream_t s) {
-    bool vec = ((N & 1) == 0) && (((uintptr_t)W & 15) == 0);
-    bool xsmem = (size_t)N * 8 <= 96 * 1024 && (((uintptr_t)x & 7) == 0);
-    if (vec && xsmem) return launch_mv_t<1, 8, true, true>(out, W, x, M, N, s);
-    if (vec) return launch_mv_t<1, 8, true, false>(out, W, x, M, N, s);
-    if (xsmem) return launch_mv_t<1, 8, false, true>(out, W, x, M, N, s);
-    return launch_mv_t<1, 8, false, false>(out, W, x, M, N, s);
+template <bool VEC, bool XSMEM>
+static int launch_mv_v(int64_t *out, const int64_t *W, const int64_t *x, int M, int N, int add, cudaStream_t s) {
+    // split rows over enough warps to fill the GPU: ~16 warps per SM
+    int want = dev_info().sms * 16;
+    static int force = getenv("IQ_MV_WPR") ? atoi(getenv("IQ_MV_WPR")) : 0;
+    int wpr = force ? force : (M >= want ? 1 : M * 2 >= want ? 2 : M * 4 >= want ? 4 : 8);
+    if (N < 64 * wpr) wpr = 1;
+    switch (wpr) {
+    case 1: return launch_mv_t<1, 8, VEC, XSMEM>(out, W, x, M, N, add, s);
+    case 2: return launch_mv_t<2, 8, VEC, XSMEM>(out, W, x, M, N, add, s);
+    case 4: return launch_mv_t<4, 8, VEC, XSMEM>(out, W, x, M, N, add, s);
+    default: return launch_mv_t<8, 8, VEC, XSMEM>(out, W, x, M, N, add, s);
+    }
+}
+
+int launch_matvec(int64_t *out, const int64_t *W, const int64_t *x, int M, int N, cudaStream_t s, int add = 0) {
+    // 16-byte weight loads need an even row length and a 16-byte aligned base;
+    // x is read as 16-byte pairs too, from shared memory (always aligned) or,
+    // for long rows, from global memory (then x must be 16-byte aligned).
+    bool xsmem = (size_t)N * 8 <= 96 * 1024;
+    bool vec = ((N & 1) == 0) && (((uintptr_t)W & 15) == 0) && (xsmem || (((uintptr_t)x & 15) == 0));
+    if (vec && xsmem) return launch_mv_v<true, true>(out, W, x, M, N, add, s);
+    if (vec) return launch_mv_v<true, false>(out, W, x, M, N, add, s);
+    if (xsmem) return launch_mv_v<false, true>(out, W, x, M, N, add, s);
+    return launch_mv_v<false, false>(out, W, x, M, N, add, s);
 }
 
 int launch_gemm(int64_t *out, const int64_t *W, const int64_t *X, int rows, int M, int N, cudaStream_t s) {

@@ -74,10 +74,10 @@ k_gemm(int64_t *__restrict__ out, const int64_t *__restrict__ W,
 #pragma unroll
                 for (int b = 0; b < TR; b++) {
                     Acc6 &c = acc[a][b];
-                    c.A0 += (int64_t)xa[b][0] * wv[a].x; c.A1 += (int64_t)xa[b][1] * wv[a].x;
-                    c.A2 += (int64_t)xa[b][2] * wv[a].x;
-                    c.B0 += (int64_t)xa[b][0] * wv[a].y; c.B1 += (int64_t)xa[b][1] * wv[a].y;
-                    c.B2 += (int64_t)xa[b][2] * wv[a].y;
+                    madw(c.A0, xa[b][0], wv[a].x); madw(c.A1, xa[b][1], wv[a].x);
+                    madw(c.A2, xa[b][2], wv[a].x);
+                    madw(c.B0, xa[b][0], wv[a].y); madw(c.B1, xa[b][1], wv[a].y);
+                    madw(c.B2, xa[b][2], wv[a].y);
                 }
         }
 #pragma unroll

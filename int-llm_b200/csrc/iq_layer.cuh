@@ -1,0 +1,159 @@
+// iq_layer.cuh -- device kernels of the integer Llama layer around the matvecs
+// (transformer_layer_forward, llama_int.c:1326-1569; llama_forward,
+// llama_int.c:2807-2886). All kernels take the token position (and token id)
+// from device memory so a whole decode step can be captured in a CUDA graph
+// and replayed per token. Layouts (int64 Q16.48 everywhere):
+//   qkv     [B][dim + 2*kvd]   q | k | v as produced by the fused QKV matvec
+//   kcache  [L][B][max_seq][kvd], vcache same  (per layer, per sequence)
+//   rope    cos/sin [max_seq][hd/2]            (rope_init table layout, llama_int.c:960-986)
+#pragma once
+#include "iq_elem.cuh"
+
+namespace iq {
+
+// hidden[b] = embed[token[b]] (llama_int.c:2822-2824)
+__global__ void k_embed(int64_t *__restrict__ hidden, const int64_t *__restrict__ embed,
+                        const int *__restrict__ tokens, int dim) {
+    const int b = blockIdx.y;
+    const int64_t *src = embed + (size_t)tokens[b] * dim;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x)
+        hidden[(size_t)b * dim + i] = src[i];
+}
+
+// RoPE on all q heads and the k heads (rope_apply, llama_int.c:997-1008), then the
+// exact K/V cache write at pos (llama_int.c:1415-1416). One thread per rotation pair.
+__global__ void k_rope_kv(int64_t *__restrict__ qkv, int64_t *__restrict__ kc, int64_t *__restrict__ vc,
+                          const int64_t *__restrict__ rcos, const int64_t *__restrict__ rsin,
+                          const int *__restrict__ pos_arr, int nh, int nkv, int hd, int max_seq) {
+    const int b = blockIdx.y;
+    const int half = hd / 2, dim = nh * hd, kvd = nkv * hd;
+    const int pos = pos_arr[b];
+    int64_t *row = qkv + (size_t)b * (dim + 2 * kvd);
+    const int64_t *c = rcos + (size_t)pos * half, *s = rsin + (size_t)pos * half;
+    int64_t *kdst = kc + ((size_t)b * max_seq + pos) * kvd;
+    int64_t *vdst = vc + ((size_t)b * max_seq + pos) * kvd;
+    const int npairs = (nh + nkv) * half;
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < npairs + kvd; p += gridDim.x * blockDim.x) {
+        if (p < npairs) {
+            int h = p / half, i = p % half;
+            int64_t *v = row + h * hd;  // q heads then k heads are contiguous
+            int64_t x0 = v[i], x1 = v[i + half];
+            int64_t a = d_mul(x0, c[i]) - d_mul(x1, s[i]);
+            int64_t bb = d_mul(x1, c[i]) + d_mul(x0, s[i]);
+            if (h < nh) { v[i] = a; v[i + half] = bb; }
+            else {
+                int kh = h - nh;
+                kdst[kh * hd + i] = a;
+                kdst[kh * hd + i + half] = bb;
+            }
+        } else {
+            int j = p - npairs;
+            vdst[j] = row[dim + kvd + j];
+        }
+    }
+}
+
+// signed 64x64 -> 128 product
+__device__ __forceinline__ i128 d_mul128(int64_t a, int64_t b) {
+    uint64_t lo = (uint64_t)a * (uint64_t)b;
+    int64_t hi = __mul64hi(a, b);
+    return (i128)(((u128)(uint64_t)hi << 64) | lo);
+}
+
+// Exact GQA attention for one (sequence, q head) per CTA, llama_int.c:1432-1529:
+//   score_t = fp_mul((int64)(sum_d (i128)q[d]*k_t[d] >> 48), fp_inv_sqrt(fp_from_int(hd)))
+//   p = softmax(score) (llama_int.c:1060-1072)
+//   out[d] = sum_t fp_mul(p_t, v_t[d])   (int64 sum of floor-shifted terms)
+// Scores live in dynamic shared memory ([T] int64); q_h in shared memory.
+__global__ void k_attention(int64_t *__restrict__ out, const int64_t *__restrict__ qkv,
+                            const int64_t *__restrict__ kc, const int64_t *__restrict__ vc,
+                            const int *__restrict__ pos_arr, int nh, int nkv, int hd, int max_seq) {
+    extern __shared__ __align__(16) int64_t sm[];
+    __shared__ uint64_t red[64];
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int dim = nh * hd, kvd = nkv * hd, kvh = h / (nh / nkv);
+    const int T = pos_arr[b] + 1;
+    int64_t *qs = sm;            // [hd]
+    int64_t *sc = sm + hd;       // [T]
+    const int64_t *q = qkv + (size_t)b * (dim + 2 * kvd) + h * hd;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) qs[d] = q[d];
+    __syncthreads();
+    const int64_t scale = d_inv_sqrt(d_from_int(hd));
+    const int64_t *kb = kc + (size_t)b * max_seq * kvd + kvh * hd;
+    const int64_t *vb = vc + (size_t)b * max_seq * kvd + kvh * hd;
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        const int64_t *kt = kb + (size_t)t * kvd;
+        i128 dot = 0;
+        for (int d = 0; d < hd; d++) dot += d_mul128(qs[d], kt[d]);
+        sc[t] = d_mul((int64_t)(dot >> 48), scale);
+    }
+    __syncthreads();
+    cta_softmax(sc, T, red);
+    __syncthreads();
+    // PV: thread groups of hd threads split t; int64 partial sums combine exactly (mod 2^64)
+    const int groups = blockDim.x / hd;
+    const int g = threadIdx.x / hd, d = threadIdx.x % hd;
+    int64_t acc = 0;
+    if (g < groups)
+        for (int t = g; t < T; t += groups) acc += d_mul(sc[t], vb[(size_t)t * kvd + d]);
+    __syncthreads();
+    int64_t *part = sm + hd;  // reuse the score area: [groups][hd]
+    if (g < groups) part[g * hd + d] = acc;
+    __syncthreads();
+    for (int dd = threadIdx.x; dd < hd; dd += blockDim.x) {
+        uint64_t s = 0;
+        for (int gg = 0; gg < groups; gg++) s += (uint64_t)part[gg * hd + dd];
+        out[(size_t)b * dim + h * hd + dd] = (int64_t)s;
+    }
+}
+
+// SwiGLU: out[i] = fp_mul(fp_silu(gate[i]), up[i]) with gu = [gate | up] (llama_int.c:1549-1552)
+__global__ void k_swiglu(int64_t *__restrict__ out, const int64_t *__restrict__ gu, int inter, int rows) {
+    const int64_t n = (int64_t)inter * rows;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        int64_t r = e / inter, i = e % inter;
+        const int64_t *row = gu + r * 2 * inter;
+        out[e] = d_mul(d_silu(row[i]), row[inter + i]);
+    }
+}
+
+// argmax, first maximum (strict >, llama_int.c:2888-2893), one CTA per row;
+// also advances the decode state: next token -> tokens[b], pos[b] += 1, and
+// records it in hist[b*hist_stride + pos+1] when hist != nullptr.
+__global__ void k_argmax(int *__restrict__ result, const int64_t *__restrict__ logits, int vocab,
+                         int *__restrict__ tokens, int *__restrict__ pos_arr, int *__restrict__ hist,
+                         int hist_stride) {
+    __shared__ int64_t bv[32];
+    __shared__ int bi[32];
+    const int b = blockIdx.x;
+    const int64_t *lg = logits + (size_t)b * vocab;
+    int64_t best = INT64_MIN;
+    int idx = 0x7fffffff;
+    for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+        int64_t v = lg[i];
+        if (v > best) { best = v; idx = i; }
+    }
+    for (int m = 16; m >= 1; m >>= 1) {
+        int64_t ov = __shfl_xor_sync(0xffffffffu, best, m);
+        int oi = __shfl_xor_sync(0xffffffffu, idx, m);
+        if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
+    }
+    int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) { bv[w] = best; bi[w] = idx; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < (int)(blockDim.x >> 5); k++)
+            if (bv[k] > best || (bv[k] == best && bi[k] < idx)) { best = bv[k]; idx = bi[k]; }
+        // warp 0's value already folded in by the shuffle; recheck entry 0
+        if (bv[0] > best || (bv[0] == best && bi[0] < idx)) { best = bv[0]; idx = bi[0]; }
+        result[b] = idx;
+        if (tokens) tokens[b] = idx;
+        if (pos_arr) {
+            int p = pos_arr[b] + 1;
+            if (hist) hist[(size_t)b * hist_stride + p] = idx;
+            pos_arr[b] = p;
+        }
+    }
+}
+
+}  // namespace iq

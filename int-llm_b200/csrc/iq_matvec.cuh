@@ -22,7 +22,8 @@
 // in shared memory together with 2^31*sum(x). One warp owns ROWS rows at a
 // time (the lane-to-column map is fixed, so the warp reduction happens once
 // per row); CTAs are persistent (grid = resident CTAs) and walk row groups
-// with a grid stride.
+// with a grid stride. With add != 0 the result is added to out (the residual
+// adds of llama_int.c:1535 and 1556 fused into the O and down projections).
 #pragma once
 #include "iq_common.cuh"
 
@@ -40,6 +41,11 @@ __device__ __forceinline__ int64_t ld_stream(const int64_t *p) {
     return v;
 }
 
+// acc += (int64)a * b as one wide integer multiply-add
+__device__ __forceinline__ void madw(int64_t &acc, int a, int b) {
+    asm("mad.wide.s32 %0, %1, %2, %0;" : "+l"(acc) : "r"(a), "r"(b));
+}
+
 // six int64 partial accumulators of one row for one lane
 struct Acc6 {
     int64_t A0, A1, A2, B0, B1, B2;
@@ -47,8 +53,8 @@ struct Acc6 {
     __device__ __forceinline__ void mac(int a0, int a1, int a2, int64_t w) {
         int wh = (int)(w >> 32);
         int ws = (int)((uint32_t)w ^ 0x80000000u);
-        A0 += (int64_t)a0 * wh; A1 += (int64_t)a1 * wh; A2 += (int64_t)a2 * wh;
-        B0 += (int64_t)a0 * ws; B1 += (int64_t)a1 * ws; B2 += (int64_t)a2 * ws;
+        madw(A0, a0, wh); madw(A1, a1, wh); madw(A2, a2, wh);
+        madw(B0, a0, ws); madw(B1, a1, ws); madw(B2, a2, ws);
     }
     // sum_k 2^{p_k} (2^32 A_k + B_k) as a 128-bit value
     __device__ __forceinline__ i128 fold() const {
@@ -102,93 +108,96 @@ __device__ __forceinline__ i128 cta_stage_x(const int64_t *__restrict__ x, int64
 // Columns per fold: 512 column pairs per lane = 32768 columns.
 #define IQ_MV_SEG 32768
 
-template <int ROWS, int UNROLL, bool VEC, bool XSMEM>
+// One warp computes a partial dot product for one row over the columns
+// [seg-interleaved 64-column blocks kpart, kpart + WPR, ...]; returns this
+// lane's 128-bit partial (not yet reduced across lanes).
+template <int UNROLL, bool VEC>
+__device__ __forceinline__ i128 warp_row_partial(const int64_t *__restrict__ wr, const int64_t *x,
+                                                 int N, int lane, int kpart, int WPR) {
+    i128 tot = 0;
+    // columns handled by this lane per fold: at most 512 pairs (VEC) / 1024 (scalar)
+    const int step = (VEC ? 64 : 32) * WPR;
+    const int per_fold = VEC ? 512 : 1024;
+    int c0 = (VEC ? 2 * lane : lane) + (VEC ? 64 : 32) * kpart;
+    while (c0 < N) {
+        Acc6 acc;
+        acc.zero();
+        for (int it = 0; it < per_fold && c0 < N; it += UNROLL, c0 += step * UNROLL) {
+            if (VEC) {
+                longlong2 wv[UNROLL];
+#pragma unroll
+                for (int u = 0; u < UNROLL; u++) {
+                    int c = c0 + step * u;
+                    if (c < N) wv[u] = ld_stream_v2(wr + c);
+                }
+#pragma unroll
+                for (int u = 0; u < UNROLL; u++) {
+                    int c = c0 + step * u;
+                    if (c < N) {
+                        longlong2 xv = *reinterpret_cast<const longlong2 *>(x + c);
+                        int p0, p1, p2, q0, q1, q2;
+                        limbs(xv.x, p0, p1, p2);
+                        limbs(xv.y, q0, q1, q2);
+                        acc.mac(p0, p1, p2, wv[u].x);
+                        acc.mac(q0, q1, q2, wv[u].y);
+                    }
+                }
+            } else {
+                int64_t wv[UNROLL];
+#pragma unroll
+                for (int u = 0; u < UNROLL; u++) {
+                    int c = c0 + step * u;
+                    if (c < N) wv[u] = ld_stream(wr + c);
+                }
+#pragma unroll
+                for (int u = 0; u < UNROLL; u++) {
+                    int c = c0 + step * u;
+                    if (c < N) {
+                        int p0, p1, p2;
+                        limbs(x[c], p0, p1, p2);
+                        acc.mac(p0, p1, p2, wv[u]);
+                    }
+                }
+            }
+        }
+        tot += acc.fold();
+    }
+    return tot;
+}
+
+// CTA of 8 warps; each row is split over WPR warps (split-K inside the CTA,
+// reduced through shared memory), so a CTA handles 8/WPR rows per pass.
+template <int WPR, int UNROLL, bool VEC, bool XSMEM>
 __global__ void __launch_bounds__(256)
 k_matvec(int64_t *__restrict__ out, const int64_t *__restrict__ W,
-         const int64_t *__restrict__ xg, int M, int N) {
+         const int64_t *__restrict__ xg, int M, int N, int add) {
     extern __shared__ __align__(16) int64_t xs_dyn[];
+    __shared__ uint64_t part[8][2];
     const int64_t *x = XSMEM ? xs_dyn : xg;
     const i128 xcorr = cta_stage_x(xg, XSMEM ? xs_dyn : nullptr, N);
     __syncthreads();
 
-    const int lane = threadIdx.x & 31;
-    const int warps_per_cta = blockDim.x >> 5;
-    const int gwarp = blockIdx.x * warps_per_cta + (threadIdx.x >> 5);
-    const int nwarps = gridDim.x * warps_per_cta;
-    const int ngroups = (M + ROWS - 1) / ROWS;
-
-    for (int g = gwarp; g < ngroups; g += nwarps) {
-        const int r0 = g * ROWS;
-        i128 tot[ROWS];
-#pragma unroll
-        for (int r = 0; r < ROWS; r++) tot[r] = 0;
-        const int64_t *wr[ROWS];
-#pragma unroll
-        for (int r = 0; r < ROWS; r++) {
-            int row = min(r0 + r, M - 1);  // clamped rows are computed and discarded
-            wr[r] = W + (size_t)row * N;
-        }
-        for (int seg = 0; seg < N; seg += IQ_MV_SEG) {
-            const int segend = min(N, seg + IQ_MV_SEG);
-            Acc6 acc[ROWS];
-#pragma unroll
-            for (int r = 0; r < ROWS; r++) acc[r].zero();
-            if (VEC) {
-                // each lane: columns c, c+1 with c = seg + 2*lane + 64*t
-                for (int c0 = seg + 2 * lane; c0 < segend; c0 += 64 * UNROLL) {
-                    longlong2 wv[UNROLL][ROWS];
-#pragma unroll
-                    for (int u = 0; u < UNROLL; u++) {
-                        int c = c0 + 64 * u;
-#pragma unroll
-                        for (int r = 0; r < ROWS; r++)
-                            if (c < segend) wv[u][r] = ld_stream_v2(wr[r] + c);
-                    }
-#pragma unroll
-                    for (int u = 0; u < UNROLL; u++) {
-                        int c = c0 + 64 * u;
-                        if (c < segend) {
-                            longlong2 xv = *reinterpret_cast<const longlong2 *>(x + c);
-                            int p0, p1, p2, q0, q1, q2;
-                            limbs(xv.x, p0, p1, p2);
-                            limbs(xv.y, q0, q1, q2);
-#pragma unroll
-                            for (int r = 0; r < ROWS; r++) {
-                                acc[r].mac(p0, p1, p2, wv[u][r].x);
-                                acc[r].mac(q0, q1, q2, wv[u][r].y);
-                            }
-                        }
-                    }
-                }
-            } else {
-                for (int c0 = seg + lane; c0 < segend; c0 += 32 * UNROLL) {
-                    int64_t wv[UNROLL][ROWS];
-#pragma unroll
-                    for (int u = 0; u < UNROLL; u++) {
-                        int c = c0 + 32 * u;
-#pragma unroll
-                        for (int r = 0; r < ROWS; r++)
-                            if (c < segend) wv[u][r] = ld_stream(wr[r] + c);
-                    }
-#pragma unroll
-                    for (int u = 0; u < UNROLL; u++) {
-                        int c = c0 + 32 * u;
-                        if (c < segend) {
-                            int p0, p1, p2;
-                            limbs(x[c], p0, p1, p2);
-#pragma unroll
-                            for (int r = 0; r < ROWS; r++) acc[r].mac(p0, p1, p2, wv[u][r]);
-                        }
-                    }
-                }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int RPC = 8 / WPR;  // rows per CTA pass
+    const int slot = warp / WPR, kpart = warp % WPR;
+    for (int r0 = blockIdx.x * RPC; r0 < M; r0 += gridDim.x * RPC) {
+        const int row = r0 + slot;
+        i128 t = 0;
+        if (row < M) t = warp_row_partial<UNROLL, VEC>(W + (size_t)row * N, x, N, lane, kpart, WPR);
+        t = warp_sum_i128(t);
+        if (WPR > 1) {
+            if (lane == 0) { part[warp][0] = (uint64_t)t; part[warp][1] = (uint64_t)((u128)t >> 64); }
+            __syncthreads();
+            if (kpart == 0) {
+                for (int k = 1; k < WPR; k++)
+                    t += (i128)(((u128)part[warp + k][1] << 64) | part[warp + k][0]);
             }
-#pragma unroll
-            for (int r = 0; r < ROWS; r++) tot[r] += acc[r].fold();
+            __syncthreads();
         }
-#pragma unroll
-        for (int r = 0; r < ROWS; r++) {
-            i128 s = warp_sum_i128(tot[r]) + xcorr;
-            if (lane == 0 && r0 + r < M) out[r0 + r] = (int64_t)(s >> 48);
+        if (kpart == 0 && lane == 0 && row < M) {
+            // add != 0: residual epilogue out += result (int64 wrap, llama_int.c:1535, 1556)
+            int64_t v = (int64_t)((t + xcorr) >> 48);
+            out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)v) : v;
         }
     }
 }
