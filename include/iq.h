@@ -105,6 +105,65 @@ IQ_API int iq_rmsnorm_dev(int64_t *d_out, const int64_t *d_x, const int64_t *d_w
 /* softmax (llama_int.c:1060-1072), in place, on `rows` vectors of length n. */
 IQ_API int iq_softmax_dev(int64_t *d_x, int rows, int n, void *stream);
 
+/* ----------------------------------------------------------------- model */
+
+/* llama_config_t (llama_int.c:788-798), same fields and meaning. */
+typedef struct iq_config {
+    int hidden_dim, num_heads, num_kv_heads, head_dim, num_layers;
+    int intermediate_dim, vocab_size, max_seq_len, rope_theta;
+} iq_config;
+
+/* A device-resident integer Llama model (the reference's llama_model_t with
+ * cached layers, llama_int.c:1575-1602): all weights in HBM, an exact int64
+ * KV cache [layer][seq][max_seq_len][num_kv_heads*head_dim] for max_batch
+ * sequences, RoPE tables built on the device by the fp_math ports
+ * (rope_init, llama_int.c:960-986). One handle = one device, one stream;
+ * calls on one handle must not overlap. */
+typedef struct iq_model iq_model;
+
+IQ_API int iq_model_create(const iq_config *cfg, int max_batch, int device, iq_model **out);
+IQ_API int iq_model_destroy(iq_model *m);
+/* Global tensors from host memory: embed_tokens [vocab][dim], final norm [dim],
+ * lm_head [vocab][dim] (llama_int.c:1575-1580; an untied head). */
+IQ_API int iq_model_load_globals(iq_model *m, const int64_t *embed, const int64_t *final_norm,
+                                 const int64_t *lm_head);
+/* One layer's 9 tensors in layer_weights_t order (llama_int.c:1250-1260):
+ * input_layernorm, q, k, v, o, post_attention_layernorm, gate, up, down. */
+IQ_API int iq_model_load_layer(iq_model *m, int layer, const int64_t *const w[9]);
+/* Fills every weight with the seeded synthetic generator (below) for the
+ * given config index, generating on `threads` host threads. */
+IQ_API int iq_model_synth(iq_model *m, int config_index, int threads);
+/* kv_cache_reset (llama_int.c:1160-1172) for every sequence. */
+IQ_API int iq_model_reset(iq_model *m);
+
+/* llama_forward (llama_int.c:2807-2886) for sequence 0: one token at pos.
+ * logits (host, may be NULL) receives vocab_size values; *argmax_out (may be
+ * NULL) the first-maximum index (llama_int.c:2888-2893). Returns IQ_ERR_RANGE
+ * where the reference returns NULL (token or pos out of range). */
+IQ_API int iq_forward(iq_model *m, int token, int pos, int64_t *logits, int *argmax_out);
+
+/* generate() with greedy sampling (llama_int.c:3067-3135): resets the cache,
+ * prefills prompt[0..prompt_len), decodes while i < max_new, stops at EOS (2).
+ * out_tokens needs prompt_len + max_new entries; *n_out gets the reference's
+ * return value (total length). logit_hash (may be NULL) receives FNV-1a-64
+ * over every logit of every forward call in order (costs a logits copy per
+ * step). */
+IQ_API int iq_generate(iq_model *m, const int *prompt, int prompt_len, int max_new,
+                       int *out_tokens, int *n_out, uint64_t *logit_hash);
+
+/* Batched greedy decode of B = max_batch independent sequences in lockstep
+ * (the reference runs each sequence alone; rows are independent, so results
+ * equal B separate generate() calls). prompts [B][prompt_len], out_tokens
+ * [B][prompt_len + max_new], n_out[B]. */
+IQ_API int iq_generate_batch(iq_model *m, const int *prompts, int prompt_len, int max_new,
+                             int *out_tokens, int *n_out);
+
+/* Timing helper: runs `steps` greedy decode steps (graph replays) of all
+ * max_batch sequences from position pos0 with no host synchronisation and no
+ * EOS check, and returns the device time in *ms (CUDA events on the model's
+ * stream). The cache must hold valid entries below pos0. */
+IQ_API int iq_decode_steps_timed(iq_model *m, int pos0, int steps, float *ms);
+
 /* ------------------------------------------------ synthetic inputs (host) */
 
 /* Seeded inputs of the synthetic benchmark configurations. No reference

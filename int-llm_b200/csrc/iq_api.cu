@@ -53,6 +53,8 @@ static int ensure_device(int dev) {
     return IQ_OK;
 }
 
+int ensure_device_pub(int dev) { return ensure_device(dev); }
+
 static int cur_device(int *dev) {
     IQ_CUDA(cudaGetDevice(dev));
     return ensure_device(*dev);
@@ -115,10 +117,11 @@ int launch_matvec(int64_t *out, const int64_t *W, const int64_t *x, int M, int N
     return launch_mv_v<false, false>(out, W, x, M, N, add, s);
 }
 
-int launch_gemm(int64_t *out, const int64_t *W, const int64_t *X, int rows, int M, int N, cudaStream_t s) {
+int launch_gemm_add(int64_t *out, const int64_t *W, const int64_t *X, int rows, int M, int N, cudaStream_t s,
+                    int add) {
     constexpr int BM = 64, BR = 32, BK = 32, TM = 4, TR = 2;
     dim3 grid((M + BM - 1) / BM, (rows + BR - 1) / BR);
-    k_gemm<BM, BR, BK, TM, TR><<<grid, (BM / TM) * (BR / TR), 0, s>>>(out, W, X, rows, M, N);
+    k_gemm<BM, BR, BK, TM, TR><<<grid, (BM / TM) * (BR / TR), 0, s>>>(out, W, X, rows, M, N, add);
     IQ_CHECK_LAUNCH();
     return IQ_OK;
 }
@@ -263,7 +266,7 @@ IQ_API int iq_gemm_dev(int64_t *d_out, const int64_t *d_w, const int64_t *d_X, i
     int dev, rc;
     if ((rc = cur_device(&dev))) return rc;
     if (rows == 1) return launch_matvec(d_out, d_w, d_X, M, N, pick(stream));
-    return launch_gemm(d_out, d_w, d_X, rows, M, N, pick(stream));
+    return launch_gemm_add(d_out, d_w, d_X, rows, M, N, pick(stream), 0);
 }
 
 IQ_API int iq_fp_dev(int fn, const int64_t *d_x, const int64_t *d_y, int64_t *d_out, int64_t n, void *stream) {

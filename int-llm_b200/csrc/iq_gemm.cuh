@@ -17,7 +17,7 @@ namespace iq {
 template <int BM, int BR, int BK, int TM, int TR>
 __global__ void __launch_bounds__((BM / TM) * (BR / TR))
 k_gemm(int64_t *__restrict__ out, const int64_t *__restrict__ W,
-       const int64_t *__restrict__ X, int rows, int M, int N) {
+       const int64_t *__restrict__ X, int rows, int M, int N, int add) {
     constexpr int NT = (BM / TM) * (BR / TR);
     __shared__ int2 ws[BK][BM + 1];      // (wh, ws) per weight, [k][m]
     __shared__ int xl[3][BK][BR + 1];    // limbs per activation, [limb][k][r]
@@ -97,7 +97,11 @@ k_gemm(int64_t *__restrict__ out, const int64_t *__restrict__ W,
 #pragma unroll
         for (int a = 0; a < TM; a++) {
             int m = m0 + tm + a * (BM / TM);
-            if (m < M) out[(size_t)r * M + m] = (int64_t)((tot[a][b] + corr) >> 48);
+            if (m < M) {
+                int64_t v = (int64_t)((tot[a][b] + corr) >> 48);
+                int64_t *o = out + (size_t)r * M + m;
+                *o = add ? (int64_t)((uint64_t)*o + (uint64_t)v) : v;  // fused residual add
+            }
         }
     }
 }

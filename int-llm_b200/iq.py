@@ -37,6 +37,16 @@ SIGNATURES = {
     "iq_fp_dev": (_I, [_I, _P, _P, _P, _I64, _P]),
     "iq_rmsnorm_dev": (_I, [_P, _P, _P, _I, _I, _P]),
     "iq_softmax_dev": (_I, [_P, _I, _I, _P]),
+    "iq_model_create": (_I, [_P, _I, _I, _P]),
+    "iq_model_destroy": (_I, [_P]),
+    "iq_model_load_globals": (_I, [_P, _P, _P, _P]),
+    "iq_model_load_layer": (_I, [_P, _I, _P]),
+    "iq_model_synth": (_I, [_P, _I, _I]),
+    "iq_model_reset": (_I, [_P]),
+    "iq_forward": (_I, [_P, _I, _I, _P, _P]),
+    "iq_generate": (_I, [_P, _P, _I, _I, _P, _P, _P]),
+    "iq_generate_batch": (_I, [_P, _P, _I, _I, _P, _P]),
+    "iq_decode_steps_timed": (_I, [_P, _I, _I, _P]),
     "iq_tensor_seed": (ctypes.c_uint64, [_I, ctypes.c_char_p]),
     "iq_synth_weights": (_I, [ctypes.c_uint64, _P, _I64]),
     "iq_synth_acts": (_I, [ctypes.c_uint64, _P, _I64]),
@@ -163,3 +173,81 @@ def synth_tokens(cfg, name, n, vocab):
     a = np.empty(n, dtype=np.int32)
     _call("iq_synth_tokens", lib().iq_tensor_seed(cfg, name.encode()), _hp(a), n, vocab)
     return a
+
+
+# ------------------------------------------------------------------- model
+
+class Config(ctypes.Structure):
+    """iq_config (llama_config_t, llama_int.c:788-798)."""
+    _fields_ = [(n, ctypes.c_int) for n in ("hidden_dim", "num_heads", "num_kv_heads", "head_dim",
+                                             "num_layers", "intermediate_dim", "vocab_size",
+                                             "max_seq_len", "rope_theta")]
+
+    @classmethod
+    def from_dict(cls, c):
+        return cls(c["dim"], c["n_heads"], c["n_kv_heads"], c["head_dim"], c["n_layers"], c["inter"],
+                   c["vocab"], c["max_seq"], c["rope_theta"])
+
+
+class Model:
+    """Device-resident integer Llama (iq_model_*): forward / generate with the
+    reference's semantics (llama_forward, generate in llama_int.c)."""
+
+    def __init__(self, cfg, max_batch=1, device=0):
+        self.cfg = cfg if isinstance(cfg, Config) else Config.from_dict(cfg)
+        self.max_batch = max_batch
+        self.h = ctypes.c_void_p()
+        _call("iq_model_create", ctypes.byref(self.cfg), max_batch, device, ctypes.byref(self.h))
+
+    def close(self):
+        if self.h:
+            _call("iq_model_destroy", self.h)
+            self.h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def load(self, w):
+        """w: dict(embed, final_norm, lm_head, layers=[9 arrays per layer])."""
+        _call("iq_model_load_globals", self.h, _hp(w["embed"]), _hp(w["final_norm"]), _hp(w["lm_head"]))
+        for l, lay in enumerate(w["layers"]):
+            arr = (ctypes.c_void_p * 9)(*[a.ctypes.data for a in lay])
+            _call("iq_model_load_layer", self.h, l, arr)
+
+    def synth(self, config_index, threads=None):
+        _call("iq_model_synth", self.h, config_index, threads or os.cpu_count() or 1)
+
+    def reset(self):
+        _call("iq_model_reset", self.h)
+
+    def forward(self, token, pos, want_logits=True):
+        lg = np.empty(self.cfg.vocab_size, dtype=np.int64) if want_logits else None
+        a = ctypes.c_int(-1)
+        _call("iq_forward", self.h, token, pos, _hp(lg) if want_logits else None, ctypes.byref(a))
+        return a.value, lg
+
+    def generate(self, prompt, max_new, logit_hash=False):
+        pr = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(len(pr) + max_new, dtype=np.int32)
+        n = ctypes.c_int(0)
+        h = ctypes.c_uint64(0)
+        _call("iq_generate", self.h, _hp(pr), len(pr), max_new, _hp(out), ctypes.byref(n),
+              ctypes.byref(h) if logit_hash else None)
+        return out[:n.value].tolist(), (h.value if logit_hash else None)
+
+    def generate_batch(self, prompts, max_new):
+        pr = np.ascontiguousarray(prompts, dtype=np.int32)
+        B, L = pr.shape
+        assert B == self.max_batch
+        out = np.zeros((B, L + max_new), dtype=np.int32)
+        n = np.zeros(B, dtype=np.int32)
+        _call("iq_generate_batch", self.h, _hp(pr), L, max_new, _hp(out), _hp(n))
+        return [out[b, :n[b]].tolist() for b in range(B)]
+
+    def decode_steps_timed(self, pos0, steps):
+        ms = ctypes.c_float(0)
+        _call("iq_decode_steps_timed", self.h, pos0, steps, ctypes.byref(ms))
+        return ms.value
