@@ -192,14 +192,20 @@ def run_ours(args):
     s = torch.cuda.Stream()
     L = iq.lib()
     sp = ctypes.c_void_p(s.cuda_stream)
-    ptrs = [(ctypes.c_void_p(o.data_ptr()), ctypes.c_void_p(w.data_ptr()), ctypes.c_void_p(x.data_ptr()))
-            for o, (w, x) in zip(outs, dev)]
+    # weights resident in HBM in the library's packed byte-plane form (8 B per
+    # weight, packed once before timing); IQ_BENCH_RAW=1 times the CUDA-core
+    # kernel on the plain int64 matrices instead
+    raw = os.environ.get("IQ_BENCH_RAW") == "1"
+    packed = [iq.Packed(w, N, K) for (w, x), (K, N) in zip(dev, SHAPES)]
+    torch.cuda.synchronize()
+    ptrs = [(ctypes.c_void_p(o.data_ptr()), ctypes.c_void_p(w.data_ptr()), ctypes.c_void_p(x.data_ptr()), pk.h)
+            for o, (w, x), pk in zip(outs, dev, packed)]
 
     def step(evs=None):
-        for i, ((po, pw, px), (K, N)) in enumerate(zip(ptrs, SHAPES)):
+        for i, ((po, pw, px, pk), (K, N)) in enumerate(zip(ptrs, SHAPES)):
             if evs is not None:
                 evs[i][0].record(s)
-            rc = L.iq_matvec_dev(po, pw, px, N, K, sp)
+            rc = L.iq_matvec_dev(po, pw, px, N, K, sp) if raw else L.iq_matvec_packed_dev(po, pk, px, sp)
             if rc:
                 raise iq.IQError("iq_matvec_dev", rc, L)
             if evs is not None:
@@ -284,7 +290,7 @@ def run_ours(args):
                           for (K, N), t in zip(SHAPES, per_shape_ms)},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)",
-                     "kernel": "k_matvec", "traffic": traffic},
+                     "kernel": "k_matvec" if raw else "k_matvec_planes", "traffic": traffic},
         "e2e": {"value": MACS_PER_STEP * e2e_steps * world / e2e_s / 1e9, "unit": UNIT,
                 "h2d_bytes_per_step": sum(8 * K for K, N in SHAPES),
                 "d2h_bytes_per_step": sum(8 * N for K, N in SHAPES),

@@ -85,6 +85,16 @@ IQ_API int iq_weight_cache_clear(void);
 IQ_API int iq_matvec_dev(int64_t *d_out, const int64_t *d_w, const int64_t *d_in,
                          int M, int N, void *stream);
 
+/* Weights repacked for the int8 tensor cores: each int64 weight split into
+ * its 8 bytes (byte planes), stored in mma fragment order, plus 128-bit row
+ * sums; 8 bytes per weight as before. No reference counterpart: the
+ * reference multiplies the int64 matrix directly (llama_int.c:1014-1046).
+ * iq_matvec_packed_dev gives results bit-identical to matmul_vec. */
+typedef struct iq_packed iq_packed;
+IQ_API int iq_pack_weights_dev(const int64_t *d_w, int M, int N, void *stream, iq_packed **out);
+IQ_API int iq_packed_free(iq_packed *p);
+IQ_API int iq_matvec_packed_dev(int64_t *d_out, const iq_packed *w, const int64_t *d_in, void *stream);
+
 /* Batched rows: d_out[r][i] = matmul_vec(d_w, d_X[r])[i] for r < rows, i.e.
  * exactly `rows` independent calls of llama_int.c:1014 (the reference has no
  * batched form; its prefill loops M=1 calls, llama_int.c:3081-3092).

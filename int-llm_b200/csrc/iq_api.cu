@@ -1,6 +1,7 @@
 // iq_api.cu -- the C ABI of libiq.so (declared in include/iq.h).
 // Single translation unit: the kernel headers are included here.
 #include <mutex>
+#include <algorithm>
 #include <unordered_map>
 #include <vector>
 #include <cstring>
@@ -9,6 +10,7 @@
 #include "iq_fpmath.cuh"
 #include "iq_matvec.cuh"
 #include "iq_gemm.cuh"
+#include "iq_planes.cuh"
 #include "iq_elem.cuh"
 
 namespace iq {
@@ -126,32 +128,120 @@ int launch_gemm_add(int64_t *out, const int64_t *W, const int64_t *X, int rows, 
     return IQ_OK;
 }
 
+// ------------------------------------------------- byte-plane matvec
+
+static int pack_weights(const int64_t *d_w, int M, int N, cudaStream_t s, Packed *P) {
+    P->M = M; P->N = N;
+    P->Mp = (M + 15) / 16 * 16;
+    P->Kp = (N + 31) / 32 * 32;
+    size_t nbytes = (size_t)P->Mp * P->Kp * 8;
+    IQ_CUDA(cudaMalloc(&P->planes, nbytes));
+    cudaError_t e = cudaMalloc(&P->rowsum, (size_t)P->Mp * 16);
+    if (e != cudaSuccess) { cudaFree(P->planes); P->planes = nullptr; return cuda_fail(e); }
+    const int KT = P->Kp / 32;
+    int64_t total = (int64_t)(P->Mp / 16) * KT * 32;
+    int64_t blocks = (total + 255) / 256;
+    k_pack_planes<<<(int)std::min<int64_t>(blocks, (int64_t)dev_info().sms * 32), 256, 0, s>>>(
+        P->planes, d_w, M, N, KT, total);
+    IQ_CHECK_LAUNCH();
+    k_row_sums<<<std::min(P->Mp / 8 + 1, dev_info().sms * 16), 256, 0, s>>>(P->rowsum, d_w, M, N, P->Mp);
+    IQ_CHECK_LAUNCH();
+    return IQ_OK;
+}
+
+static void free_packed(Packed *P) {
+    if (P->planes) cudaFree(P->planes);
+    if (P->rowsum) cudaFree(P->rowsum);
+    P->planes = nullptr;
+    P->rowsum = nullptr;
+}
+
+// racc: RowAcc scratch with >= M zeroed entries (zero again on completion).
+int launch_matvec_planes(int64_t *out, const Packed &P, const int64_t *x, cudaStream_t s, int add, RowAcc *racc) {
+    auto kern = k_matvec_planes<2>;
+    size_t smem = (size_t)8 * (P.Kp + 16);
+    if (smem > 200 * 1024) return IQ_ERR_UNSUPPORTED;
+    if (smem > 48 * 1024) IQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int occ = 0;
+    IQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 256, smem));
+    if (occ < 1) occ = 1;
+    int64_t units = (int64_t)(P.Mp / 16) * (P.Kp / 32);
+    int64_t grid = (int64_t)dev_info().sms * occ;
+    int64_t need = (units + 7) / 8;
+    if (grid > need) grid = need;
+    if (grid < 1) grid = 1;
+    kern<<<(int)grid, 256, smem, s>>>(out, P.planes, P.rowsum, x, P.M, P.N, P.Kp, add, racc);
+    IQ_CHECK_LAUNCH();
+    return IQ_OK;
+}
+
+// Library-owned RowAcc scratch per (device, stream), grown on demand outside
+// stream capture. Launches on one stream are ordered, so they share it safely.
+struct ScratchKey {
+    int dev; cudaStream_t s;
+    bool operator==(const ScratchKey &o) const { return dev == o.dev && s == o.s; }
+};
+struct ScratchHash {
+    size_t operator()(const ScratchKey &k) const { return std::hash<void *>()((void *)k.s) ^ (size_t)k.dev; }
+};
+struct ScratchBuf { RowAcc *p = nullptr; size_t cap = 0; };
+static std::mutex g_scr_mu;
+static std::unordered_map<ScratchKey, ScratchBuf, ScratchHash> g_scr;
+
+int stream_scratch(cudaStream_t s, size_t rows, RowAcc **out) {
+    int dev = 0;
+    IQ_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(g_scr_mu);
+    ScratchBuf &b = g_scr[ScratchKey{dev, s}];
+    if (b.cap < rows) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        IQ_CUDA(cudaStreamIsCapturing(s, &cs));
+        if (cs != cudaStreamCaptureStatusNone) return IQ_ERR_STATE;  // grow before capturing
+        size_t n = rows < 65536 ? 65536 : rows;
+        RowAcc *p = nullptr;
+        if (b.p) { IQ_CUDA(cudaStreamSynchronize(s)); cudaFree(b.p); b.p = nullptr; b.cap = 0; }
+        IQ_CUDA(cudaMalloc(&p, n * sizeof(RowAcc)));
+        IQ_CUDA(cudaMemsetAsync(p, 0, n * sizeof(RowAcc), s));
+        b.p = p;
+        b.cap = n;
+    }
+    *out = b.p;
+    return IQ_OK;
+}
+
 // ------------------------------------------------------- weight cache
 
-struct WEntry { int64_t *d = nullptr; int M = 0, N = 0; int dev = 0; };
+struct WEntry { Packed P; int M = 0, N = 0; int dev = 0; };
 static std::mutex g_wmu;
 static std::unordered_map<const void *, WEntry> g_wcache;
 
-static int weight_lookup(const int64_t *w, int M, int N, int dev, bool create, int64_t **dptr) {
+// Drop-in weight cache: the host matrix is uploaded once and kept only in the
+// packed byte-plane form (same 8 bytes per weight).
+static int weight_lookup(const int64_t *w, int M, int N, int dev, bool create, Packed **pp) {
     std::lock_guard<std::mutex> lk(g_wmu);
     auto it = g_wcache.find(w);
     if (it != g_wcache.end()) {
         if (it->second.M == M && it->second.N == N && it->second.dev == dev) {
-            *dptr = it->second.d;
+            *pp = &it->second.P;
             return IQ_OK;
         }
-        cudaFree(it->second.d);
+        free_packed(&it->second.P);
         g_wcache.erase(it);
     }
-    if (!create) { *dptr = nullptr; return IQ_OK; }
+    if (!create) { *pp = nullptr; return IQ_OK; }
     size_t bytes = (size_t)M * N * sizeof(int64_t);
     int64_t *d = nullptr;
     IQ_CUDA(cudaMalloc(&d, bytes));
     cudaError_t e = cudaMemcpy(d, w, bytes, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) { cudaFree(d); return cuda_fail(e); }
-    WEntry en; en.d = d; en.M = M; en.N = N; en.dev = dev;
+    WEntry en; en.M = M; en.N = N; en.dev = dev;
+    int rc = pack_weights(d, M, N, 0, &en.P);
+    e = cudaDeviceSynchronize();
+    cudaFree(d);
+    if (rc) return rc;
+    if (e != cudaSuccess) { free_packed(&en.P); return cuda_fail(e); }
     g_wcache[w] = en;
-    *dptr = d;
+    *pp = &g_wcache[w].P;
     return IQ_OK;
 }
 
@@ -195,7 +285,7 @@ IQ_API int iq_weight_register(const int64_t *weight, int M, int N) {
     IQ_CUDA(cudaSetDevice(g_host_device));
     int rc = ensure_device(g_host_device);
     if (rc) return rc;
-    int64_t *d;
+    Packed *d;
     return weight_lookup(weight, M, N, g_host_device, true, &d);
 }
 
@@ -203,14 +293,14 @@ IQ_API int iq_weight_unregister(const int64_t *weight) {
     std::lock_guard<std::mutex> lk(g_wmu);
     auto it = g_wcache.find(weight);
     if (it == g_wcache.end()) return IQ_ERR_STATE;
-    cudaFree(it->second.d);
+    free_packed(&it->second.P);
     g_wcache.erase(it);
     return IQ_OK;
 }
 
 IQ_API int iq_weight_cache_clear(void) {
     std::lock_guard<std::mutex> lk(g_wmu);
-    for (auto &kv : g_wcache) cudaFree(kv.second.d);
+    for (auto &kv : g_wcache) free_packed(&kv.second.P);
     g_wcache.clear();
     return IQ_OK;
 }
@@ -238,7 +328,7 @@ IQ_API int iq_matmul_vec(int64_t *out, const int64_t *weight, const int64_t *in,
     IQ_CUDA(cudaSetDevice(dev));
     int rc = ensure_device(dev);
     if (rc) return rc;
-    int64_t *dw = nullptr;
+    Packed *dw = nullptr;
     rc = weight_lookup(weight, M, N, dev, true, &dw);
     if (rc) return rc;
     std::lock_guard<std::mutex> lk(g_stage_mu);
@@ -247,7 +337,9 @@ IQ_API int iq_matmul_vec(int64_t *out, const int64_t *weight, const int64_t *in,
     if ((rc = stage_grow(&st.d_out, &st.cap_out, (size_t)M))) return rc;
     cudaStream_t s = g_dev[dev].stream;
     IQ_CUDA(cudaMemcpyAsync(st.d_in, in, (size_t)N * 8, cudaMemcpyHostToDevice, s));
-    if ((rc = launch_matvec(st.d_out, dw, st.d_in, M, N, s))) return rc;
+    RowAcc *racc = nullptr;
+    if ((rc = stream_scratch(s, (size_t)dw->Mp, &racc))) return rc;
+    if ((rc = launch_matvec_planes(st.d_out, *dw, st.d_in, s, 0, racc))) return rc;
     IQ_CUDA(cudaMemcpyAsync(out, st.d_out, (size_t)M * 8, cudaMemcpyDeviceToHost, s));
     IQ_CUDA(cudaStreamSynchronize(s));
     return IQ_OK;
@@ -298,6 +390,39 @@ IQ_API int iq_softmax_dev(int64_t *d_x, int rows, int n, void *stream) {
     k_softmax<<<rows, 256, 0, pick(stream)>>>(d_x, n);
     IQ_CHECK_LAUNCH();
     return IQ_OK;
+}
+
+struct iq_packed { Packed P; int dev; };
+
+IQ_API int iq_pack_weights_dev(const int64_t *d_w, int M, int N, void *stream, iq_packed **out) {
+    if (!d_w || !out || M <= 0 || N <= 0) return IQ_ERR_ARG;
+    *out = nullptr;
+    int dev, rc;
+    if ((rc = cur_device(&dev))) return rc;
+    iq_packed *p = new iq_packed();
+    p->dev = dev;
+    if ((rc = pack_weights(d_w, M, N, pick(stream), &p->P))) { delete p; return rc; }
+    *out = p;
+    return IQ_OK;
+}
+
+IQ_API int iq_packed_free(iq_packed *p) {
+    if (!p) return IQ_ERR_ARG;
+    cudaDeviceSynchronize();
+    free_packed(&p->P);
+    delete p;
+    return IQ_OK;
+}
+
+IQ_API int iq_matvec_packed_dev(int64_t *d_out, const iq_packed *w, const int64_t *d_in, void *stream) {
+    if (!d_out || !w || !d_in || d_out == d_in) return IQ_ERR_ARG;
+    int dev, rc;
+    if ((rc = cur_device(&dev))) return rc;
+    if (dev != w->dev) return IQ_ERR_ARG;
+    cudaStream_t s = pick(stream);
+    RowAcc *racc = nullptr;
+    if ((rc = stream_scratch(s, (size_t)w->P.Mp, &racc))) return rc;
+    return launch_matvec_planes(d_out, w->P, d_in, s, 0, racc);
 }
 
 }  // extern "C"

@@ -1,0 +1,246 @@
+// iq_planes.cuh -- exact Q16.48 matvec on the int8 tensor cores (sm_100a).
+//
+// Byte-plane decomposition
+// ------------------------
+// A weight w (int64) is the sum of its bytes: w = sum_{i<8} B_i(w) 2^{8i} with
+// B_0..B_6 unsigned and B_7 signed (two's complement). An activation x is
+// biased to x_u = x + 2^63 (an unsigned 64-bit value, the sign bit flipped)
+// with unsigned bytes D_j(x_u). Then, summed over the row,
+//   sum_k x_k w_k = sum_{i,j} 2^{8(i+j)} P_ij - 2^63 sum_k w_k      (mod 2^128)
+//   P_ij = sum_k B_i(w_k) D_j(x_u,k)
+// Each P_ij is an int8 x uint8 dot product accumulated exactly in int32 by the
+// tensor cores (|u8*u8| <= 65025, so <= 33025 terms fit; the kernel folds into
+// 128 bits every 1024 k-tiles = 32768 terms). sum_k w_k is a per-row constant
+// computed when the weights are packed. out = low64(sum >> 48) exactly as
+// matmul_vec (llama_int.c:1014-1046); every step is exact integer arithmetic.
+//
+// Packed layout (same 8 bytes per weight as the int64 matrix): for each
+// 16-row x 32-column tile, 8 planes x 32 lanes x 16 bytes, where lane l holds
+// exactly its A fragment of mma.m16n8k32 (rows l/4 and l/4+8, columns
+// 4(l%4)..+3 and 16+4(l%4)..+3), so one 16-byte load per plane per lane
+// streams the tile. Rows are padded to 16 and columns to 32 with zeros.
+//
+// The x digits D_j form the MMA's B operand (N = 8 = one column per digit),
+// staged once per CTA in shared memory as 8 byte-rows of Kp (+16 pad).
+// Work split: stream-K over (row tile, column tile) units, equal slices per
+// resident warp; row tiles split between warps meet in RowAcc scratch through
+// exact 128-bit atomics, and the warp that completes a row writes it.
+#pragma once
+#include "iq_matvec.cuh"
+
+namespace iq {
+
+struct Packed {
+    int M = 0, N = 0;       // logical shape: M rows of N columns
+    int Mp = 0, Kp = 0;     // padded to 16 rows / 32 columns
+    uint4 *planes = nullptr;
+    int64_t *rowsum = nullptr;  // [Mp][2] = 128-bit sum_k w[row][k] (lo, hi)
+};
+
+// Per-row scratch for rows whose columns are split between warps: a 128-bit
+// accumulator and a count of column tiles done. Zero before the first launch;
+// the warp that completes a row resets its entry.
+struct RowAcc { unsigned long long lo, hi; unsigned int done, pad; };
+
+// Exact 128-bit atomic accumulate: add the lo word atomically, and fold the
+// carry out of that very addition (known from the returned old value) into
+// the hi word's atomic add; concurrent adders then sum exactly mod 2^128.
+__device__ __forceinline__ void atomic_add_i128(RowAcc *a, i128 v) {
+    unsigned long long lo = (unsigned long long)(uint64_t)v;
+    unsigned long long hi = (unsigned long long)(uint64_t)((u128)v >> 64);
+    unsigned long long old = atomicAdd(&a->lo, lo);
+    hi += (old + lo < old) ? 1ull : 0ull;
+    atomicAdd(&a->hi, hi);
+}
+
+// ---------------------------------------------------------------- packing
+
+// One thread per (row tile, column tile, lane): gathers the 16 weights of the
+// lane's A fragment and writes its 16 bytes in each of the 8 planes.
+__global__ void k_pack_planes(uint4 *__restrict__ planes, const int64_t *__restrict__ W, int M, int N,
+                              int KT, int64_t total) {
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int lane = (int)(e & 31);
+        const int64_t tile = e >> 5;
+        const int rt = (int)(tile / KT), kt = (int)(tile % KT);
+        const int g = lane >> 2, t = lane & 3;
+        uint64_t w[4][4];  // [reg][byte-lane]
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            int row = rt * 16 + g + ((r & 1) ? 8 : 0);
+            int col0 = kt * 32 + 4 * t + ((r & 2) ? 16 : 0);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                int col = col0 + j;
+                w[r][j] = (row < M && col < N) ? (uint64_t)W[(size_t)row * N + col] : 0ull;
+            }
+        }
+        uint4 *dst = planes + (size_t)tile * 8 * 32 + lane;
+#pragma unroll
+        for (int p = 0; p < 8; p++) {
+            uint32_t v[4];
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                uint32_t b = 0;
+#pragma unroll
+                for (int j = 0; j < 4; j++) b |= (uint32_t)((w[r][j] >> (8 * p)) & 0xff) << (8 * j);
+                v[r] = b;
+            }
+            dst[p * 32] = make_uint4(v[0], v[1], v[2], v[3]);
+        }
+    }
+}
+
+// 128-bit row sums of W (one warp per row).
+__global__ void k_row_sums(int64_t *__restrict__ rs, const int64_t *__restrict__ W, int M, int N, int Mp) {
+    const int lane = threadIdx.x & 31;
+    for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < Mp;
+         row += gridDim.x * (blockDim.x >> 5)) {
+        i128 s = 0;
+        if (row < M)
+            for (int k = lane; k < N; k += 32) s += (i128)W[(size_t)row * N + k];
+        s = warp_sum_i128(s);
+        if (lane == 0) {
+            rs[2 * row] = (int64_t)(uint64_t)s;
+            rs[2 * row + 1] = (int64_t)(uint64_t)((u128)s >> 64);
+        }
+    }
+}
+
+// ----------------------------------------------------------------- kernel
+
+__device__ __forceinline__ uint4 ld_stream_u4(const uint4 *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
+// D(16x8, s32) += A(16x32, u8 or s8) * B(32x8, u8)
+template <bool ASIGNED>
+__device__ __forceinline__ void mma_i8(int (&d)[4], const uint4 &a, uint32_t b0, uint32_t b1) {
+    if (ASIGNED)
+        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 "
+                     "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                     : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                     : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
+    else
+        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 "
+                     "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                     : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                     : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
+}
+
+// Folds the 8 plane accumulators of this lane into its two rows' 128-bit
+// partials: lane (g, t) holds digits 2t, 2t+1 of rows g (c0, c1) and g+8 (c2, c3).
+__device__ __forceinline__ void fold_planes(int (&c)[8][4], int t, i128 &r0, i128 &r1) {
+#pragma unroll
+    for (int p = 0; p < 8; p++) {
+        const int s0 = 8 * (p + 2 * t);
+        r0 += ((i128)c[p][0] << s0) + ((i128)c[p][1] << (s0 + 8));
+        r1 += ((i128)c[p][2] << s0) + ((i128)c[p][3] << (s0 + 8));
+#pragma unroll
+        for (int q = 0; q < 4; q++) c[p][q] = 0;
+    }
+}
+
+template <int UNROLL>
+__global__ void __launch_bounds__(256)
+k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const int64_t *__restrict__ rowsum,
+                const int64_t *__restrict__ xg, int M, int N, int Kp, int add, RowAcc *__restrict__ racc) {
+    extern __shared__ __align__(16) unsigned char xd[];  // [8][Kp + 16] digit rows
+    const int ld = Kp + 16;
+    for (int k = threadIdx.x; k < Kp; k += blockDim.x) {
+        uint64_t xu = (k < N ? (uint64_t)xg[k] : 0ull) ^ 0x8000000000000000ull;
+#pragma unroll
+        for (int j = 0; j < 8; j++) xd[j * ld + k] = (unsigned char)(xu >> (8 * j));
+    }
+    __syncthreads();
+
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int KT = Kp / 32, RT = (M + 15) / 16;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int64_t total = (int64_t)RT * KT;
+    const int64_t u0 = total * gw / nwarps, u1 = total * (gw + 1) / nwarps;
+    const unsigned char *xb = xd + g * ld + 4 * t;
+
+    int64_t u = u0;
+    while (u < u1) {
+        const int rt = (int)(u / KT);
+        const int k0 = (int)(u - (int64_t)rt * KT);
+        const int k1 = (int)min((int64_t)KT, (int64_t)k0 + (u1 - u));
+        int c[8][4];
+#pragma unroll
+        for (int p = 0; p < 8; p++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) c[p][q] = 0;
+        i128 r0 = 0, r1 = 0;
+        const uint4 *tp = planes + (size_t)rt * KT * 256 + lane;
+        int since_fold = 0;
+        for (int kt = k0; kt < k1; kt += UNROLL) {
+            uint4 a[UNROLL][8];
+#pragma unroll
+            for (int v = 0; v < UNROLL; v++)
+                if (kt + v < k1)
+#pragma unroll
+                    for (int p = 0; p < 8; p++) a[v][p] = ld_stream_u4(tp + (size_t)(kt + v) * 256 + p * 32);
+#pragma unroll
+            for (int v = 0; v < UNROLL; v++) {
+                if (kt + v < k1) {
+                    const int kk = (kt + v) * 32;
+                    uint32_t b0 = *reinterpret_cast<const uint32_t *>(xb + kk);
+                    uint32_t b1 = *reinterpret_cast<const uint32_t *>(xb + kk + 16);
+#pragma unroll
+                    for (int p = 0; p < 7; p++) mma_i8<false>(c[p], a[v][p], b0, b1);
+                    mma_i8<true>(c[7], a[v][7], b0, b1);
+                }
+            }
+            since_fold += UNROLL;
+            if (since_fold >= 1024) { fold_planes(c, t, r0, r1); since_fold = 0; }
+        }
+        fold_planes(c, t, r0, r1);
+        // the 4 lanes of a row group hold the 8 digits: reduce over t
+#pragma unroll
+        for (int m = 1; m <= 2; m <<= 1) {
+            r0 += shfl_xor_i128(r0, m);
+            r1 += shfl_xor_i128(r1, m);
+        }
+        if (t == 0) {
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int row = rt * 16 + g + 8 * h;
+                if (row >= M) continue;
+                i128 part = h ? r1 : r0;
+                i128 fin = 0;
+                bool write = false;
+                if (k0 == 0 && k1 == KT) { fin = part; write = true; }
+                else {
+                    RowAcc *ra = racc + row;
+                    atomic_add_i128(ra, part);
+                    __threadfence();
+                    unsigned int prev = atomicAdd(&ra->done, (unsigned int)(k1 - k0));
+                    if (prev + (unsigned int)(k1 - k0) == (unsigned int)KT) {
+                        __threadfence();
+                        unsigned long long lo = atomicExch(&ra->lo, 0ull);
+                        unsigned long long hi = atomicExch(&ra->hi, 0ull);
+                        atomicExch(&ra->done, 0u);
+                        fin = (i128)(((u128)hi << 64) | lo);
+                        write = true;
+                    }
+                }
+                if (write) {
+                    i128 ws = (i128)(((u128)(uint64_t)rowsum[2 * row + 1] << 64) | (uint64_t)rowsum[2 * row]);
+                    i128 s = (i128)((u128)fin - ((u128)ws << 63));
+                    // add != 0: residual epilogue out += result (int64 wrap, llama_int.c:1535, 1556)
+                    int64_t val = (int64_t)(s >> 48);
+                    out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)val) : val;
+                }
+            }
+        }
+        u += k1 - k0;
+    }
+}
+
+}  // namespace iq

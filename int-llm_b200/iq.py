@@ -34,6 +34,9 @@ SIGNATURES = {
     "iq_weight_cache_clear": (_I, []),
     "iq_matvec_dev": (_I, [_P, _P, _P, _I, _I, _P]),
     "iq_gemm_dev": (_I, [_P, _P, _P, _I, _I, _I, _P]),
+    "iq_pack_weights_dev": (_I, [_P, _I, _I, _P, _P]),
+    "iq_packed_free": (_I, [_P]),
+    "iq_matvec_packed_dev": (_I, [_P, _P, _P, _P]),
     "iq_fp_dev": (_I, [_I, _P, _P, _P, _I64, _P]),
     "iq_rmsnorm_dev": (_I, [_P, _P, _P, _I, _I, _P]),
     "iq_softmax_dev": (_I, [_P, _I, _I, _P]),
@@ -136,6 +139,30 @@ def set_device(d):
 
 def matvec_dev(out, w, x, M, N, stream=None):
     _call("iq_matvec_dev", _dp(out), _dp(w), _dp(x), M, N, _sp(stream))
+
+
+class Packed:
+    """Byte-plane packed weights on the device (iq_pack_weights_dev)."""
+
+    def __init__(self, d_w, M, N, stream=None):
+        self.h = ctypes.c_void_p()
+        self.M, self.N = M, N
+        _call("iq_pack_weights_dev", _dp(d_w), M, N, _sp(stream), ctypes.byref(self.h))
+
+    def free(self):
+        if self.h:
+            _call("iq_packed_free", self.h)
+            self.h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def matvec_packed_dev(out, packed, x, stream=None):
+    _call("iq_matvec_packed_dev", _dp(out), packed.h, _dp(x), _sp(stream))
 
 
 def gemm_dev(out, w, X, rows, M, N, stream=None):

@@ -202,3 +202,28 @@ def test_rmsnorm_softmax_vs_oracle():
         ds = dev(s)
         iq.softmax_dev(ds, rows, dim)
         assert (host(ds) == want).all()
+
+
+# ------------------------------------------------------------ packed planes
+
+@pytest.mark.parametrize("M,N", [(1, 1), (3, 17), (5, 64), (16, 32), (17, 33), (64, 1000), (33, 2048),
+                                 (1000, 63), (129, 4097), (7, 40000), (2048, 2048)])
+@pytest.mark.parametrize("dist", ["full", "cfg"])
+def test_matvec_packed_vs_oracle(M, N, dist):
+    """Byte-plane tensor-core matvec: exact on full-range int64 (mod 2^128 wrap)
+    and on config-distributed inputs; repeated launches (row scratch resets)."""
+    import torch
+    rng = np.random.default_rng(M * 31 + N)
+    if dist == "full":
+        w, x = rand_full(rng, (M, N)), rand_full(rng, (N,))
+    else:
+        w = orc.synth_weights(1, f"w:{M}x{N}", (M, N))
+        x = orc.synth_acts(1, f"x:{M}x{N}", (N,))
+    want = orc.matmul_vec(w, x)
+    pk = iq.Packed(dev(w), M, N)
+    dx = dev(x)
+    for _ in range(2):
+        do = torch.zeros(M, dtype=torch.int64, device="cuda")
+        iq.matvec_packed_dev(do, pk, dx)
+        assert (host(do) == want).all()
+    pk.free()
