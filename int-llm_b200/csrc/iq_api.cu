@@ -158,9 +158,10 @@ static void free_packed(Packed *P) {
 
 // racc: RowAcc scratch with >= M zeroed entries (zero again on completion).
 int launch_matvec_planes(int64_t *out, const Packed &P, const int64_t *x, cudaStream_t s, int add, RowAcc *racc) {
-    auto kern = k_matvec_planes<2>;
     size_t smem = (size_t)8 * (P.Kp + 16);
-    if (smem > 200 * 1024) return IQ_ERR_UNSUPPORTED;
+    bool xs = smem <= 100 * 1024;
+    auto kern = xs ? k_matvec_planes<2, true> : k_matvec_planes<2, false>;
+    if (!xs) smem = 0;
     if (smem > 48 * 1024) IQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int occ = 0;
     IQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 256, smem));

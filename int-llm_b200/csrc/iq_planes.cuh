@@ -145,18 +145,32 @@ __device__ __forceinline__ void fold_planes(int (&c)[8][4], int t, i128 &r0, i12
     }
 }
 
-template <int UNROLL>
-__global__ void __launch_bounds__(256)
+// 4 digits j of x_u[k..k+3] packed into one word (byte i = element k+i)
+__device__ __forceinline__ uint32_t digit_word(const int64_t *__restrict__ xg, int N, int k, int j) {
+    uint32_t v = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        uint64_t xu = (k + i < N ? (uint64_t)__ldg(xg + k + i) : 0ull) ^ 0x8000000000000000ull;
+        v |= (uint32_t)((xu >> (8 * j)) & 0xff) << (8 * i);
+    }
+    return v;
+}
+
+// XSMEM: digits staged in shared memory (Kp small enough), else gathered from
+// x in global memory (L1-cached) per column tile.
+template <int UNROLL, bool XSMEM>
+__global__ void __launch_bounds__(256, 2)
 k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const int64_t *__restrict__ rowsum,
                 const int64_t *__restrict__ xg, int M, int N, int Kp, int add, RowAcc *__restrict__ racc) {
     extern __shared__ __align__(16) unsigned char xd[];  // [8][Kp + 16] digit rows
     const int ld = Kp + 16;
-    for (int k = threadIdx.x; k < Kp; k += blockDim.x) {
-        uint64_t xu = (k < N ? (uint64_t)xg[k] : 0ull) ^ 0x8000000000000000ull;
+    if (XSMEM) {
+        for (int k = 4 * threadIdx.x; k < Kp; k += 4 * blockDim.x)
 #pragma unroll
-        for (int j = 0; j < 8; j++) xd[j * ld + k] = (unsigned char)(xu >> (8 * j));
+            for (int j = 0; j < 8; j++)
+                *reinterpret_cast<uint32_t *>(xd + j * ld + k) = digit_word(xg, N, k, j);
+        __syncthreads();
     }
-    __syncthreads();
 
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int KT = Kp / 32, RT = (M + 15) / 16;
@@ -190,8 +204,14 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
             for (int v = 0; v < UNROLL; v++) {
                 if (kt + v < k1) {
                     const int kk = (kt + v) * 32;
-                    uint32_t b0 = *reinterpret_cast<const uint32_t *>(xb + kk);
-                    uint32_t b1 = *reinterpret_cast<const uint32_t *>(xb + kk + 16);
+                    uint32_t b0, b1;
+                    if (XSMEM) {
+                        b0 = *reinterpret_cast<const uint32_t *>(xb + kk);
+                        b1 = *reinterpret_cast<const uint32_t *>(xb + kk + 16);
+                    } else {
+                        b0 = digit_word(xg, N, kk + 4 * t, g);
+                        b1 = digit_word(xg, N, kk + 16 + 4 * t, g);
+                    }
 #pragma unroll
                     for (int p = 0; p < 7; p++) mma_i8<false>(c[p], a[v][p], b0, b1);
                     mma_i8<true>(c[7], a[v][7], b0, b1);

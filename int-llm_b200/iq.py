@@ -105,7 +105,14 @@ def _dp(t):
 
 
 def _sp(stream):
+    """Stream argument: an explicit stream, else torch's current stream when torch
+    has initialised CUDA (so device calls order with the tensors' producers),
+    else NULL = the library's own stream."""
     if stream is None:
+        import sys
+        t = sys.modules.get("torch")
+        if t is not None and t.cuda.is_initialized():
+            return ctypes.c_void_p(t.cuda.current_stream().cuda_stream)
         return None
     return ctypes.c_void_p(getattr(stream, "cuda_stream", stream))
 
