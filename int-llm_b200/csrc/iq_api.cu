@@ -160,7 +160,8 @@ static void free_packed(Packed *P) {
 int launch_matvec_planes(int64_t *out, const Packed &P, const int64_t *x, cudaStream_t s, int add, RowAcc *racc) {
     size_t smem = (size_t)8 * (P.Kp + 16);
     bool xs = smem <= 100 * 1024;
-    auto kern = xs ? k_matvec_planes<2, true> : k_matvec_planes<2, false>;
+    // one column tile per loop trip measured fastest (more warps resident)
+    auto kern = xs ? k_matvec_planes<1, true> : k_matvec_planes<1, false>;
     if (!xs) smem = 0;
     if (smem > 48 * 1024) IQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int occ = 0;

@@ -165,10 +165,20 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
     extern __shared__ __align__(16) unsigned char xd[];  // [8][Kp + 16] digit rows
     const int ld = Kp + 16;
     if (XSMEM) {
-        for (int k = 4 * threadIdx.x; k < Kp; k += 4 * blockDim.x)
+        // each thread: 4 consecutive x values -> 8 digit words (one per digit row)
+        for (int k = 4 * threadIdx.x; k < Kp; k += 4 * blockDim.x) {
+            uint64_t xu[4];
 #pragma unroll
-            for (int j = 0; j < 8; j++)
-                *reinterpret_cast<uint32_t *>(xd + j * ld + k) = digit_word(xg, N, k, j);
+            for (int i = 0; i < 4; i++)
+                xu[i] = (k + i < N ? (uint64_t)__ldg(xg + k + i) : 0ull) ^ 0x8000000000000000ull;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                uint32_t v = 0;
+#pragma unroll
+                for (int i = 0; i < 4; i++) v |= (uint32_t)((xu[i] >> (8 * j)) & 0xff) << (8 * i);
+                *reinterpret_cast<uint32_t *>(xd + j * ld + k) = v;
+            }
+        }
         __syncthreads();
     }
 
