@@ -95,6 +95,21 @@ IQ_API int iq_pack_weights_dev(const int64_t *d_w, int M, int N, void *stream, i
 IQ_API int iq_packed_free(iq_packed *p);
 IQ_API int iq_matvec_packed_dev(int64_t *d_out, const iq_packed *w, const int64_t *d_in, void *stream);
 
+/* Same result as iq_matvec_packed_dev, but allocates no device memory: for
+ * callers that cannot call cudaMalloc when they run (a process whose device
+ * memory is owned by an external pool or budget, or a latency-critical loop
+ * that must not hit an allocation's implicit synchronisation). No counterpart
+ * in the reference, which has no device memory at all.
+ * Its scratch is a fixed array inside the library, one per GPU, kept until the
+ * process exits; it holds IQ_NOALLOC_MAX_ROWS = 32768 rows (the padded row
+ * count, M rounded up to 16), and larger matrices are rejected with
+ * IQ_ERR_RANGE. The first call on each device looks up and clears that array
+ * (make it before any stream capture). All calls share the array: calls that
+ * overlap on one GPU (on different streams, or issued from several host
+ * threads) race and give wrong results; serialise them. */
+IQ_API int iq_matvec_packed_noalloc_dev(int64_t *d_out, const iq_packed *w, const int64_t *d_in,
+                                        void *stream);
+
 /* Batched rows: d_out[r][i] = matmul_vec(d_w, d_X[r])[i] for r < rows, i.e.
  * exactly `rows` independent calls of llama_int.c:1014 (the reference has no
  * batched form; its prefill loops M=1 calls, llama_int.c:3081-3092).

@@ -396,6 +396,12 @@ IQ_API int iq_softmax_dev(int64_t *d_x, int rows, int n, void *stream) {
 
 struct iq_packed { Packed P; int dev; };
 
+// Accessor for iq_noalloc.cu (the packed handle's layout stays private here).
+const Packed *iq_packed_inner(const iq_packed *w, int *dev) {
+    *dev = w->dev;
+    return &w->P;
+}
+
 IQ_API int iq_pack_weights_dev(const int64_t *d_w, int M, int N, void *stream, iq_packed **out) {
     if (!d_w || !out || M <= 0 || N <= 0) return IQ_ERR_ARG;
     *out = nullptr;

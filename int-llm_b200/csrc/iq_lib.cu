@@ -3,3 +3,4 @@
 #include "iq_api.cu"
 #include "iq_model.cu"
 #include "iq_synth.cu"
+#include "iq_noalloc.cu"

@@ -37,6 +37,7 @@ SIGNATURES = {
     "iq_pack_weights_dev": (_I, [_P, _I, _I, _P, _P]),
     "iq_packed_free": (_I, [_P]),
     "iq_matvec_packed_dev": (_I, [_P, _P, _P, _P]),
+    "iq_matvec_packed_noalloc_dev": (_I, [_P, _P, _P, _P]),
     "iq_fp_dev": (_I, [_I, _P, _P, _P, _I64, _P]),
     "iq_rmsnorm_dev": (_I, [_P, _P, _P, _I, _I, _P]),
     "iq_softmax_dev": (_I, [_P, _I, _I, _P]),
