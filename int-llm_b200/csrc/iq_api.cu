@@ -157,6 +157,7 @@ static void free_packed(Packed *P) {
 }
 
 // racc: RowAcc scratch with >= M zeroed entries (zero again on completion).
+
 int launch_matvec_planes(int64_t *out, const Packed &P, const int64_t *x, cudaStream_t s, int add, RowAcc *racc) {
     size_t smem = (size_t)8 * (P.Kp + 16);
     bool xs = smem <= 100 * 1024;

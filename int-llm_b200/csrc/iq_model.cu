@@ -36,6 +36,10 @@ struct iq_model {
     int64_t *hidden = nullptr, *normed = nullptr, *qkv = nullptr, *att = nullptr, *gu = nullptr,
             *act = nullptr, *logits = nullptr;
     int *d_tok = nullptr, *d_pos = nullptr, *d_arg = nullptr, *d_hist = nullptr;
+    // byte-plane packed copies of every projection (M=1 decode path)
+    std::vector<Packed> pqkv, po, pgu, pdown;
+    Packed plm;
+    RowAcc *racc = nullptr;  // split-row scratch of the packed matvec (self-resetting)
     int *h_pin = nullptr;  // pinned host scratch: tokens / pos / argmax
     int64_t *h_logits = nullptr;
     size_t attn_smem = 0;
@@ -79,6 +83,13 @@ static int model_alloc(iq_model *m) {
     m->norm1.resize(L); m->wqkv.resize(L); m->wo.resize(L); m->norm2.resize(L);
     m->wgu.resize(L); m->wdown.resize(L); m->kc.resize(L); m->vc.resize(L);
     m->loaded_layer.assign(L, false);
+    m->pqkv.resize(L); m->po.resize(L); m->pgu.resize(L); m->pdown.resize(L);
+    {
+        size_t rows = std::max(std::max((size_t)c.vocab_size, (size_t)m->qkv_rows),
+                               std::max((size_t)2 * c.intermediate_dim, (size_t)d)) + 16;
+        DALLOC(m->racc, rows * sizeof(RowAcc));
+        IQ_CUDA(cudaMemset(m->racc, 0, rows * sizeof(RowAcc)));
+    }
     for (int l = 0; l < L; l++) {
         DALLOC(m->norm1[l], (size_t)d * 8);
         DALLOC(m->wqkv[l], (size_t)m->qkv_rows * d * 8);
@@ -122,8 +133,9 @@ static int enqueue_step(iq_model *m, int B) {
     const int d = c.hidden_dim, inter = c.intermediate_dim, hd = c.head_dim;
     cudaStream_t s = m->s;
     int rc;
-    auto proj = [&](int64_t *out, const int64_t *W, const int64_t *x, int M, int N, int add) -> int {
-        if (B == 1) return launch_matvec(out, W, x, M, N, s, add);
+    auto proj = [&](int64_t *out, const int64_t *W, const Packed &P, const int64_t *x, int M, int N,
+                    int add) -> int {
+        if (B == 1) return launch_matvec_planes(out, P, x, s, add, m->racc);
         return launch_gemm_add(out, W, x, B, M, N, s, add);
     };
     k_embed<<<dim3((d + 255) / 256, B), 256, 0, s>>>(m->hidden, m->embed, m->d_tok, d);
@@ -132,7 +144,7 @@ static int enqueue_step(iq_model *m, int B) {
     for (int l = 0; l < c.num_layers; l++) {
         k_rmsnorm<<<B, 256, 0, s>>>(m->normed, m->hidden, m->norm1[l], d);
         IQ_CHECK_LAUNCH();
-        if ((rc = proj(m->qkv, m->wqkv[l], m->normed, m->qkv_rows, d, 0))) return rc;
+        if ((rc = proj(m->qkv, m->wqkv[l], m->pqkv[l], m->normed, m->qkv_rows, d, 0))) return rc;
         k_rope_kv<<<dim3((pairs + 255) / 256, B), 256, 0, s>>>(m->qkv, m->kc[l], m->vc[l], m->rcos, m->rsin,
                                                                m->d_pos, c.num_heads, c.num_kv_heads, hd,
                                                                c.max_seq_len);
@@ -141,17 +153,17 @@ static int enqueue_step(iq_model *m, int B) {
                                                                     c.num_heads, c.num_kv_heads, hd,
                                                                     c.max_seq_len);
         IQ_CHECK_LAUNCH();
-        if ((rc = proj(m->hidden, m->wo[l], m->att, d, d, 1))) return rc;
+        if ((rc = proj(m->hidden, m->wo[l], m->po[l], m->att, d, d, 1))) return rc;
         k_rmsnorm<<<B, 256, 0, s>>>(m->normed, m->hidden, m->norm2[l], d);
         IQ_CHECK_LAUNCH();
-        if ((rc = proj(m->gu, m->wgu[l], m->normed, 2 * inter, d, 0))) return rc;
+        if ((rc = proj(m->gu, m->wgu[l], m->pgu[l], m->normed, 2 * inter, d, 0))) return rc;
         k_swiglu<<<(B * inter + 255) / 256, 256, 0, s>>>(m->act, m->gu, inter, B);
         IQ_CHECK_LAUNCH();
-        if ((rc = proj(m->hidden, m->wdown[l], m->act, d, inter, 1))) return rc;
+        if ((rc = proj(m->hidden, m->wdown[l], m->pdown[l], m->act, d, inter, 1))) return rc;
     }
     k_rmsnorm<<<B, 256, 0, s>>>(m->normed, m->hidden, m->fnorm, d);
     IQ_CHECK_LAUNCH();
-    if ((rc = proj(m->logits, m->lm, m->normed, c.vocab_size, d, 0))) return rc;
+    if ((rc = proj(m->logits, m->lm, m->plm, m->normed, c.vocab_size, d, 0))) return rc;
     k_argmax<<<B, 1024, 0, s>>>(m->d_arg, m->logits, c.vocab_size, m->d_tok, m->d_pos, m->d_hist,
                                 c.max_seq_len + 1);
     IQ_CHECK_LAUNCH();
@@ -188,6 +200,22 @@ static int h2d(void *dst, const void *src, size_t bytes) {
 static int fill_const(int64_t *dst, int64_t v, size_t n) {
     std::vector<int64_t> h(n, v);
     return h2d(dst, h.data(), n * 8);
+}
+
+static int repack(iq_model *m, Packed *P, const int64_t *W, int M, int N) {
+    if (P->planes) { IQ_CUDA(cudaStreamSynchronize(m->s)); free_packed(P); }
+    int rc = pack_weights(W, M, N, m->s, P);
+    if (rc) return rc;
+    IQ_CUDA(cudaStreamSynchronize(m->s));
+    return IQ_OK;
+}
+static int repack_layer(iq_model *m, int l) {
+    const iq_config &c = m->c;
+    int rc, d = c.hidden_dim, it = c.intermediate_dim;
+    if ((rc = repack(m, &m->pqkv[l], m->wqkv[l], m->qkv_rows, d))) return rc;
+    if ((rc = repack(m, &m->po[l], m->wo[l], d, d))) return rc;
+    if ((rc = repack(m, &m->pgu[l], m->wgu[l], 2 * it, d))) return rc;
+    return repack(m, &m->pdown[l], m->wdown[l], d, it);
 }
 
 extern "C" {
@@ -234,6 +262,10 @@ IQ_API int iq_model_destroy(iq_model *m) {
     for (void *p : bufs) if (p) cudaFree(p);
     for (auto *v : {&m->norm1, &m->wqkv, &m->wo, &m->norm2, &m->wgu, &m->wdown, &m->kc, &m->vc})
         for (int64_t *p : *v) if (p) cudaFree(p);
+    for (auto *v : {&m->pqkv, &m->po, &m->pgu, &m->pdown})
+        for (Packed &P : *v) free_packed(&P);
+    free_packed(&m->plm);
+    if (m->racc) cudaFree(m->racc);
     if (m->h_pin) cudaFreeHost(m->h_pin);
     if (m->h_logits) cudaFreeHost(m->h_logits);
     if (m->s) cudaStreamDestroy(m->s);
@@ -250,6 +282,7 @@ IQ_API int iq_model_load_globals(iq_model *m, const int64_t *embed, const int64_
     if ((rc = h2d(m->embed, embed, (size_t)c.vocab_size * c.hidden_dim * 8))) return rc;
     if ((rc = h2d(m->fnorm, final_norm, (size_t)c.hidden_dim * 8))) return rc;
     if ((rc = h2d(m->lm, lm_head, (size_t)c.vocab_size * c.hidden_dim * 8))) return rc;
+    if ((rc = repack(m, &m->plm, m->lm, c.vocab_size, c.hidden_dim))) return rc;
     m->loaded_globals = true;
     return IQ_OK;
 }
@@ -269,6 +302,7 @@ IQ_API int iq_model_load_layer(iq_model *m, int l, const int64_t *const w[9]) {
     if ((rc = h2d(m->wgu[l], w[6], it * d * 8))) return rc;
     if ((rc = h2d(m->wgu[l] + it * d, w[7], it * d * 8))) return rc;
     if ((rc = h2d(m->wdown[l], w[8], d * it * 8))) return rc;
+    if ((rc = repack_layer(m, l))) return rc;
     m->loaded_layer[l] = true;
     return IQ_OK;
 }
@@ -334,6 +368,11 @@ IQ_API int iq_model_synth(iq_model *m, int config_index, int threads) {
     for (int t = 0; t < threads; t++) pool.emplace_back(worker);
     for (auto &t : pool) t.join();
     if (status.load() != IQ_OK) return status.load();
+    int rc;
+    IQ_CUDA(cudaSetDevice(m->dev));
+    if ((rc = repack(m, &m->plm, m->lm, c.vocab_size, c.hidden_dim))) return rc;
+    for (int l = 0; l < c.num_layers; l++)
+        if ((rc = repack_layer(m, l))) return rc;
     m->loaded_globals = true;
     m->loaded_layer.assign(c.num_layers, true);
     return IQ_OK;
