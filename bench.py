@@ -107,7 +107,7 @@ def load_traffic():
     """dram bytes per launch of the dominant kernel from the committed ncu summary."""
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            return json.load(f).get("k_matvec_per_step_bytes")
+            return json.load(f).get("k_matvec_planes_per_step_bytes")
     except Exception:
         return None
 
