@@ -147,6 +147,24 @@ typedef struct iq_config {
 typedef struct iq_model iq_model;
 
 IQ_API int iq_model_create(const iq_config *cfg, int max_batch, int device, iq_model **out);
+
+/* Tensor-parallel model: rank tp_rank of tp_size, one process (or thread) per
+ * GPU, every rank calling every model entry point in lockstep. Each rank keeps
+ * the output rows it owns of every projection (a contiguous block of q heads
+ * with the kv heads they read, 1/tp_size of the rows of O, gate, up, down and
+ * the LM head) and all-gathers each projection's output over NCCL, so results
+ * are bit-identical to tp_size = 1. Load / synth calls take the FULL tensors;
+ * each rank copies its rows. nccl_id: 128 bytes from iq_nccl_unique_id on one
+ * rank, shared with the others (no reference counterpart: the reference is
+ * single-threaded). num_heads, hidden_dim, intermediate_dim and vocab_size
+ * must divide by tp_size. */
+IQ_API int iq_nccl_unique_id(void *id_out);
+/* Rows owned by tp_rank (host-only query, no device work): info = {first q
+ * head, q heads, first kv head, kv heads, first O/down row, O/down rows, first
+ * gate/up row, gate/up rows}; LM-head rows are [rank*V/P, (rank+1)*V/P). */
+IQ_API int iq_tp_shard_info(const iq_config *cfg, int tp_size, int tp_rank, int info[8]);
+IQ_API int iq_model_create_tp(const iq_config *cfg, int max_batch, int device, int tp_rank, int tp_size,
+                              const void *nccl_id, iq_model **out);
 IQ_API int iq_model_destroy(iq_model *m);
 /* Global tensors from host memory: embed_tokens [vocab][dim], final norm [dim],
  * lm_head [vocab][dim] (llama_int.c:1575-1580; an untied head). */

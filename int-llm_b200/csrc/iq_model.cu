@@ -3,11 +3,18 @@
 // built from the kernels in iq_layer.cuh, captured once into a CUDA graph and
 // replayed per token; greedy generate (llama_int.c:3067-3135) on top.
 //
-// Per layer the step is 7 launches:
-//   rmsnorm -> QKV matvec (q|k|v rows fused, exact: rows are independent)
-//   -> RoPE + KV write -> attention -> O matvec (+= residual)
-//   -> rmsnorm -> gate|up matvec (fused rows) -> SwiGLU -> down matvec (+= residual)
-// then final rmsnorm, LM head matvec and argmax.
+// Tensor parallelism (output rows): rank r of P owns a contiguous block of q
+// heads, the kv heads they read (a kv head is replicated on every rank whose q
+// heads use it when P > n_kv), rows [r*d/P, (r+1)*d/P) of O and down,
+// rows [r*inter/P, ...) of gate and of up, and rows [r*V/P, ...) of the LM
+// head. Every projection output is all-gathered (NCCL, int64, a pure copy), so
+// no partial sum ever crosses a GPU and the result is bit-identical at every P.
+// Per layer: rmsnorm -> QKV (local heads) -> RoPE + KV write -> attention
+// (local heads) -> gather -> O rows -> gather -> += residual -> rmsnorm ->
+// gate|up rows -> SwiGLU -> gather -> down rows -> gather -> += residual;
+// then final rmsnorm, LM-head rows, gather of the logits, first-max argmax.
+// With P = 1 the gathers vanish and the residual adds fuse into the O and
+// down projections' epilogues.
 #include <cstring>
 #include <thread>
 #include <atomic>
@@ -15,42 +22,73 @@
 #include <algorithm>
 #include <cstdio>
 #include <vector>
+#include <nccl.h>
 #include "iq_common.cuh"
 #include "iq_layer.cuh"
 
-
 using namespace iq;
+
+struct Shard {
+    int P = 1, r = 0;
+    int nh_l = 0, nkv_l = 0;         // local q / kv heads
+    int q_lo = 0, kv_lo = 0;         // first local q / kv head (global index)
+    int d_l = 0, it_l = 0, v_l = 0;  // local rows of O/down, of gate (and of up), of the LM head
+};
+
+// Row ownership of rank r among P; IQ_ERR_ARG where the shapes do not divide.
+static int make_shard(const iq_config &c, int P, int r, Shard *s) {
+    if (P < 1 || r < 0 || r >= P) return IQ_ERR_ARG;
+    if (c.num_heads % P || c.hidden_dim % P || c.intermediate_dim % P || c.vocab_size % P) return IQ_ERR_ARG;
+    const int grp = c.num_heads / c.num_kv_heads;
+    s->P = P; s->r = r;
+    s->nh_l = c.num_heads / P;
+    s->q_lo = r * s->nh_l;
+    const int kv_first = s->q_lo / grp, kv_last = (s->q_lo + s->nh_l - 1) / grp;
+    s->kv_lo = kv_first;
+    s->nkv_l = kv_last - kv_first + 1;
+    // local head h_l must read local kv head h_l / (nh_l / nkv_l), the same map as globally
+    if (s->nh_l % s->nkv_l || s->nh_l / s->nkv_l != std::min(grp, s->nh_l)) return IQ_ERR_ARG;
+    if (grp < s->nh_l && s->nh_l % grp) return IQ_ERR_ARG;
+    s->d_l = c.hidden_dim / P;
+    s->it_l = c.intermediate_dim / P;
+    s->v_l = c.vocab_size / P;
+    return IQ_OK;
+}
 
 struct iq_model {
     iq_config c;
+    Shard sh;
     int dev = 0;
     int max_batch = 1;
-    int kvd = 0, qkv_rows = 0;
+    int kvd_l = 0, qkv_rows = 0;  // local kv width, local fused QKV rows
     cudaStream_t s = nullptr;
-    // weights
+    ncclComm_t comm = nullptr;
+    // weights (local rows)
     int64_t *embed = nullptr, *fnorm = nullptr, *lm = nullptr;
     std::vector<int64_t *> norm1, wqkv, wo, norm2, wgu, wdown;
-    std::vector<int64_t *> kc, vc;  // per layer [B][max_seq][kvd]
+    std::vector<int64_t *> kc, vc;  // per layer [B][max_seq][kvd_l]
     int64_t *rcos = nullptr, *rsin = nullptr;
-    // activations (device)
-    int64_t *hidden = nullptr, *normed = nullptr, *qkv = nullptr, *att = nullptr, *gu = nullptr,
-            *act = nullptr, *logits = nullptr;
-    int *d_tok = nullptr, *d_pos = nullptr, *d_arg = nullptr, *d_hist = nullptr;
     // byte-plane packed copies of every projection (M=1 decode path)
     std::vector<Packed> pqkv, po, pgu, pdown;
     Packed plm;
     RowAcc *racc = nullptr;  // split-row scratch of the packed matvec (self-resetting)
+    // activations (device)
+    int64_t *hidden = nullptr, *normed = nullptr, *qkv = nullptr, *att = nullptr, *gu = nullptr,
+            *act = nullptr, *logits = nullptr;
+    // tensor-parallel buffers: local pieces and gather staging (P > 1)
+    int64_t *att_l = nullptr, *proj_l = nullptr, *act_l = nullptr, *logits_l = nullptr, *gath = nullptr,
+            *proj_full = nullptr;
+    int *d_tok = nullptr, *d_pos = nullptr, *d_arg = nullptr, *d_hist = nullptr;
     int *h_pin = nullptr;  // pinned host scratch: tokens / pos / argmax
     int64_t *h_logits = nullptr;
     size_t attn_smem = 0;
-    // graph of one decode step at batch max_batch
-    cudaGraphExec_t graph = nullptr;
+    cudaGraphExec_t graph = nullptr;  // one decode step at batch max_batch
     bool loaded_globals = false;
     std::vector<bool> loaded_layer;
 };
 
 static int dalloc(void **p, size_t bytes) {
-    cudaError_t e = cudaMalloc(p, bytes);
+    cudaError_t e = cudaMalloc(p, bytes ? bytes : 8);
     if (e != cudaSuccess) return cuda_fail(e);
     return IQ_OK;
 }
@@ -72,45 +110,69 @@ __global__ void k_rope_init(int64_t *cs, int64_t *sn, int hd, int max_seq, int t
     }
 }
 
+// x[i] += y[i] (int64 wrap): the residual adds of llama_int.c:1535, 1556
+__global__ void k_add(int64_t *__restrict__ x, const int64_t *__restrict__ y, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        x[i] = (int64_t)((uint64_t)x[i] + (uint64_t)y[i]);
+}
+
+// all-gather output [P][B][w] -> [B][P*w]
+__global__ void k_unshard(int64_t *__restrict__ out, const int64_t *__restrict__ g, int P, int B, int w) {
+    const int64_t n = (int64_t)P * B * w;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        int64_t p = e / ((int64_t)B * w), rem = e % ((int64_t)B * w);
+        int64_t b = rem / w, i = rem % w;
+        out[b * (int64_t)P * w + p * w + i] = g[e];
+    }
+}
+
 static int model_alloc(iq_model *m) {
     const iq_config &c = m->c;
-    const int B = m->max_batch, d = c.hidden_dim, L = c.num_layers;
-    m->kvd = c.num_kv_heads * c.head_dim;
-    m->qkv_rows = d + 2 * m->kvd;
+    const Shard &S = m->sh;
+    const int B = m->max_batch, d = c.hidden_dim, L = c.num_layers, hd = c.head_dim;
+    m->kvd_l = S.nkv_l * hd;
+    m->qkv_rows = S.nh_l * hd + 2 * m->kvd_l;
     DALLOC(m->embed, (size_t)c.vocab_size * d * 8);
     DALLOC(m->fnorm, (size_t)d * 8);
-    DALLOC(m->lm, (size_t)c.vocab_size * d * 8);
+    DALLOC(m->lm, (size_t)S.v_l * d * 8);
     m->norm1.resize(L); m->wqkv.resize(L); m->wo.resize(L); m->norm2.resize(L);
     m->wgu.resize(L); m->wdown.resize(L); m->kc.resize(L); m->vc.resize(L);
-    m->loaded_layer.assign(L, false);
     m->pqkv.resize(L); m->po.resize(L); m->pgu.resize(L); m->pdown.resize(L);
-    {
-        size_t rows = std::max(std::max((size_t)c.vocab_size, (size_t)m->qkv_rows),
-                               std::max((size_t)2 * c.intermediate_dim, (size_t)d)) + 16;
-        DALLOC(m->racc, rows * sizeof(RowAcc));
-        IQ_CUDA(cudaMemset(m->racc, 0, rows * sizeof(RowAcc)));
-    }
+    m->loaded_layer.assign(L, false);
     for (int l = 0; l < L; l++) {
         DALLOC(m->norm1[l], (size_t)d * 8);
         DALLOC(m->wqkv[l], (size_t)m->qkv_rows * d * 8);
-        DALLOC(m->wo[l], (size_t)d * d * 8);
+        DALLOC(m->wo[l], (size_t)S.d_l * d * 8);
         DALLOC(m->norm2[l], (size_t)d * 8);
-        DALLOC(m->wgu[l], (size_t)2 * c.intermediate_dim * d * 8);
-        DALLOC(m->wdown[l], (size_t)d * c.intermediate_dim * 8);
-        size_t kvb = (size_t)B * c.max_seq_len * m->kvd * 8;
+        DALLOC(m->wgu[l], (size_t)2 * S.it_l * d * 8);
+        DALLOC(m->wdown[l], (size_t)S.d_l * c.intermediate_dim * 8);
+        size_t kvb = (size_t)B * c.max_seq_len * m->kvd_l * 8;
         DALLOC(m->kc[l], kvb);
         DALLOC(m->vc[l], kvb);
     }
-    size_t half = c.head_dim / 2;
+    size_t rows = std::max(std::max((size_t)S.v_l, (size_t)m->qkv_rows),
+                           std::max((size_t)2 * S.it_l, (size_t)d)) + 16;
+    DALLOC(m->racc, rows * sizeof(RowAcc));
+    IQ_CUDA(cudaMemset(m->racc, 0, rows * sizeof(RowAcc)));
+    size_t half = hd / 2;
     DALLOC(m->rcos, (size_t)c.max_seq_len * half * 8);
     DALLOC(m->rsin, (size_t)c.max_seq_len * half * 8);
     DALLOC(m->hidden, (size_t)B * d * 8);
     DALLOC(m->normed, (size_t)B * d * 8);
     DALLOC(m->qkv, (size_t)B * m->qkv_rows * 8);
     DALLOC(m->att, (size_t)B * d * 8);
-    DALLOC(m->gu, (size_t)B * 2 * c.intermediate_dim * 8);
+    DALLOC(m->gu, (size_t)B * 2 * S.it_l * 8);
     DALLOC(m->act, (size_t)B * c.intermediate_dim * 8);
     DALLOC(m->logits, (size_t)B * c.vocab_size * 8);
+    if (S.P > 1) {
+        size_t wmax = std::max(std::max((size_t)d, (size_t)c.intermediate_dim), (size_t)c.vocab_size);
+        DALLOC(m->att_l, (size_t)B * S.nh_l * hd * 8);
+        DALLOC(m->proj_l, (size_t)B * S.d_l * 8);
+        DALLOC(m->act_l, (size_t)B * S.it_l * 8);
+        DALLOC(m->logits_l, (size_t)B * S.v_l * 8);
+        DALLOC(m->gath, (size_t)B * wmax * 8);
+        DALLOC(m->proj_full, (size_t)B * d * 8);
+    }
     DALLOC(m->d_tok, (size_t)B * 4);
     DALLOC(m->d_pos, (size_t)B * 4);
     DALLOC(m->d_arg, (size_t)B * 4);
@@ -119,18 +181,44 @@ static int model_alloc(iq_model *m) {
     IQ_CUDA(cudaMallocHost(&m->h_pin, ((size_t)B + 16 + (size_t)2 * B * (c.max_seq_len + 2)) * 4));
     IQ_CUDA(cudaMallocHost(&m->h_logits, (size_t)c.vocab_size * 8));
     int groups_area = 256;  // attention block size (PV partials reuse the score area)
-    m->attn_smem = (size_t)(c.head_dim + (c.max_seq_len > groups_area ? c.max_seq_len : groups_area)) * 8;
+    m->attn_smem = (size_t)(hd + (c.max_seq_len > groups_area ? c.max_seq_len : groups_area)) * 8;
     return IQ_OK;
 }
 
 // ---------------------------------------------------------------- the step
 
+static int nccl_fail(ncclResult_t r) { return r == ncclSuccess ? IQ_OK : IQ_ERR_NCCL; }
+#define IQ_NCCL(call) do { ncclResult_t _r = (call); if (_r != ncclSuccess) return nccl_fail(_r); } while (0)
+
+// all-gather of a [B][w] local piece into out [B][P*w] (rank-major columns)
+static int gather_rows(iq_model *m, const int64_t *local, int64_t *out, int B, int w) {
+    const int P = m->sh.P;
+    if (B == 1) {
+        IQ_NCCL(ncclAllGather(local, out, (size_t)w, ncclInt64, m->comm, m->s));
+        return IQ_OK;
+    }
+    IQ_NCCL(ncclAllGather(local, m->gath, (size_t)B * w, ncclInt64, m->comm, m->s));
+    int64_t n = (int64_t)P * B * w;
+    k_unshard<<<(int)std::min<int64_t>((n + 255) / 256, 4096), 256, 0, m->s>>>(out, m->gath, P, B, w);
+    IQ_CHECK_LAUNCH();
+    return IQ_OK;
+}
+
+static int add_into(iq_model *m, int64_t *x, const int64_t *y, int64_t n) {
+    k_add<<<(int)std::min<int64_t>((n + 255) / 256, 4096), 256, 0, m->s>>>(x, y, n);
+    IQ_CHECK_LAUNCH();
+    return IQ_OK;
+}
+
 // Enqueues one forward step for sequences [0, B): tokens in d_tok, positions in
-// d_pos (both device), logits -> m->logits, argmax -> d_arg; the argmax kernel
-// then advances d_tok / d_pos and records the token in d_hist.
+// d_pos (both device), logits -> m->logits (full vocabulary on every rank),
+// argmax -> d_arg; the argmax kernel then advances d_tok / d_pos and records the
+// token in d_hist.
 static int enqueue_step(iq_model *m, int B) {
     const iq_config &c = m->c;
-    const int d = c.hidden_dim, inter = c.intermediate_dim, hd = c.head_dim;
+    const Shard &S = m->sh;
+    const bool tp = S.P > 1;
+    const int d = c.hidden_dim, hd = c.head_dim;
     cudaStream_t s = m->s;
     int rc;
     auto proj = [&](int64_t *out, const int64_t *W, const Packed &P, const int64_t *x, int M, int N,
@@ -140,30 +228,49 @@ static int enqueue_step(iq_model *m, int B) {
     };
     k_embed<<<dim3((d + 255) / 256, B), 256, 0, s>>>(m->hidden, m->embed, m->d_tok, d);
     IQ_CHECK_LAUNCH();
-    const int pairs = (c.num_heads + c.num_kv_heads) * (hd / 2) + m->kvd;
+    const int pairs = (S.nh_l + S.nkv_l) * (hd / 2) + m->kvd_l;
+    int64_t *att_out = tp ? m->att_l : m->att;
+    int64_t *act_out = tp ? m->act_l : m->act;
     for (int l = 0; l < c.num_layers; l++) {
         k_rmsnorm<<<B, 256, 0, s>>>(m->normed, m->hidden, m->norm1[l], d);
         IQ_CHECK_LAUNCH();
         if ((rc = proj(m->qkv, m->wqkv[l], m->pqkv[l], m->normed, m->qkv_rows, d, 0))) return rc;
         k_rope_kv<<<dim3((pairs + 255) / 256, B), 256, 0, s>>>(m->qkv, m->kc[l], m->vc[l], m->rcos, m->rsin,
-                                                               m->d_pos, c.num_heads, c.num_kv_heads, hd,
-                                                               c.max_seq_len);
+                                                               m->d_pos, S.nh_l, S.nkv_l, hd, c.max_seq_len);
         IQ_CHECK_LAUNCH();
-        k_attention<<<dim3(c.num_heads, B), 256, m->attn_smem, s>>>(m->att, m->qkv, m->kc[l], m->vc[l], m->d_pos,
-                                                                    c.num_heads, c.num_kv_heads, hd,
-                                                                    c.max_seq_len);
+        k_attention<<<dim3(S.nh_l, B), 256, m->attn_smem, s>>>(att_out, m->qkv, m->kc[l], m->vc[l], m->d_pos,
+                                                               S.nh_l, S.nkv_l, hd, c.max_seq_len);
         IQ_CHECK_LAUNCH();
-        if ((rc = proj(m->hidden, m->wo[l], m->po[l], m->att, d, d, 1))) return rc;
+        if (tp) {
+            if ((rc = gather_rows(m, m->att_l, m->att, B, S.nh_l * hd))) return rc;
+            if ((rc = proj(m->proj_l, m->wo[l], m->po[l], m->att, S.d_l, d, 0))) return rc;
+            if ((rc = gather_rows(m, m->proj_l, m->proj_full, B, S.d_l))) return rc;
+            if ((rc = add_into(m, m->hidden, m->proj_full, (int64_t)B * d))) return rc;
+        } else if ((rc = proj(m->hidden, m->wo[l], m->po[l], m->att, d, d, 1))) {
+            return rc;
+        }
         k_rmsnorm<<<B, 256, 0, s>>>(m->normed, m->hidden, m->norm2[l], d);
         IQ_CHECK_LAUNCH();
-        if ((rc = proj(m->gu, m->wgu[l], m->pgu[l], m->normed, 2 * inter, d, 0))) return rc;
-        k_swiglu<<<(B * inter + 255) / 256, 256, 0, s>>>(m->act, m->gu, inter, B);
+        if ((rc = proj(m->gu, m->wgu[l], m->pgu[l], m->normed, 2 * S.it_l, d, 0))) return rc;
+        k_swiglu<<<(B * S.it_l + 255) / 256, 256, 0, s>>>(act_out, m->gu, S.it_l, B);
         IQ_CHECK_LAUNCH();
-        if ((rc = proj(m->hidden, m->wdown[l], m->pdown[l], m->act, d, inter, 1))) return rc;
+        if (tp) {
+            if ((rc = gather_rows(m, m->act_l, m->act, B, S.it_l))) return rc;
+            if ((rc = proj(m->proj_l, m->wdown[l], m->pdown[l], m->act, S.d_l, c.intermediate_dim, 0))) return rc;
+            if ((rc = gather_rows(m, m->proj_l, m->proj_full, B, S.d_l))) return rc;
+            if ((rc = add_into(m, m->hidden, m->proj_full, (int64_t)B * d))) return rc;
+        } else if ((rc = proj(m->hidden, m->wdown[l], m->pdown[l], m->act, d, c.intermediate_dim, 1))) {
+            return rc;
+        }
     }
     k_rmsnorm<<<B, 256, 0, s>>>(m->normed, m->hidden, m->fnorm, d);
     IQ_CHECK_LAUNCH();
-    if ((rc = proj(m->logits, m->lm, m->plm, m->normed, c.vocab_size, d, 0))) return rc;
+    if (tp) {
+        if ((rc = proj(m->logits_l, m->lm, m->plm, m->normed, S.v_l, d, 0))) return rc;
+        if ((rc = gather_rows(m, m->logits_l, m->logits, B, S.v_l))) return rc;
+    } else if ((rc = proj(m->logits, m->lm, m->plm, m->normed, c.vocab_size, d, 0))) {
+        return rc;
+    }
     k_argmax<<<B, 1024, 0, s>>>(m->d_arg, m->logits, c.vocab_size, m->d_tok, m->d_pos, m->d_hist,
                                 c.max_seq_len + 1);
     IQ_CHECK_LAUNCH();
@@ -197,11 +304,6 @@ static int h2d(void *dst, const void *src, size_t bytes) {
     return IQ_OK;
 }
 
-static int fill_const(int64_t *dst, int64_t v, size_t n) {
-    std::vector<int64_t> h(n, v);
-    return h2d(dst, h.data(), n * 8);
-}
-
 static int repack(iq_model *m, Packed *P, const int64_t *W, int M, int N) {
     if (P->planes) { IQ_CUDA(cudaStreamSynchronize(m->s)); free_packed(P); }
     int rc = pack_weights(W, M, N, m->s, P);
@@ -211,17 +313,86 @@ static int repack(iq_model *m, Packed *P, const int64_t *W, int M, int N) {
 }
 static int repack_layer(iq_model *m, int l) {
     const iq_config &c = m->c;
-    int rc, d = c.hidden_dim, it = c.intermediate_dim;
+    const Shard &S = m->sh;
+    int rc, d = c.hidden_dim;
     if ((rc = repack(m, &m->pqkv[l], m->wqkv[l], m->qkv_rows, d))) return rc;
-    if ((rc = repack(m, &m->po[l], m->wo[l], d, d))) return rc;
-    if ((rc = repack(m, &m->pgu[l], m->wgu[l], 2 * it, d))) return rc;
-    return repack(m, &m->pdown[l], m->wdown[l], d, it);
+    if ((rc = repack(m, &m->po[l], m->wo[l], S.d_l, d))) return rc;
+    if ((rc = repack(m, &m->pgu[l], m->wgu[l], 2 * S.it_l, d))) return rc;
+    return repack(m, &m->pdown[l], m->wdown[l], S.d_l, c.intermediate_dim);
+}
+
+// Where each full host tensor's rows land on this rank: (first row, row count,
+// device destination) pieces; the tensor has `cols` columns.
+struct Piece { size_t row0, nrows; int64_t *dst; };
+struct TensorPlan { std::string name; size_t rows, cols; bool ones; std::vector<Piece> pieces; };
+
+static std::vector<TensorPlan> tensor_plan(iq_model *m) {
+    const iq_config &c = m->c;
+    const Shard &S = m->sh;
+    const size_t d = c.hidden_dim, hd = c.head_dim, kvd = (size_t)c.num_kv_heads * hd, it = c.intermediate_dim,
+                 V = c.vocab_size;
+    std::vector<TensorPlan> t;
+    t.push_back({"model.embed_tokens.weight", V, d, false, {{0, V, m->embed}}});
+    t.push_back({"lm_head.weight", V, d, false, {{(size_t)S.r * S.v_l, (size_t)S.v_l, m->lm}}});
+    t.push_back({"model.norm.weight", 1, d, true, {{0, 1, m->fnorm}}});
+    char nm[160];
+    for (int l = 0; l < c.num_layers; l++) {
+        auto name = [&](const char *x) { snprintf(nm, sizeof nm, "model.layers.%d.%s.weight", l, x); return std::string(nm); };
+        const size_t qr = (size_t)S.nh_l * hd, kr = (size_t)S.nkv_l * hd;
+        int64_t *q = m->wqkv[l], *k = q + qr * d, *v = k + kr * d;
+        t.push_back({name("input_layernorm"), 1, d, true, {{0, 1, m->norm1[l]}}});
+        t.push_back({name("self_attn.q_proj"), d, d, false, {{(size_t)S.q_lo * hd, qr, q}}});
+        t.push_back({name("self_attn.k_proj"), kvd, d, false, {{(size_t)S.kv_lo * hd, kr, k}}});
+        t.push_back({name("self_attn.v_proj"), kvd, d, false, {{(size_t)S.kv_lo * hd, kr, v}}});
+        t.push_back({name("self_attn.o_proj"), d, d, false, {{(size_t)S.r * S.d_l, (size_t)S.d_l, m->wo[l]}}});
+        t.push_back({name("post_attention_layernorm"), 1, d, true, {{0, 1, m->norm2[l]}}});
+        t.push_back({name("mlp.gate_proj"), it, d, false, {{(size_t)S.r * S.it_l, (size_t)S.it_l, m->wgu[l]}}});
+        t.push_back({name("mlp.up_proj"), it, d, false,
+                     {{(size_t)S.r * S.it_l, (size_t)S.it_l, m->wgu[l] + (size_t)S.it_l * d}}});
+        t.push_back({name("mlp.down_proj"), d, it, false, {{(size_t)S.r * S.d_l, (size_t)S.d_l, m->wdown[l]}}});
+    }
+    return t;
+}
+
+static int upload_pieces(const TensorPlan &tp, const int64_t *full) {
+    for (const Piece &p : tp.pieces) {
+        int rc = h2d(p.dst, full + p.row0 * tp.cols, p.nrows * tp.cols * 8);
+        if (rc) return rc;
+    }
+    return IQ_OK;
+}
+
+static int repack_all(iq_model *m) {
+    int rc;
+    if ((rc = repack(m, &m->plm, m->lm, m->sh.v_l, m->c.hidden_dim))) return rc;
+    for (int l = 0; l < m->c.num_layers; l++)
+        if ((rc = repack_layer(m, l))) return rc;
+    return IQ_OK;
 }
 
 extern "C" {
 
-IQ_API int iq_model_create(const iq_config *cfg, int max_batch, int device, iq_model **out) {
-    if (!cfg || !out || max_batch < 1) return IQ_ERR_ARG;
+IQ_API int iq_tp_shard_info(const iq_config *cfg, int tp_size, int tp_rank, int info[8]) {
+    if (!cfg || !info) return IQ_ERR_ARG;
+    Shard s;
+    int rc = make_shard(*cfg, tp_size, tp_rank, &s);
+    if (rc) return rc;
+    int v[8] = {s.q_lo, s.nh_l, s.kv_lo, s.nkv_l, s.r * s.d_l, s.d_l, s.r * s.it_l, s.it_l};
+    memcpy(info, v, sizeof v);
+    return IQ_OK;
+}
+
+IQ_API int iq_nccl_unique_id(void *id_out) {
+    if (!id_out) return IQ_ERR_ARG;
+    ncclUniqueId id;
+    IQ_NCCL(ncclGetUniqueId(&id));
+    memcpy(id_out, &id, sizeof(id));
+    return IQ_OK;
+}
+
+IQ_API int iq_model_create_tp(const iq_config *cfg, int max_batch, int device, int tp_rank, int tp_size,
+                              const void *nccl_id, iq_model **out) {
+    if (!cfg || !out || max_batch < 1 || tp_size < 1 || (tp_size > 1 && !nccl_id)) return IQ_ERR_ARG;
     *out = nullptr;
     const iq_config &c = *cfg;
     if (c.hidden_dim <= 0 || c.num_heads <= 0 || c.num_kv_heads <= 0 || c.head_dim <= 1 ||
@@ -229,16 +400,28 @@ IQ_API int iq_model_create(const iq_config *cfg, int max_batch, int device, iq_m
         c.num_heads % c.num_kv_heads != 0 || c.hidden_dim != c.num_heads * c.head_dim ||
         (c.head_dim & 1) || c.head_dim > 256)
         return IQ_ERR_ARG;
-    IQ_CUDA(cudaSetDevice(device));
-    int rc = ensure_device_pub(device);
+    Shard sh;
+    int rc = make_shard(c, tp_size, tp_rank, &sh);
     if (rc) return rc;
+    IQ_CUDA(cudaSetDevice(device));
+    if ((rc = ensure_device_pub(device))) return rc;
     iq_model *m = new iq_model();
     m->c = c;
+    m->sh = sh;
     m->dev = device;
     m->max_batch = max_batch;
     cudaError_t e = cudaStreamCreateWithFlags(&m->s, cudaStreamNonBlocking);
     if (e != cudaSuccess) { delete m; return cuda_fail(e); }
     if ((rc = model_alloc(m))) { iq_model_destroy(m); return rc; }
+    if (tp_size > 1) {
+        ncclUniqueId id;
+        memcpy(&id, nccl_id, sizeof(id));
+        if (ncclCommInitRank(&m->comm, tp_size, id, tp_rank) != ncclSuccess) {
+            m->comm = nullptr;
+            iq_model_destroy(m);
+            return IQ_ERR_NCCL;
+        }
+    }
     if (m->attn_smem > 200 * 1024) { iq_model_destroy(m); return IQ_ERR_UNSUPPORTED; }
     if (m->attn_smem > 48 * 1024) {
         e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->attn_smem);
@@ -252,20 +435,25 @@ IQ_API int iq_model_create(const iq_config *cfg, int max_batch, int device, iq_m
     return IQ_OK;
 }
 
+IQ_API int iq_model_create(const iq_config *cfg, int max_batch, int device, iq_model **out) {
+    return iq_model_create_tp(cfg, max_batch, device, 0, 1, nullptr, out);
+}
+
 IQ_API int iq_model_destroy(iq_model *m) {
     if (!m) return IQ_ERR_ARG;
     cudaSetDevice(m->dev);
     if (m->s) cudaStreamSynchronize(m->s);
     if (m->graph) cudaGraphExecDestroy(m->graph);
+    if (m->comm) ncclCommDestroy(m->comm);
     void *bufs[] = {m->embed, m->fnorm, m->lm, m->rcos, m->rsin, m->hidden, m->normed, m->qkv, m->att,
-                    m->gu, m->act, m->logits, m->d_tok, m->d_pos, m->d_arg, m->d_hist};
+                    m->gu, m->act, m->logits, m->att_l, m->proj_l, m->act_l, m->logits_l, m->gath,
+                    m->proj_full, m->d_tok, m->d_pos, m->d_arg, m->d_hist, m->racc};
     for (void *p : bufs) if (p) cudaFree(p);
     for (auto *v : {&m->norm1, &m->wqkv, &m->wo, &m->norm2, &m->wgu, &m->wdown, &m->kc, &m->vc})
         for (int64_t *p : *v) if (p) cudaFree(p);
     for (auto *v : {&m->pqkv, &m->po, &m->pgu, &m->pdown})
         for (Packed &P : *v) free_packed(&P);
     free_packed(&m->plm);
-    if (m->racc) cudaFree(m->racc);
     if (m->h_pin) cudaFreeHost(m->h_pin);
     if (m->h_logits) cudaFreeHost(m->h_logits);
     if (m->s) cudaStreamDestroy(m->s);
@@ -277,12 +465,12 @@ IQ_API int iq_model_load_globals(iq_model *m, const int64_t *embed, const int64_
                                  const int64_t *lm_head) {
     if (!m || !embed || !final_norm || !lm_head) return IQ_ERR_ARG;
     IQ_CUDA(cudaSetDevice(m->dev));
-    const iq_config &c = m->c;
+    std::vector<TensorPlan> plan = tensor_plan(m);
+    const int64_t *src[3] = {embed, lm_head, final_norm};
     int rc;
-    if ((rc = h2d(m->embed, embed, (size_t)c.vocab_size * c.hidden_dim * 8))) return rc;
-    if ((rc = h2d(m->fnorm, final_norm, (size_t)c.hidden_dim * 8))) return rc;
-    if ((rc = h2d(m->lm, lm_head, (size_t)c.vocab_size * c.hidden_dim * 8))) return rc;
-    if ((rc = repack(m, &m->plm, m->lm, c.vocab_size, c.hidden_dim))) return rc;
+    for (int i = 0; i < 3; i++)
+        if ((rc = upload_pieces(plan[i], src[i]))) return rc;
+    if ((rc = repack(m, &m->plm, m->lm, m->sh.v_l, m->c.hidden_dim))) return rc;
     m->loaded_globals = true;
     return IQ_OK;
 }
@@ -291,17 +479,10 @@ IQ_API int iq_model_load_layer(iq_model *m, int l, const int64_t *const w[9]) {
     if (!m || !w || l < 0 || l >= m->c.num_layers) return IQ_ERR_ARG;
     for (int i = 0; i < 9; i++) if (!w[i]) return IQ_ERR_ARG;
     IQ_CUDA(cudaSetDevice(m->dev));
-    const size_t d = m->c.hidden_dim, kvd = m->kvd, it = m->c.intermediate_dim;
+    std::vector<TensorPlan> plan = tensor_plan(m);
     int rc;
-    if ((rc = h2d(m->norm1[l], w[0], d * 8))) return rc;
-    if ((rc = h2d(m->wqkv[l], w[1], d * d * 8))) return rc;
-    if ((rc = h2d(m->wqkv[l] + d * d, w[2], kvd * d * 8))) return rc;
-    if ((rc = h2d(m->wqkv[l] + (d + kvd) * d, w[3], kvd * d * 8))) return rc;
-    if ((rc = h2d(m->wo[l], w[4], d * d * 8))) return rc;
-    if ((rc = h2d(m->norm2[l], w[5], d * 8))) return rc;
-    if ((rc = h2d(m->wgu[l], w[6], it * d * 8))) return rc;
-    if ((rc = h2d(m->wgu[l] + it * d, w[7], it * d * 8))) return rc;
-    if ((rc = h2d(m->wdown[l], w[8], d * it * 8))) return rc;
+    for (int i = 0; i < 9; i++)
+        if ((rc = upload_pieces(plan[3 + 9 * l + i], w[i]))) return rc;
     if ((rc = repack_layer(m, l))) return rc;
     m->loaded_layer[l] = true;
     return IQ_OK;
@@ -310,7 +491,7 @@ IQ_API int iq_model_load_layer(iq_model *m, int l, const int64_t *const w[9]) {
 IQ_API int iq_model_reset(iq_model *m) {
     if (!m) return IQ_ERR_ARG;
     IQ_CUDA(cudaSetDevice(m->dev));
-    size_t kvb = (size_t)m->max_batch * m->c.max_seq_len * m->kvd * 8;
+    size_t kvb = (size_t)m->max_batch * m->c.max_seq_len * m->kvd_l * 8;
     for (int l = 0; l < m->c.num_layers; l++) {
         IQ_CUDA(cudaMemsetAsync(m->kc[l], 0, kvb, m->s));
         IQ_CUDA(cudaMemsetAsync(m->vc[l], 0, kvb, m->s));
@@ -319,34 +500,9 @@ IQ_API int iq_model_reset(iq_model *m) {
     return IQ_OK;
 }
 
-// ------------------------------------------------------------- synthetic
-
-struct SynthJob { std::string name; int64_t *dst; size_t n; bool ones; };
-
 IQ_API int iq_model_synth(iq_model *m, int config_index, int threads) {
     if (!m) return IQ_ERR_ARG;
-    const iq_config &c = m->c;
-    const size_t d = c.hidden_dim, kvd = m->kvd, it = c.intermediate_dim, V = c.vocab_size;
-    std::vector<SynthJob> jobs;
-    jobs.push_back({"model.embed_tokens.weight", m->embed, V * d, false});
-    jobs.push_back({"lm_head.weight", m->lm, V * d, false});
-    jobs.push_back({"model.norm.weight", m->fnorm, d, true});
-    char nm[160];
-    for (int l = 0; l < c.num_layers; l++) {
-        auto add = [&](const char *t, int64_t *dst, size_t n, bool ones) {
-            snprintf(nm, sizeof nm, "model.layers.%d.%s.weight", l, t);
-            jobs.push_back({nm, dst, n, ones});
-        };
-        add("input_layernorm", m->norm1[l], d, true);
-        add("self_attn.q_proj", m->wqkv[l], d * d, false);
-        add("self_attn.k_proj", m->wqkv[l] + d * d, kvd * d, false);
-        add("self_attn.v_proj", m->wqkv[l] + (d + kvd) * d, kvd * d, false);
-        add("self_attn.o_proj", m->wo[l], d * d, false);
-        add("post_attention_layernorm", m->norm2[l], d, true);
-        add("mlp.gate_proj", m->wgu[l], it * d, false);
-        add("mlp.up_proj", m->wgu[l] + it * d, it * d, false);
-        add("mlp.down_proj", m->wdown[l], d * it, false);
-    }
+    std::vector<TensorPlan> plan = tensor_plan(m);
     if (threads < 1) threads = 1;
     std::atomic<size_t> next(0);
     std::atomic<int> status(IQ_OK);
@@ -355,29 +511,27 @@ IQ_API int iq_model_synth(iq_model *m, int config_index, int threads) {
         std::vector<int64_t> buf;
         for (;;) {
             size_t j = next.fetch_add(1);
-            if (j >= jobs.size() || status.load() != IQ_OK) return;
-            const SynthJob &jb = jobs[j];
-            buf.resize(jb.n);
-            if (jb.ones) std::fill(buf.begin(), buf.end(), IQ_ONE);
-            else iq_synth_weights(iq_tensor_seed(config_index, jb.name.c_str()), buf.data(), (int64_t)jb.n);
-            cudaError_t e = cudaMemcpy(jb.dst, buf.data(), jb.n * 8, cudaMemcpyHostToDevice);
-            if (e != cudaSuccess) status.store(cuda_fail(e));
+            if (j >= plan.size() || status.load() != IQ_OK) return;
+            const TensorPlan &tp = plan[j];
+            size_t n = tp.rows * tp.cols;
+            buf.resize(n);
+            if (tp.ones) std::fill(buf.begin(), buf.end(), IQ_ONE);
+            else iq_synth_weights(iq_tensor_seed(config_index, tp.name.c_str()), buf.data(), (int64_t)n);
+            int rc = upload_pieces(tp, buf.data());
+            if (rc) status.store(rc);
         }
     };
     std::vector<std::thread> pool;
     for (int t = 0; t < threads; t++) pool.emplace_back(worker);
     for (auto &t : pool) t.join();
     if (status.load() != IQ_OK) return status.load();
-    int rc;
     IQ_CUDA(cudaSetDevice(m->dev));
-    if ((rc = repack(m, &m->plm, m->lm, c.vocab_size, c.hidden_dim))) return rc;
-    for (int l = 0; l < c.num_layers; l++)
-        if ((rc = repack_layer(m, l))) return rc;
+    int rc = repack_all(m);
+    if (rc) return rc;
     m->loaded_globals = true;
-    m->loaded_layer.assign(c.num_layers, true);
+    m->loaded_layer.assign(m->c.num_layers, true);
     return IQ_OK;
 }
-
 // ------------------------------------------------------------- forward
 
 static int set_tok_pos(iq_model *m, const int *tok, const int *pos, int B, int slot) {

@@ -42,6 +42,9 @@ SIGNATURES = {
     "iq_rmsnorm_dev": (_I, [_P, _P, _P, _I, _I, _P]),
     "iq_softmax_dev": (_I, [_P, _I, _I, _P]),
     "iq_model_create": (_I, [_P, _I, _I, _P]),
+    "iq_nccl_unique_id": (_I, [_P]),
+    "iq_tp_shard_info": (_I, [_P, _I, _I, _P]),
+    "iq_model_create_tp": (_I, [_P, _I, _I, _I, _I, _P, _P]),
     "iq_model_destroy": (_I, [_P]),
     "iq_model_load_globals": (_I, [_P, _P, _P, _P]),
     "iq_model_load_layer": (_I, [_P, _I, _P]),
@@ -139,6 +142,22 @@ def weight_cache_clear():
     _call("iq_weight_cache_clear")
 
 
+def nccl_unique_id():
+    """128-byte NCCL id for iq_model_create_tp (made on one rank, shared with all)."""
+    buf = ctypes.create_string_buffer(128)
+    _call("iq_nccl_unique_id", buf)
+    return buf.raw
+
+
+def tp_shard_info(cfg, tp_size, tp_rank):
+    """Row ownership of a tensor-parallel rank (see iq_tp_shard_info)."""
+    c = cfg if isinstance(cfg, Config) else Config.from_dict(cfg)
+    info = (ctypes.c_int * 8)()
+    _call("iq_tp_shard_info", ctypes.byref(c), tp_size, tp_rank, info)
+    keys = ("q_lo", "nh", "kv_lo", "nkv", "d_lo", "d_n", "it_lo", "it_n")
+    return dict(zip(keys, list(info)))
+
+
 def set_device(d):
     _call("iq_set_device", d)
 
@@ -228,11 +247,16 @@ class Model:
     """Device-resident integer Llama (iq_model_*): forward / generate with the
     reference's semantics (llama_forward, generate in llama_int.c)."""
 
-    def __init__(self, cfg, max_batch=1, device=0):
+    def __init__(self, cfg, max_batch=1, device=0, tp_rank=0, tp_size=1, nccl_id=None):
         self.cfg = cfg if isinstance(cfg, Config) else Config.from_dict(cfg)
         self.max_batch = max_batch
         self.h = ctypes.c_void_p()
-        _call("iq_model_create", ctypes.byref(self.cfg), max_batch, device, ctypes.byref(self.h))
+        if tp_size == 1:
+            _call("iq_model_create", ctypes.byref(self.cfg), max_batch, device, ctypes.byref(self.h))
+        else:
+            idbuf = ctypes.create_string_buffer(bytes(nccl_id), 128)
+            _call("iq_model_create_tp", ctypes.byref(self.cfg), max_batch, device, tp_rank, tp_size,
+                  idbuf, ctypes.byref(self.h))
 
     def close(self):
         if self.h:

@@ -1,0 +1,73 @@
+"""Tensor-parallel model on 2 GPUs (one process per GPU, NCCL): tokens and the
+hash of every logit equal the single-GPU reference goldens, and batched decode
+equals the unsharded model. Skipped when fewer than 2 GPUs are visible."""
+import json
+import os
+
+import numpy as np
+import pytest
+
+import configs
+import helpers
+import iq
+import oracle as orc
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _rank(rank, world, ids, q):
+    import torch
+    torch.cuda.set_device(rank)
+    try:
+        g = json.load(open(os.path.join(GOLD, "tiny_model.json")))
+        c = g["config"]
+        w = helpers.model_weights(g["cfg_index"], c)
+        m = iq.Model(c, device=rank, tp_rank=rank, tp_size=world, nccl_id=ids[0])
+        m.load(w)
+        toks, lh = m.generate(np.array(g["prompt"]), g["max_new"], logit_hash=True)
+        toks2, _ = m.generate(np.array(g["prompt"]), g["max_new"])   # graph replays, no host sync
+        a, lg = m.forward(int(g["prompt"][0]), 0)
+        ok = toks == g["tokens"] and lh == g["logit_hash"] and toks2 == g["tokens"]
+        ok = ok and orc.fnv_hash(lg) == g["step_logit_hashes"][0]
+        m.close()
+        # batched decode (B = 3): every sequence equals the unsharded model's
+        cb = dict(c, max_seq=48)
+        mb = iq.Model(cb, max_batch=3, device=rank, tp_rank=rank, tp_size=world, nccl_id=ids[1])
+        mb.load(w)
+        prompts = np.stack([orc.synth_tokens(9, f"prompt:tp{b}", 6, c["vocab"]) for b in range(3)])
+        got = mb.generate_batch(prompts, 20)
+        mb.close()
+        m1 = iq.Model(cb, device=rank)
+        m1.load(w)
+        for b in range(3):
+            want, _ = m1.generate(prompts[b], 20)
+            ok = ok and got[b] == want
+        m1.close()
+        q.put((rank, bool(ok), None))
+    except Exception as e:  # report to the parent instead of hanging it
+        q.put((rank, False, repr(e)))
+
+
+def test_tp2_generate_matches_goldens():
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ids = [iq.nccl_unique_id(), iq.nccl_unique_id()]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, 2, ids, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in procs:
+            r, ok, err = q.get(timeout=600)
+            res[r] = (ok, err)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    assert res == {0: (True, None), 1: (True, None)}, res
