@@ -110,6 +110,20 @@ IQ_API int iq_matvec_packed_dev(int64_t *d_out, const iq_packed *w, const int64_
 IQ_API int iq_matvec_packed_noalloc_dev(int64_t *d_out, const iq_packed *w, const int64_t *d_in,
                                         void *stream);
 
+/* Weights packed for the tcgen05 tensor-core GEMM (byte planes, row-major
+ * per plane, plus a TMA descriptor); N (the reduction length) <= 32768.
+ * iq_gemm_tc_dev: d_out[r][i] = matmul_vec(d_w, d_X[r])[i] for r < rows, the
+ * same values as `rows` calls of llama_int.c:1014, on the int8 tensor cores.
+ * No reference counterpart (the reference has no batched form). */
+typedef struct iq_packed_tc iq_packed_tc;
+IQ_API int iq_pack_weights_tc_dev(const int64_t *d_w, int M, int N, void *stream, iq_packed_tc **out);
+IQ_API int iq_packed_tc_free(iq_packed_tc *p);
+IQ_API int iq_gemm_tc_dev(int64_t *d_out, const iq_packed_tc *w, const int64_t *d_X, int rows, void *stream);
+
+/* Synchronises the current device and returns (and clears) the status that
+ * kernels with bounded waits record: IQ_OK or IQ_ERR_TIMEOUT. */
+IQ_API int iq_device_status(void);
+
 /* Batched rows: d_out[r][i] = matmul_vec(d_w, d_X[r])[i] for r < rows, i.e.
  * exactly `rows` independent calls of llama_int.c:1014 (the reference has no
  * batched form; its prefill loops M=1 calls, llama_int.c:3081-3092).

@@ -11,6 +11,7 @@
 #include "iq_matvec.cuh"
 #include "iq_gemm.cuh"
 #include "iq_planes.cuh"
+#include "iq_tc_gemm.cuh"
 #include "iq_elem.cuh"
 
 namespace iq {
@@ -210,6 +211,122 @@ int stream_scratch(cudaStream_t s, size_t rows, RowAcc **out) {
     }
     *out = b.p;
     return IQ_OK;
+}
+
+// ------------------------------------------------ tcgen05 GEMM (rows >= 2)
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                                    CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                    CUtensorMapFloatOOBfill);
+static PFN_encodeTiled g_encode = nullptr;
+
+static int get_encoder() {
+    if (g_encode) return IQ_OK;
+    cudaDriverEntryPointQueryResult q;
+    void *fn = nullptr;
+    IQ_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || !fn) return IQ_ERR_UNSUPPORTED;
+    g_encode = (PFN_encodeTiled)fn;
+    return IQ_OK;
+}
+
+// 2-D map over a [rows][cols] byte matrix, box {128 bytes, box_rows}, 128-byte swizzle
+static int encode_u8_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    int rc = get_encoder();
+    if (rc) return rc;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols};
+    cuuint32_t box[2] = {128, box_rows};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? IQ_OK : IQ_ERR_CUDA;
+}
+
+struct PackedTC {
+    int M = 0, K = 0, Mpad = 0, Kpad = 0;
+    uint8_t *planes = nullptr;   // [8][Mpad][Kpad]
+    int64_t *rowsum = nullptr;   // [Mpad][2]
+    CUtensorMap mapA;
+};
+
+static void free_packed_tc(PackedTC *P) {
+    if (P->planes) cudaFree(P->planes);
+    if (P->rowsum) cudaFree(P->rowsum);
+    P->planes = nullptr;
+    P->rowsum = nullptr;
+}
+
+static int pack_weights_tc(const int64_t *d_w, int M, int K, cudaStream_t s, PackedTC *P) {
+    if (K > 32768) return IQ_ERR_UNSUPPORTED;  // int32 partials exact up to 33025 terms
+    P->M = M; P->K = K;
+    P->Mpad = (M + TC_BM - 1) / TC_BM * TC_BM;
+    P->Kpad = (K + TC_BK - 1) / TC_BK * TC_BK;
+    size_t n = (size_t)P->Mpad * P->Kpad;
+    IQ_CUDA(cudaMalloc(&P->planes, 8 * n));
+    cudaError_t e = cudaMalloc(&P->rowsum, (size_t)P->Mpad * 16);
+    if (e != cudaSuccess) { free_packed_tc(P); return cuda_fail(e); }
+    k_pack_rowplanes<<<(int)std::min<size_t>((n + 255) / 256, (size_t)dev_info().sms * 64), 256, 0, s>>>(
+        P->planes, d_w, M, K, P->Mpad, P->Kpad);
+    IQ_CHECK_LAUNCH();
+    k_row_sums<<<std::min(P->Mpad / 8 + 1, dev_info().sms * 16), 256, 0, s>>>(P->rowsum, d_w, M, K, P->Mpad);
+    IQ_CHECK_LAUNCH();
+    int rc = encode_u8_map(&P->mapA, P->planes, (uint64_t)8 * P->Mpad, (uint64_t)P->Kpad, TC_BM);
+    if (rc) { free_packed_tc(P); return rc; }
+    return IQ_OK;
+}
+
+// Byte scratch per (device, stream) for the digit matrix, grown outside capture.
+struct ByteScratch { uint8_t *p = nullptr; size_t cap = 0; };
+static std::mutex g_bs_mu;
+static std::unordered_map<ScratchKey, ByteScratch, ScratchHash> g_bs;
+
+static int stream_bytes(cudaStream_t s, size_t bytes, uint8_t **out) {
+    int dev = 0;
+    IQ_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(g_bs_mu);
+    ByteScratch &b = g_bs[ScratchKey{dev, s}];
+    if (b.cap < bytes) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        IQ_CUDA(cudaStreamIsCapturing(s, &cs));
+        if (cs != cudaStreamCaptureStatusNone) return IQ_ERR_STATE;
+        if (b.p) { IQ_CUDA(cudaStreamSynchronize(s)); cudaFree(b.p); b.p = nullptr; b.cap = 0; }
+        IQ_CUDA(cudaMalloc(&b.p, bytes));
+        b.cap = bytes;
+    }
+    *out = b.p;
+    return IQ_OK;
+}
+
+// out[r][i] (+)= rows of matmul_vec for X [R][K]; digits: >= Rpad*8*Kpad bytes scratch
+int launch_gemm_tc(int64_t *out, const PackedTC &P, const int64_t *X, int R, cudaStream_t s, int add,
+                   uint8_t *digits) {
+    const int Rpad = (R + TC_BR - 1) / TC_BR * TC_BR;
+    int64_t n = (int64_t)Rpad * P.Kpad;
+    k_x_digits<<<(int)std::min<int64_t>((n + 255) / 256, (int64_t)dev_info().sms * 64), 256, 0, s>>>(
+        digits, X, R, P.K, Rpad, P.Kpad);
+    IQ_CHECK_LAUNCH();
+    CUtensorMap mapB;
+    int rc = encode_u8_map(&mapB, digits, (uint64_t)Rpad * 8, (uint64_t)P.Kpad, TC_BR * 8);
+    if (rc) return rc;
+    IQ_CUDA(cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
+    dim3 grid(P.Mpad / TC_BM, Rpad / TC_BR);
+    k_gemm_tc<<<grid, 192, TC_SMEM, s>>>(P.mapA, mapB, out, P.rowsum, P.M, R, P.Mpad, P.Kpad, add);
+    IQ_CHECK_LAUNCH();
+    return IQ_OK;
+}
+
+// Reads and clears the device status word after a synchronisation point.
+int take_dev_error() {
+    int v = 0;
+    IQ_CUDA(cudaMemcpyFromSymbol(&v, g_iq_err, sizeof(int)));
+    if (v) {
+        int z = 0;
+        IQ_CUDA(cudaMemcpyToSymbol(g_iq_err, &z, sizeof(int)));
+    }
+    return v;
 }
 
 // ------------------------------------------------------- weight cache
@@ -432,6 +549,47 @@ IQ_API int iq_matvec_packed_dev(int64_t *d_out, const iq_packed *w, const int64_
     RowAcc *racc = nullptr;
     if ((rc = stream_scratch(s, (size_t)w->P.Mp, &racc))) return rc;
     return launch_matvec_planes(d_out, w->P, d_in, s, 0, racc);
+}
+
+struct iq_packed_tc { PackedTC P; int dev; };
+
+IQ_API int iq_pack_weights_tc_dev(const int64_t *d_w, int M, int N, void *stream, iq_packed_tc **out) {
+    if (!d_w || !out || M <= 0 || N <= 0) return IQ_ERR_ARG;
+    *out = nullptr;
+    int dev, rc;
+    if ((rc = cur_device(&dev))) return rc;
+    iq_packed_tc *p = new iq_packed_tc();
+    p->dev = dev;
+    if ((rc = pack_weights_tc(d_w, M, N, pick(stream), &p->P))) { delete p; return rc; }
+    *out = p;
+    return IQ_OK;
+}
+
+IQ_API int iq_packed_tc_free(iq_packed_tc *p) {
+    if (!p) return IQ_ERR_ARG;
+    cudaDeviceSynchronize();
+    free_packed_tc(&p->P);
+    delete p;
+    return IQ_OK;
+}
+
+IQ_API int iq_gemm_tc_dev(int64_t *d_out, const iq_packed_tc *w, const int64_t *d_X, int rows, void *stream) {
+    if (!d_out || !w || !d_X || rows <= 0 || (const void *)d_out == (const void *)d_X) return IQ_ERR_ARG;
+    int dev, rc;
+    if ((rc = cur_device(&dev))) return rc;
+    if (dev != w->dev) return IQ_ERR_ARG;
+    cudaStream_t s = pick(stream);
+    const size_t Rpad = (size_t)(rows + TC_BR - 1) / TC_BR * TC_BR;
+    uint8_t *dg = nullptr;
+    if ((rc = stream_bytes(s, Rpad * 8 * (size_t)w->P.Kpad, &dg))) return rc;
+    return launch_gemm_tc(d_out, w->P, d_X, rows, s, 0, dg);
+}
+
+IQ_API int iq_device_status(void) {
+    int dev, rc;
+    if ((rc = cur_device(&dev))) return rc;
+    IQ_CUDA(cudaDeviceSynchronize());
+    return take_dev_error();
 }
 
 }  // extern "C"

@@ -1,0 +1,177 @@
+// iq_tc_gemm.cuh -- exact Q16.48 GEMM (rows of matmul_vec) on the 5th-gen
+// tensor cores: tcgen05.mma kind::i8, operands staged by TMA, accumulators in
+// TMEM.
+//
+// Same byte-plane identity as iq_planes.cuh: with W's bytes B_p (B_7 signed)
+// and the unsigned digits D_j of x_u = x + 2^63,
+//   out[r][i] = low64( (sum_{p,j} 2^{8(p+j)} P_pj[r][i] - 2^63 sum_k W[i][k]) >> 48 )
+//   P_pj[r][i] = sum_k B_p(W[i][k]) * D_j(x_u[r][k])       (exact int32)
+// For plane p the products for all digits are one GEMM: A = plane p of W
+// ([Mpad][Kpad] bytes, K-major) times B = the digit matrix
+// ([(row, digit)][Kpad] bytes, K-major, row = 8*r + j), so the MMA's N
+// columns are (x-row, digit) pairs: N = 256 covers 32 x-rows.
+//
+// CTA tile: 128 output rows of W x 32 rows of X. Warp roles (192 threads):
+//   warp 0      TMA producer: for each plane p and 128-byte K block, loads A
+//               (128 x 128 B) and B (256 x 128 B) into a 4-stage ring;
+//   warp 1      owns TMEM (512 columns) and issues the MMAs from one thread:
+//               4 x (M=128, N=256, K=32) per stage into accumulator buffer p&1,
+//               committing each stage's smem back to the producer and each
+//               finished plane to the epilogue;
+//   warps 2..5  epilogue: per plane, read the 128 x 256 int32 tile from TMEM
+//               (warp w reads lanes 32*(w%4)..+31) and fold it into 32
+//               128-bit sums per thread (thread = one W row, 32 x-rows), then
+//               release the buffer; finally subtract 2^63*rowsum and store.
+// K per plane pass <= 32768 keeps every int32 partial exact (|u8*u8| <= 65025).
+#pragma once
+#include "iq_sync.cuh"
+#include "iq_planes.cuh"
+
+namespace iq {
+
+constexpr int TC_BM = 128, TC_BR = 32, TC_BK = 128, TC_STAGES = 4;
+constexpr int TC_A_BYTES = TC_BM * TC_BK;            // 16 KB
+constexpr int TC_B_BYTES = TC_BR * 8 * TC_BK;        // 32 KB
+constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
+constexpr size_t TC_SMEM = 1024 + (size_t)TC_STAGES * TC_STAGE_BYTES + 256;
+
+// W [M][K] int64 -> planes [8][Mpad][Kpad] bytes (zero padded)
+__global__ void k_pack_rowplanes(uint8_t *__restrict__ out, const int64_t *__restrict__ W, int M, int K,
+                                 int Mpad, int Kpad) {
+    const int64_t n = (int64_t)Mpad * Kpad;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        int m = (int)(e / Kpad), k = (int)(e % Kpad);
+        uint64_t w = (m < M && k < K) ? (uint64_t)W[(size_t)m * K + k] : 0ull;
+#pragma unroll
+        for (int p = 0; p < 8; p++) out[(size_t)p * n + e] = (uint8_t)(w >> (8 * p));
+    }
+}
+
+// X [R][K] int64 -> digits [Rpad*8][Kpad] bytes, row 8r+j = byte j of (x ^ 2^63)
+__global__ void k_x_digits(uint8_t *__restrict__ out, const int64_t *__restrict__ X, int R, int K, int Rpad,
+                           int Kpad) {
+    const int64_t n = (int64_t)Rpad * Kpad;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        int r = (int)(e / Kpad), k = (int)(e % Kpad);
+        uint64_t xu = (r < R && k < K) ? ((uint64_t)X[(size_t)r * K + k] ^ 0x8000000000000000ull) : 0ull;
+#pragma unroll
+        for (int j = 0; j < 8; j++) out[((size_t)r * 8 + j) * Kpad + k] = (uint8_t)(xu >> (8 * j));
+    }
+}
+
+__global__ void __launch_bounds__(192, 1)
+k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
+          int64_t *__restrict__ out, const int64_t *__restrict__ rowsum, int M, int R, int Mpad, int Kpad,
+          int add) {
+    extern __shared__ unsigned char smraw[];
+    unsigned char *sm = smraw + ((1024 - (smem_u32(smraw) & 1023)) & 1023);  // 1024-aligned stages
+    unsigned char *stage = sm;
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + TC_STAGES * TC_STAGE_BYTES);
+    uint64_t *empty = full + TC_STAGES;
+    uint64_t *afull = empty + TC_STAGES;   // [2]
+    uint64_t *aempty = afull + 2;          // [2]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(aempty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * TC_BM, r0 = blockIdx.y * TC_BR;
+    const int KB = Kpad / TC_BK;
+    const int total = 8 * KB;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < TC_STAGES; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int b = 0; b < 2; b++) { mbar_init(&afull[b], 1); mbar_init(&aempty[b], 4); }
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int it = 0;
+            for (; it < total; it++) {
+                const int p = it / KB, kb = it % KB, s = it % TC_STAGES;
+                if (it >= TC_STAGES && !mbar_wait(&empty[s], (uint32_t)((it / TC_STAGES) - 1) & 1u)) break;
+                mbar_expect_tx(&full[s], TC_STAGE_BYTES);
+                unsigned char *a = stage + (size_t)s * TC_STAGE_BYTES;
+                tma_load_2d(a, &mapA, kb * TC_BK, p * Mpad + m0, &full[s]);
+                tma_load_2d(a + TC_A_BYTES, &mapB, kb * TC_BK, r0 * 8, &full[s]);
+            }
+            // drain: the last copies into each stage have landed before the CTA can exit
+            for (int j = (it > TC_STAGES ? it - TC_STAGES : 0); j < it; j++)
+                mbar_wait(&full[j % TC_STAGES], (uint32_t)(j / TC_STAGES) & 1u);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            bool ok = true;
+            for (int p = 0; p < 8 && ok; p++) {
+                const int buf = p & 1;
+                if (p >= 2 && !mbar_wait(&aempty[buf], (uint32_t)((p / 2) - 1) & 1u)) break;
+                tc_fence_after();
+                const uint32_t idesc = idesc_i8(p == 7, false, TC_BM, TC_BR * 8);
+                const uint32_t d = tmem + (uint32_t)(buf * 256);
+                for (int kb = 0; kb < KB; kb++) {
+                    const int it = p * KB + kb, s = it % TC_STAGES;
+                    if (!mbar_wait(&full[s], (uint32_t)(it / TC_STAGES) & 1u)) { ok = false; break; }
+                    tc_fence_after();
+                    const unsigned char *a = stage + (size_t)s * TC_STAGE_BYTES;
+                    const uint64_t ad = smem_desc_sw128(a), bd = smem_desc_sw128(a + TC_A_BYTES);
+#pragma unroll
+                    for (int k = 0; k < TC_BK / 32; k++)  // advance 32 bytes of K = 2 descriptor units
+                        tc_mma_i8(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+                    tc_commit(&empty[s]);
+                }
+                if (ok) tc_commit(&afull[buf]);
+            }
+        }
+    } else {
+        // epilogue warps: TMEM lane quadrant = warp % 4
+        const int quad = warp & 3;
+        const int row = m0 + quad * 32 + lane;
+        i128 acc[TC_BR];
+#pragma unroll
+        for (int r = 0; r < TC_BR; r++) acc[r] = 0;
+        bool ok = true;
+        for (int p = 0; p < 8 && ok; p++) {
+            const int buf = p & 1;
+            if (!mbar_wait(&afull[buf], (uint32_t)(p / 2) & 1u)) { ok = false; break; }
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < 8; c++) {  // 32 columns = 4 x-rows x 8 digits
+                uint32_t v[32];
+                tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * 256 + c * 32), v);
+                tmem_ld_wait();
+#pragma unroll
+                for (int rr = 0; rr < 4; rr++)
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        acc[4 * c + rr] += (i128)(int32_t)v[rr * 8 + j] << (8 * (p + j));
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&aempty[buf]);
+        }
+        if (ok && row < M) {
+            const i128 ws = (i128)(((u128)(uint64_t)rowsum[2 * row + 1] << 64) | (uint64_t)rowsum[2 * row]);
+            const u128 bias = (u128)ws << 63;
+#pragma unroll
+            for (int r = 0; r < TC_BR; r++) {
+                if (r0 + r < R) {
+                    int64_t v = (int64_t)((i128)((u128)acc[r] - bias) >> 48);
+                    int64_t *o = out + (size_t)(r0 + r) * M + row;
+                    *o = add ? (int64_t)((uint64_t)*o + (uint64_t)v) : v;  // fused residual add
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+}  // namespace iq

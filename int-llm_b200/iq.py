@@ -38,6 +38,10 @@ SIGNATURES = {
     "iq_packed_free": (_I, [_P]),
     "iq_matvec_packed_dev": (_I, [_P, _P, _P, _P]),
     "iq_matvec_packed_noalloc_dev": (_I, [_P, _P, _P, _P]),
+    "iq_pack_weights_tc_dev": (_I, [_P, _I, _I, _P, _P]),
+    "iq_packed_tc_free": (_I, [_P]),
+    "iq_gemm_tc_dev": (_I, [_P, _P, _P, _I, _P]),
+    "iq_device_status": (_I, []),
     "iq_fp_dev": (_I, [_I, _P, _P, _P, _I64, _P]),
     "iq_rmsnorm_dev": (_I, [_P, _P, _P, _I, _I, _P]),
     "iq_softmax_dev": (_I, [_P, _I, _I, _P]),
@@ -190,6 +194,34 @@ class Packed:
 
 def matvec_packed_dev(out, packed, x, stream=None):
     _call("iq_matvec_packed_dev", _dp(out), packed.h, _dp(x), _sp(stream))
+
+
+class PackedTC:
+    """Weights packed for the tcgen05 GEMM (iq_pack_weights_tc_dev)."""
+
+    def __init__(self, d_w, M, N, stream=None):
+        self.h = ctypes.c_void_p()
+        _call("iq_pack_weights_tc_dev", _dp(d_w), M, N, _sp(stream), ctypes.byref(self.h))
+
+    def free(self):
+        if self.h:
+            _call("iq_packed_tc_free", self.h)
+            self.h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def gemm_tc_dev(out, packed, X, rows, stream=None):
+    _call("iq_gemm_tc_dev", _dp(out), packed.h, _dp(X), rows, _sp(stream))
+
+
+def device_status():
+    """IQ_OK, or the timeout status a kernel's bounded wait recorded (then cleared)."""
+    return lib().iq_device_status()
 
 
 def gemm_dev(out, w, X, rows, M, N, stream=None):

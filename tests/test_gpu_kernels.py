@@ -227,3 +227,28 @@ def test_matvec_packed_vs_oracle(M, N, dist):
         iq.matvec_packed_dev(do, pk, dx)
         assert (host(do) == want).all()
     pk.free()
+
+
+# ------------------------------------------------------------- tcgen05 GEMM
+
+@pytest.mark.parametrize("rows,M,N", [(2, 5, 7), (31, 64, 129), (33, 130, 1000), (64, 256, 2048),
+                                      (100, 300, 5632), (512, 128, 256)])
+@pytest.mark.parametrize("dist", ["full", "cfg"])
+def test_gemm_tc_vs_oracle(rows, M, N, dist):
+    """tcgen05 kind::i8 byte-plane GEMM: exact on full-range int64 and on
+    config-distributed inputs; padding of rows (128), x-rows (32) and K (128)."""
+    import torch
+    rng = np.random.default_rng(rows * 7 + M + N)
+    if dist == "full":
+        w, X = rand_full(rng, (M, N)), rand_full(rng, (rows, N))
+    else:
+        w = orc.synth_weights(2, f"w:{M}x{N}", (M, N))
+        X = orc.synth_acts(2, f"X:{rows}x{N}", (rows, N))
+    want = orc.matmul_rows(w, X)
+    pk = iq.PackedTC(dev(w), M, N)
+    do = torch.zeros((rows, M), dtype=torch.int64, device="cuda")
+    iq.gemm_tc_dev(do, pk, dev(X), rows)
+    got = host(do)
+    assert iq.device_status() == 0
+    assert (got == want).all()
+    pk.free()
