@@ -22,16 +22,18 @@ __global__ void k_embed(int64_t *__restrict__ hidden, const int64_t *__restrict_
 
 // RoPE on all q heads and the k heads (rope_apply, llama_int.c:997-1008), then the
 // exact K/V cache write at pos (llama_int.c:1415-1416). One thread per rotation pair.
+// Row r of qkv belongs to sequence seq_arr[r] at position pos_arr[r].
 __global__ void k_rope_kv(int64_t *__restrict__ qkv, int64_t *__restrict__ kc, int64_t *__restrict__ vc,
                           const int64_t *__restrict__ rcos, const int64_t *__restrict__ rsin,
-                          const int *__restrict__ pos_arr, int nh, int nkv, int hd, int max_seq) {
+                          const int *__restrict__ pos_arr, const int *__restrict__ seq_arr, int nh, int nkv,
+                          int hd, int max_seq) {
     const int b = blockIdx.y;
     const int half = hd / 2, dim = nh * hd, kvd = nkv * hd;
-    const int pos = pos_arr[b];
+    const int pos = pos_arr[b], sq = seq_arr[b];
     int64_t *row = qkv + (size_t)b * (dim + 2 * kvd);
     const int64_t *c = rcos + (size_t)pos * half, *s = rsin + (size_t)pos * half;
-    int64_t *kdst = kc + ((size_t)b * max_seq + pos) * kvd;
-    int64_t *vdst = vc + ((size_t)b * max_seq + pos) * kvd;
+    int64_t *kdst = kc + ((size_t)sq * max_seq + pos) * kvd;
+    int64_t *vdst = vc + ((size_t)sq * max_seq + pos) * kvd;
     const int npairs = (nh + nkv) * half;
     for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < npairs + kvd; p += gridDim.x * blockDim.x) {
         if (p < npairs) {
@@ -65,9 +67,13 @@ __device__ __forceinline__ i128 d_mul128(int64_t a, int64_t b) {
 //   p = softmax(score) (llama_int.c:1060-1072)
 //   out[d] = sum_t fp_mul(p_t, v_t[d])   (int64 sum of floor-shifted terms)
 // Scores live in dynamic shared memory ([T] int64); q_h in shared memory.
+// Row b = (sequence seq_arr[b], position pos_arr[b]) attends to positions
+// 0..pos of its sequence: a batched prefill row computes exactly what the
+// reference's sequential call at that position computes.
 __global__ void k_attention(int64_t *__restrict__ out, const int64_t *__restrict__ qkv,
                             const int64_t *__restrict__ kc, const int64_t *__restrict__ vc,
-                            const int *__restrict__ pos_arr, int nh, int nkv, int hd, int max_seq) {
+                            const int *__restrict__ pos_arr, const int *__restrict__ seq_arr, int nh, int nkv,
+                            int hd, int max_seq) {
     extern __shared__ __align__(16) int64_t sm[];
     __shared__ uint64_t red[64];
     const int h = blockIdx.x, b = blockIdx.y;
@@ -79,8 +85,9 @@ __global__ void k_attention(int64_t *__restrict__ out, const int64_t *__restrict
     for (int d = threadIdx.x; d < hd; d += blockDim.x) qs[d] = q[d];
     __syncthreads();
     const int64_t scale = d_inv_sqrt(d_from_int(hd));
-    const int64_t *kb = kc + (size_t)b * max_seq * kvd + kvh * hd;
-    const int64_t *vb = vc + (size_t)b * max_seq * kvd + kvh * hd;
+    const int sq = seq_arr[b];
+    const int64_t *kb = kc + (size_t)sq * max_seq * kvd + kvh * hd;
+    const int64_t *vb = vc + (size_t)sq * max_seq * kvd + kvh * hd;
     for (int t = threadIdx.x; t < T; t += blockDim.x) {
         const int64_t *kt = kb + (size_t)t * kvd;
         i128 dot = 0;
@@ -153,6 +160,17 @@ __global__ void k_argmax(int *__restrict__ result, const int64_t *__restrict__ l
             if (hist) hist[(size_t)b * hist_stride + p] = idx;
             pos_arr[b] = p;
         }
+    }
+}
+
+// After a prefill: the argmax of the sequence's last prompt row becomes its
+// next token at position L, recorded in the history (llama_int.c:3087-3089).
+__global__ void k_prefill_done(const int *__restrict__ arg, int *__restrict__ tokens, int *__restrict__ pos_arr,
+                               int *__restrict__ hist, int hist_stride, int seq, int L) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        tokens[seq] = arg[0];
+        pos_arr[seq] = L;
+        hist[(size_t)seq * hist_stride + L] = arg[0];
     }
 }
 

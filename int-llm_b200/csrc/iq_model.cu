@@ -71,6 +71,13 @@ struct iq_model {
     // byte-plane packed copies of every projection (M=1 decode path)
     std::vector<Packed> pqkv, po, pgu, pdown;
     Packed plm;
+    // tcgen05 row-plane copies (rows >= 2: batched decode, prefill)
+    std::vector<PackedTC> tqkv, to, tgu, tdown;
+    PackedTC tlm;
+    uint8_t *digits = nullptr;  // x-digit scratch of the tcgen05 GEMM
+    int rmax = 1;               // row capacity of the activation buffers
+    int *d_seq = nullptr;       // sequence of each decode row (identity)
+    int *d_ptok = nullptr, *d_ppos = nullptr, *d_pseq = nullptr;  // prefill rows
     RowAcc *racc = nullptr;  // split-row scratch of the packed matvec (self-resetting)
     // activations (device)
     int64_t *hidden = nullptr, *normed = nullptr, *qkv = nullptr, *att = nullptr, *gu = nullptr,
@@ -80,6 +87,7 @@ struct iq_model {
             *proj_full = nullptr;
     int *d_tok = nullptr, *d_pos = nullptr, *d_arg = nullptr, *d_hist = nullptr;
     int *h_pin = nullptr;  // pinned host scratch: tokens / pos / argmax
+    int *h_rows = nullptr; // pinned host scratch: prefill rows (token, pos, seq) x max_seq
     int64_t *h_logits = nullptr;
     size_t attn_smem = 0;
     cudaGraphExec_t graph = nullptr;  // one decode step at batch max_batch
@@ -126,27 +134,41 @@ __global__ void k_unshard(int64_t *__restrict__ out, const int64_t *__restrict__
     }
 }
 
+// raw int64 weights live on the device only while a layer is being packed
+static int alloc_raw_layer(iq_model *m, int l) {
+    const iq_config &c = m->c;
+    const Shard &S = m->sh;
+    const size_t d = c.hidden_dim;
+    if (!m->norm1[l]) DALLOC(m->norm1[l], d * 8);
+    if (!m->norm2[l]) DALLOC(m->norm2[l], d * 8);
+    if (!m->wqkv[l]) DALLOC(m->wqkv[l], (size_t)m->qkv_rows * d * 8);
+    if (!m->wo[l]) DALLOC(m->wo[l], (size_t)S.d_l * d * 8);
+    if (!m->wgu[l]) DALLOC(m->wgu[l], (size_t)2 * S.it_l * d * 8);
+    if (!m->wdown[l]) DALLOC(m->wdown[l], (size_t)S.d_l * c.intermediate_dim * 8);
+    return IQ_OK;
+}
+static void free_raw_layer(iq_model *m, int l) {
+    for (int64_t **p : {&m->wqkv[l], &m->wo[l], &m->wgu[l], &m->wdown[l]})
+        if (*p) { cudaFree(*p); *p = nullptr; }
+}
+
 static int model_alloc(iq_model *m) {
     const iq_config &c = m->c;
     const Shard &S = m->sh;
-    const int B = m->max_batch, d = c.hidden_dim, L = c.num_layers, hd = c.head_dim;
+    const int B = m->rmax, d = c.hidden_dim, L = c.num_layers, hd = c.head_dim;
     m->kvd_l = S.nkv_l * hd;
     m->qkv_rows = S.nh_l * hd + 2 * m->kvd_l;
     DALLOC(m->embed, (size_t)c.vocab_size * d * 8);
     DALLOC(m->fnorm, (size_t)d * 8);
-    DALLOC(m->lm, (size_t)S.v_l * d * 8);
     m->norm1.resize(L); m->wqkv.resize(L); m->wo.resize(L); m->norm2.resize(L);
     m->wgu.resize(L); m->wdown.resize(L); m->kc.resize(L); m->vc.resize(L);
     m->pqkv.resize(L); m->po.resize(L); m->pgu.resize(L); m->pdown.resize(L);
+    m->tqkv.resize(L); m->to.resize(L); m->tgu.resize(L); m->tdown.resize(L);
     m->loaded_layer.assign(L, false);
     for (int l = 0; l < L; l++) {
         DALLOC(m->norm1[l], (size_t)d * 8);
-        DALLOC(m->wqkv[l], (size_t)m->qkv_rows * d * 8);
-        DALLOC(m->wo[l], (size_t)S.d_l * d * 8);
         DALLOC(m->norm2[l], (size_t)d * 8);
-        DALLOC(m->wgu[l], (size_t)2 * S.it_l * d * 8);
-        DALLOC(m->wdown[l], (size_t)S.d_l * c.intermediate_dim * 8);
-        size_t kvb = (size_t)B * c.max_seq_len * m->kvd_l * 8;
+        size_t kvb = (size_t)m->max_batch * c.max_seq_len * m->kvd_l * 8;
         DALLOC(m->kc[l], kvb);
         DALLOC(m->vc[l], kvb);
     }
@@ -173,13 +195,29 @@ static int model_alloc(iq_model *m) {
         DALLOC(m->gath, (size_t)B * wmax * 8);
         DALLOC(m->proj_full, (size_t)B * d * 8);
     }
-    DALLOC(m->d_tok, (size_t)B * 4);
-    DALLOC(m->d_pos, (size_t)B * 4);
+    const int NB = m->max_batch;
+    DALLOC(m->d_tok, (size_t)NB * 4);
+    DALLOC(m->d_pos, (size_t)NB * 4);
+    DALLOC(m->d_seq, (size_t)NB * 4);
     DALLOC(m->d_arg, (size_t)B * 4);
-    DALLOC(m->d_hist, (size_t)B * (c.max_seq_len + 1) * 4);
-    // pinned ints: [0, B) results, then (max_seq + 2) slots of 2*B (token, pos)
-    IQ_CUDA(cudaMallocHost(&m->h_pin, ((size_t)B + 16 + (size_t)2 * B * (c.max_seq_len + 2)) * 4));
+    DALLOC(m->d_hist, (size_t)NB * (c.max_seq_len + 1) * 4);
+    DALLOC(m->d_ptok, (size_t)B * 4);
+    DALLOC(m->d_ppos, (size_t)B * 4);
+    DALLOC(m->d_pseq, (size_t)B * 4);
+    {
+        std::vector<int> ident(NB);
+        for (int i = 0; i < NB; i++) ident[i] = i;
+        IQ_CUDA(cudaMemcpy(m->d_seq, ident.data(), (size_t)NB * 4, cudaMemcpyHostToDevice));
+    }
+    {
+        size_t kmax = std::max((size_t)d, (size_t)c.intermediate_dim);
+        size_t kpad = (kmax + TC_BK - 1) / TC_BK * TC_BK, rpad = ((size_t)B + TC_BR - 1) / TC_BR * TC_BR;
+        DALLOC(m->digits, rpad * 8 * kpad);
+    }
+    // pinned ints: [0, B) results, then (max_seq + 2) slots of 2*NB (token, pos)
+    IQ_CUDA(cudaMallocHost(&m->h_pin, ((size_t)B + 16 + (size_t)2 * NB * (c.max_seq_len + 2)) * 4));
     IQ_CUDA(cudaMallocHost(&m->h_logits, (size_t)c.vocab_size * 8));
+    IQ_CUDA(cudaMallocHost(&m->h_rows, (size_t)3 * (c.max_seq_len + 1) * 4));
     int groups_area = 256;  // attention block size (PV partials reuse the score area)
     m->attn_smem = (size_t)(hd + (c.max_seq_len > groups_area ? c.max_seq_len : groups_area)) * 8;
     return IQ_OK;
@@ -210,71 +248,87 @@ static int add_into(iq_model *m, int64_t *x, const int64_t *y, int64_t n) {
     return IQ_OK;
 }
 
-// Enqueues one forward step for sequences [0, B): tokens in d_tok, positions in
-// d_pos (both device), logits -> m->logits (full vocabulary on every rank),
-// argmax -> d_arg; the argmax kernel then advances d_tok / d_pos and records the
-// token in d_hist.
-static int enqueue_step(iq_model *m, int B) {
+// Enqueues one forward pass over R rows: row r is token tok[r] of sequence
+// seq[r] at position pos[r] (device arrays). Decode: R = B rows, one per
+// sequence. Prefill: R = L rows of one sequence at positions 0..L-1 -- each
+// row computes exactly what the reference's sequential llama_forward call at
+// that position computes (causal attention per row).
+// lm: 0 = LM head on every row (logits [R][V]); 1 = only the last row (prefill
+// sampling, logits [1][V]); 2 = no LM head (an inner prefill chunk). decode != 0: argmax advances d_tok / d_pos and
+// records the token in d_hist.
+static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, const int *seq, int lm, int decode) {
     const iq_config &c = m->c;
     const Shard &S = m->sh;
     const bool tp = S.P > 1;
     const int d = c.hidden_dim, hd = c.head_dim;
     cudaStream_t s = m->s;
     int rc;
-    auto proj = [&](int64_t *out, const int64_t *W, const Packed &P, const int64_t *x, int M, int N,
+    auto proj = [&](int64_t *out, const Packed &P, const PackedTC &T, const int64_t *x, int rows,
                     int add) -> int {
-        if (B == 1) return launch_matvec_planes(out, P, x, s, add, m->racc);
-        return launch_gemm_add(out, W, x, B, M, N, s, add);
+        if (rows == 1) return launch_matvec_planes(out, P, x, s, add, m->racc);
+        return launch_gemm_tc(out, T, x, rows, s, add, m->digits);
     };
-    k_embed<<<dim3((d + 255) / 256, B), 256, 0, s>>>(m->hidden, m->embed, m->d_tok, d);
+    k_embed<<<dim3((d + 255) / 256, R), 256, 0, s>>>(m->hidden, m->embed, tok, d);
     IQ_CHECK_LAUNCH();
     const int pairs = (S.nh_l + S.nkv_l) * (hd / 2) + m->kvd_l;
     int64_t *att_out = tp ? m->att_l : m->att;
     int64_t *act_out = tp ? m->act_l : m->act;
     for (int l = 0; l < c.num_layers; l++) {
-        k_rmsnorm<<<B, 256, 0, s>>>(m->normed, m->hidden, m->norm1[l], d);
+        k_rmsnorm<<<R, 256, 0, s>>>(m->normed, m->hidden, m->norm1[l], d);
         IQ_CHECK_LAUNCH();
-        if ((rc = proj(m->qkv, m->wqkv[l], m->pqkv[l], m->normed, m->qkv_rows, d, 0))) return rc;
-        k_rope_kv<<<dim3((pairs + 255) / 256, B), 256, 0, s>>>(m->qkv, m->kc[l], m->vc[l], m->rcos, m->rsin,
-                                                               m->d_pos, S.nh_l, S.nkv_l, hd, c.max_seq_len);
+        if ((rc = proj(m->qkv, m->pqkv[l], m->tqkv[l], m->normed, R, 0))) return rc;
+        k_rope_kv<<<dim3((pairs + 255) / 256, R), 256, 0, s>>>(m->qkv, m->kc[l], m->vc[l], m->rcos, m->rsin,
+                                                               pos, seq, S.nh_l, S.nkv_l, hd, c.max_seq_len);
         IQ_CHECK_LAUNCH();
-        k_attention<<<dim3(S.nh_l, B), 256, m->attn_smem, s>>>(att_out, m->qkv, m->kc[l], m->vc[l], m->d_pos,
+        k_attention<<<dim3(S.nh_l, R), 256, m->attn_smem, s>>>(att_out, m->qkv, m->kc[l], m->vc[l], pos, seq,
                                                                S.nh_l, S.nkv_l, hd, c.max_seq_len);
         IQ_CHECK_LAUNCH();
         if (tp) {
-            if ((rc = gather_rows(m, m->att_l, m->att, B, S.nh_l * hd))) return rc;
-            if ((rc = proj(m->proj_l, m->wo[l], m->po[l], m->att, S.d_l, d, 0))) return rc;
-            if ((rc = gather_rows(m, m->proj_l, m->proj_full, B, S.d_l))) return rc;
-            if ((rc = add_into(m, m->hidden, m->proj_full, (int64_t)B * d))) return rc;
-        } else if ((rc = proj(m->hidden, m->wo[l], m->po[l], m->att, d, d, 1))) {
+            if ((rc = gather_rows(m, m->att_l, m->att, R, S.nh_l * hd))) return rc;
+            if ((rc = proj(m->proj_l, m->po[l], m->to[l], m->att, R, 0))) return rc;
+            if ((rc = gather_rows(m, m->proj_l, m->proj_full, R, S.d_l))) return rc;
+            if ((rc = add_into(m, m->hidden, m->proj_full, (int64_t)R * d))) return rc;
+        } else if ((rc = proj(m->hidden, m->po[l], m->to[l], m->att, R, 1))) {
             return rc;
         }
-        k_rmsnorm<<<B, 256, 0, s>>>(m->normed, m->hidden, m->norm2[l], d);
+        k_rmsnorm<<<R, 256, 0, s>>>(m->normed, m->hidden, m->norm2[l], d);
         IQ_CHECK_LAUNCH();
-        if ((rc = proj(m->gu, m->wgu[l], m->pgu[l], m->normed, 2 * S.it_l, d, 0))) return rc;
-        k_swiglu<<<(B * S.it_l + 255) / 256, 256, 0, s>>>(act_out, m->gu, S.it_l, B);
+        if ((rc = proj(m->gu, m->pgu[l], m->tgu[l], m->normed, R, 0))) return rc;
+        k_swiglu<<<(R * S.it_l + 255) / 256, 256, 0, s>>>(act_out, m->gu, S.it_l, R);
         IQ_CHECK_LAUNCH();
         if (tp) {
-            if ((rc = gather_rows(m, m->act_l, m->act, B, S.it_l))) return rc;
-            if ((rc = proj(m->proj_l, m->wdown[l], m->pdown[l], m->act, S.d_l, c.intermediate_dim, 0))) return rc;
-            if ((rc = gather_rows(m, m->proj_l, m->proj_full, B, S.d_l))) return rc;
-            if ((rc = add_into(m, m->hidden, m->proj_full, (int64_t)B * d))) return rc;
-        } else if ((rc = proj(m->hidden, m->wdown[l], m->pdown[l], m->act, d, c.intermediate_dim, 1))) {
+            if ((rc = gather_rows(m, m->act_l, m->act, R, S.it_l))) return rc;
+            if ((rc = proj(m->proj_l, m->pdown[l], m->tdown[l], m->act, R, 0))) return rc;
+            if ((rc = gather_rows(m, m->proj_l, m->proj_full, R, S.d_l))) return rc;
+            if ((rc = add_into(m, m->hidden, m->proj_full, (int64_t)R * d))) return rc;
+        } else if ((rc = proj(m->hidden, m->pdown[l], m->tdown[l], m->act, R, 1))) {
             return rc;
         }
     }
-    k_rmsnorm<<<B, 256, 0, s>>>(m->normed, m->hidden, m->fnorm, d);
+    if (lm == 2) return IQ_OK;                                  // no LM head wanted
+    const int LR = lm ? 1 : R;                                  // rows through the LM head
+    const int64_t *fin = m->normed + (size_t)(R - LR) * d;
+    k_rmsnorm<<<R, 256, 0, s>>>(m->normed, m->hidden, m->fnorm, d);
     IQ_CHECK_LAUNCH();
     if (tp) {
-        if ((rc = proj(m->logits_l, m->lm, m->plm, m->normed, S.v_l, d, 0))) return rc;
-        if ((rc = gather_rows(m, m->logits_l, m->logits, B, S.v_l))) return rc;
-    } else if ((rc = proj(m->logits, m->lm, m->plm, m->normed, c.vocab_size, d, 0))) {
+        if ((rc = proj(m->logits_l, m->plm, m->tlm, fin, LR, 0))) return rc;
+        if ((rc = gather_rows(m, m->logits_l, m->logits, LR, S.v_l))) return rc;
+    } else if ((rc = proj(m->logits, m->plm, m->tlm, fin, LR, 0))) {
         return rc;
     }
-    k_argmax<<<B, 1024, 0, s>>>(m->d_arg, m->logits, c.vocab_size, m->d_tok, m->d_pos, m->d_hist,
-                                c.max_seq_len + 1);
+    if (decode) {
+        k_argmax<<<LR, 1024, 0, s>>>(m->d_arg, m->logits, c.vocab_size, m->d_tok, m->d_pos, m->d_hist,
+                                     c.max_seq_len + 1);
+    } else {
+        k_argmax<<<1, 1024, 0, s>>>(m->d_arg, m->logits + (size_t)(LR - 1) * c.vocab_size, c.vocab_size,
+                                    nullptr, nullptr, nullptr, 0);
+    }
     IQ_CHECK_LAUNCH();
     return IQ_OK;
+}
+
+static int enqueue_step(iq_model *m, int B) {
+    return enqueue_rows(m, B, m->d_tok, m->d_pos, m->d_seq, 0, 1);
 }
 
 static int ensure_graph(iq_model *m) {
@@ -311,14 +365,36 @@ static int repack(iq_model *m, Packed *P, const int64_t *W, int M, int N) {
     IQ_CUDA(cudaStreamSynchronize(m->s));
     return IQ_OK;
 }
+static int repack_tc(iq_model *m, PackedTC *P, const int64_t *W, int M, int N) {
+    if (P->planes) { IQ_CUDA(cudaStreamSynchronize(m->s)); free_packed_tc(P); }
+    int rc = pack_weights_tc(W, M, N, m->s, P);
+    if (rc) return rc;
+    IQ_CUDA(cudaStreamSynchronize(m->s));
+    return IQ_OK;
+}
+// Packs layer l's projections in both formats, then frees its raw int64 copies.
 static int repack_layer(iq_model *m, int l) {
     const iq_config &c = m->c;
     const Shard &S = m->sh;
-    int rc, d = c.hidden_dim;
+    int rc, d = c.hidden_dim, it = c.intermediate_dim;
     if ((rc = repack(m, &m->pqkv[l], m->wqkv[l], m->qkv_rows, d))) return rc;
     if ((rc = repack(m, &m->po[l], m->wo[l], S.d_l, d))) return rc;
     if ((rc = repack(m, &m->pgu[l], m->wgu[l], 2 * S.it_l, d))) return rc;
-    return repack(m, &m->pdown[l], m->wdown[l], S.d_l, c.intermediate_dim);
+    if ((rc = repack(m, &m->pdown[l], m->wdown[l], S.d_l, it))) return rc;
+    if ((rc = repack_tc(m, &m->tqkv[l], m->wqkv[l], m->qkv_rows, d))) return rc;
+    if ((rc = repack_tc(m, &m->to[l], m->wo[l], S.d_l, d))) return rc;
+    if ((rc = repack_tc(m, &m->tgu[l], m->wgu[l], 2 * S.it_l, d))) return rc;
+    if ((rc = repack_tc(m, &m->tdown[l], m->wdown[l], S.d_l, it))) return rc;
+    free_raw_layer(m, l);
+    return IQ_OK;
+}
+static int repack_lm(iq_model *m) {
+    int rc;
+    if ((rc = repack(m, &m->plm, m->lm, m->sh.v_l, m->c.hidden_dim))) return rc;
+    if ((rc = repack_tc(m, &m->tlm, m->lm, m->sh.v_l, m->c.hidden_dim))) return rc;
+    cudaFree(m->lm);
+    m->lm = nullptr;
+    return IQ_OK;
 }
 
 // Where each full host tensor's rows land on this rank: (first row, row count,
@@ -362,13 +438,6 @@ static int upload_pieces(const TensorPlan &tp, const int64_t *full) {
     return IQ_OK;
 }
 
-static int repack_all(iq_model *m) {
-    int rc;
-    if ((rc = repack(m, &m->plm, m->lm, m->sh.v_l, m->c.hidden_dim))) return rc;
-    for (int l = 0; l < m->c.num_layers; l++)
-        if ((rc = repack_layer(m, l))) return rc;
-    return IQ_OK;
-}
 
 extern "C" {
 
@@ -410,6 +479,8 @@ IQ_API int iq_model_create_tp(const iq_config *cfg, int max_batch, int device, i
     m->sh = sh;
     m->dev = device;
     m->max_batch = max_batch;
+    // activation rows: the decode batch, or a prefill chunk of up to 1024 positions
+    m->rmax = std::max(max_batch, std::min(c.max_seq_len, 1024));
     cudaError_t e = cudaStreamCreateWithFlags(&m->s, cudaStreamNonBlocking);
     if (e != cudaSuccess) { delete m; return cuda_fail(e); }
     if ((rc = model_alloc(m))) { iq_model_destroy(m); return rc; }
@@ -447,15 +518,20 @@ IQ_API int iq_model_destroy(iq_model *m) {
     if (m->comm) ncclCommDestroy(m->comm);
     void *bufs[] = {m->embed, m->fnorm, m->lm, m->rcos, m->rsin, m->hidden, m->normed, m->qkv, m->att,
                     m->gu, m->act, m->logits, m->att_l, m->proj_l, m->act_l, m->logits_l, m->gath,
-                    m->proj_full, m->d_tok, m->d_pos, m->d_arg, m->d_hist, m->racc};
+                    m->proj_full, m->d_tok, m->d_pos, m->d_arg, m->d_hist, m->racc, m->digits, m->d_seq,
+                    m->d_ptok, m->d_ppos, m->d_pseq};
     for (void *p : bufs) if (p) cudaFree(p);
     for (auto *v : {&m->norm1, &m->wqkv, &m->wo, &m->norm2, &m->wgu, &m->wdown, &m->kc, &m->vc})
         for (int64_t *p : *v) if (p) cudaFree(p);
     for (auto *v : {&m->pqkv, &m->po, &m->pgu, &m->pdown})
         for (Packed &P : *v) free_packed(&P);
     free_packed(&m->plm);
+    for (auto *v : {&m->tqkv, &m->to, &m->tgu, &m->tdown})
+        for (PackedTC &P : *v) free_packed_tc(&P);
+    free_packed_tc(&m->tlm);
     if (m->h_pin) cudaFreeHost(m->h_pin);
     if (m->h_logits) cudaFreeHost(m->h_logits);
+    if (m->h_rows) cudaFreeHost(m->h_rows);
     if (m->s) cudaStreamDestroy(m->s);
     delete m;
     return IQ_OK;
@@ -465,12 +541,13 @@ IQ_API int iq_model_load_globals(iq_model *m, const int64_t *embed, const int64_
                                  const int64_t *lm_head) {
     if (!m || !embed || !final_norm || !lm_head) return IQ_ERR_ARG;
     IQ_CUDA(cudaSetDevice(m->dev));
+    if (!m->lm) DALLOC(m->lm, (size_t)m->sh.v_l * m->c.hidden_dim * 8);
     std::vector<TensorPlan> plan = tensor_plan(m);
     const int64_t *src[3] = {embed, lm_head, final_norm};
     int rc;
     for (int i = 0; i < 3; i++)
         if ((rc = upload_pieces(plan[i], src[i]))) return rc;
-    if ((rc = repack(m, &m->plm, m->lm, m->sh.v_l, m->c.hidden_dim))) return rc;
+    if ((rc = repack_lm(m))) return rc;
     m->loaded_globals = true;
     return IQ_OK;
 }
@@ -479,8 +556,9 @@ IQ_API int iq_model_load_layer(iq_model *m, int l, const int64_t *const w[9]) {
     if (!m || !w || l < 0 || l >= m->c.num_layers) return IQ_ERR_ARG;
     for (int i = 0; i < 9; i++) if (!w[i]) return IQ_ERR_ARG;
     IQ_CUDA(cudaSetDevice(m->dev));
-    std::vector<TensorPlan> plan = tensor_plan(m);
     int rc;
+    if ((rc = alloc_raw_layer(m, l))) return rc;
+    std::vector<TensorPlan> plan = tensor_plan(m);
     for (int i = 0; i < 9; i++)
         if ((rc = upload_pieces(plan[3 + 9 * l + i], w[i]))) return rc;
     if ((rc = repack_layer(m, l))) return rc;
@@ -500,18 +578,19 @@ IQ_API int iq_model_reset(iq_model *m) {
     return IQ_OK;
 }
 
-IQ_API int iq_model_synth(iq_model *m, int config_index, int threads) {
-    if (!m) return IQ_ERR_ARG;
-    std::vector<TensorPlan> plan = tensor_plan(m);
-    if (threads < 1) threads = 1;
-    std::atomic<size_t> next(0);
+// Synthetic weights: the global tensors, then layer by layer (generate on host
+// threads, upload this rank's rows, pack, free the raw copies), so the device
+// never holds more than one layer of raw int64 weights.
+static int synth_jobs(iq_model *m, const std::vector<TensorPlan> &plan, size_t j0, size_t j1, int config_index,
+                      int threads) {
+    std::atomic<size_t> next(j0);
     std::atomic<int> status(IQ_OK);
     auto worker = [&]() {
         cudaSetDevice(m->dev);
         std::vector<int64_t> buf;
         for (;;) {
             size_t j = next.fetch_add(1);
-            if (j >= plan.size() || status.load() != IQ_OK) return;
+            if (j >= j1 || status.load() != IQ_OK) return;
             const TensorPlan &tp = plan[j];
             size_t n = tp.rows * tp.cols;
             buf.resize(n);
@@ -521,17 +600,35 @@ IQ_API int iq_model_synth(iq_model *m, int config_index, int threads) {
             if (rc) status.store(rc);
         }
     };
+    int nt = (int)std::min<size_t>((size_t)threads, j1 - j0);
     std::vector<std::thread> pool;
-    for (int t = 0; t < threads; t++) pool.emplace_back(worker);
+    for (int t = 0; t < nt; t++) pool.emplace_back(worker);
     for (auto &t : pool) t.join();
-    if (status.load() != IQ_OK) return status.load();
+    return status.load();
+}
+
+IQ_API int iq_model_synth(iq_model *m, int config_index, int threads) {
+    if (!m) return IQ_ERR_ARG;
+    if (threads < 1) threads = 1;
     IQ_CUDA(cudaSetDevice(m->dev));
-    int rc = repack_all(m);
-    if (rc) return rc;
+    if (!m->lm) DALLOC(m->lm, (size_t)m->sh.v_l * m->c.hidden_dim * 8);
+    int rc;
+    for (int l = 0; l < m->c.num_layers; l++)
+        if (!m->norm1[l] && (rc = alloc_raw_layer(m, l))) return rc;
+    std::vector<TensorPlan> plan = tensor_plan(m);  // norms and globals are stable pointers
+    if ((rc = synth_jobs(m, plan, 0, 3, config_index, threads))) return rc;
+    if ((rc = repack_lm(m))) return rc;
+    for (int l = 0; l < m->c.num_layers; l++) {
+        if ((rc = alloc_raw_layer(m, l))) return rc;
+        plan = tensor_plan(m);
+        if ((rc = synth_jobs(m, plan, 3 + 9 * (size_t)l, 3 + 9 * (size_t)(l + 1), config_index, threads))) return rc;
+        if ((rc = repack_layer(m, l))) return rc;
+    }
     m->loaded_globals = true;
     m->loaded_layer.assign(m->c.num_layers, true);
     return IQ_OK;
 }
+
 // ------------------------------------------------------------- forward
 
 static int set_tok_pos(iq_model *m, const int *tok, const int *pos, int B, int slot) {
@@ -543,20 +640,52 @@ static int set_tok_pos(iq_model *m, const int *tok, const int *pos, int B, int s
     return IQ_OK;
 }
 
+// Enqueues the prefill of sequence sq: prompt positions 0..L-1 in chunks of up
+// to rmax rows. hash_logits: LM head on every row and the logits of every
+// position appended to *hv in order; otherwise only the last row's logits.
+// Ends with the sequence's decode state at position L (k_prefill_done).
+static int enqueue_prefill(iq_model *m, int sq, const int *prompt, int L, std::vector<int64_t> *hv) {
+    int *h = m->h_rows;
+    for (int p = 0; p < L; p++) { h[p] = prompt[p]; h[L + p] = p; h[2 * L + p] = sq; }
+    int rc;
+    for (int p0 = 0; p0 < L; p0 += m->rmax) {
+        const int n = std::min(m->rmax, L - p0);
+        const bool last = p0 + n == L;
+        IQ_CUDA(cudaMemcpyAsync(m->d_ptok, h + p0, (size_t)n * 4, cudaMemcpyHostToDevice, m->s));
+        IQ_CUDA(cudaMemcpyAsync(m->d_ppos, h + L + p0, (size_t)n * 4, cudaMemcpyHostToDevice, m->s));
+        IQ_CUDA(cudaMemcpyAsync(m->d_pseq, h + 2 * L + p0, (size_t)n * 4, cudaMemcpyHostToDevice, m->s));
+        if ((rc = enqueue_rows(m, n, m->d_ptok, m->d_ppos, m->d_pseq, hv ? 0 : (last ? 1 : 2), 0))) return rc;
+        if (hv) {
+            size_t old = hv->size(), cnt = (size_t)n * m->c.vocab_size;
+            hv->resize(old + cnt);
+            IQ_CUDA(cudaMemcpyAsync(hv->data() + old, m->logits, cnt * 8, cudaMemcpyDeviceToHost, m->s));
+        }
+        // the pinned row arrays are reused by the next chunk only after these copies ran
+        IQ_CUDA(cudaStreamSynchronize(m->s));
+    }
+    k_prefill_done<<<1, 32, 0, m->s>>>(m->d_arg, m->d_tok, m->d_pos, m->d_hist, m->c.max_seq_len + 1, sq, L);
+    IQ_CHECK_LAUNCH();
+    return IQ_OK;
+}
+
 IQ_API int iq_forward(iq_model *m, int token, int pos, int64_t *logits, int *argmax_out) {
     if (!model_ready(m)) return m ? IQ_ERR_STATE : IQ_ERR_ARG;
     if (token < 0 || token >= m->c.vocab_size || pos < 0 || pos >= m->c.max_seq_len) return IQ_ERR_RANGE;
     IQ_CUDA(cudaSetDevice(m->dev));
     IQ_CUDA(cudaStreamSynchronize(m->s));
     int rc;
-    if ((rc = set_tok_pos(m, &token, &pos, 1, 0))) return rc;
-    if ((rc = enqueue_step(m, 1))) return rc;
+    int *h = m->h_rows;
+    h[0] = token; h[1] = pos; h[2] = 0;
+    IQ_CUDA(cudaMemcpyAsync(m->d_ptok, h, 4, cudaMemcpyHostToDevice, m->s));
+    IQ_CUDA(cudaMemcpyAsync(m->d_ppos, h + 1, 4, cudaMemcpyHostToDevice, m->s));
+    IQ_CUDA(cudaMemcpyAsync(m->d_pseq, h + 2, 4, cudaMemcpyHostToDevice, m->s));
+    if ((rc = enqueue_rows(m, 1, m->d_ptok, m->d_ppos, m->d_pseq, 0, 0))) return rc;
     if (logits) IQ_CUDA(cudaMemcpyAsync(m->h_logits, m->logits, (size_t)m->c.vocab_size * 8, cudaMemcpyDeviceToHost, m->s));
     IQ_CUDA(cudaMemcpyAsync(m->h_pin, m->d_arg, 4, cudaMemcpyDeviceToHost, m->s));
     IQ_CUDA(cudaStreamSynchronize(m->s));
     if (logits) memcpy(logits, m->h_logits, (size_t)m->c.vocab_size * 8);
     if (argmax_out) *argmax_out = m->h_pin[0];
-    return IQ_OK;
+    return take_dev_error();
 }
 
 static uint64_t fnv_mix(uint64_t h, const int64_t *v, size_t n) {
@@ -590,31 +719,27 @@ IQ_API int iq_generate(iq_model *m, const int *prompt, int plen, int max_new, in
     int rc;
     if ((rc = iq_model_reset(m))) return rc;
     const bool hash = logit_hash != nullptr;
+    const int V = c.vocab_size;
     uint64_t h = 1469598103934665603ULL;
     memcpy(out, prompt, (size_t)plen * sizeof(int));
-    const int V = c.vocab_size;
-    auto pull = [&]() -> int {  // sync, fold this step's logits into the hash, return argmax
-        IQ_CUDA(cudaMemcpyAsync(m->h_logits, m->logits, (size_t)V * 8, cudaMemcpyDeviceToHost, m->s));
-        IQ_CUDA(cudaMemcpyAsync(m->h_pin, m->d_arg, 4, cudaMemcpyDeviceToHost, m->s));
-        IQ_CUDA(cudaStreamSynchronize(m->s));
-        h = fnv_mix(h, m->h_logits, V);
-        return IQ_OK;
-    };
-    // prefill: one M=1 forward per prompt position (llama_int.c:3081-3092)
-    for (int p = 0; p < plen; p++) {
-        if ((rc = set_tok_pos(m, &prompt[p], &p, 1, p))) return rc;
-        if ((rc = run_step(m, 1))) return rc;
-        if (hash && (rc = pull())) return rc;
-    }
+    // prefill: every prompt position in batched rows (== the M=1 loop of llama_int.c:3081-3092)
+    std::vector<int64_t> hv;
+    if ((rc = enqueue_prefill(m, 0, prompt, plen, hash ? &hv : nullptr))) return rc;
+    if (hash) h = fnv_mix(h, hv.data(), hv.size());
     int total = plen;
     // decode positions plen .. ; the reference stops when pos reaches max_seq_len
-    int steps = std::min(max_new - 1, c.max_seq_len - plen);
+    const int steps = std::min(max_new - 1, c.max_seq_len - plen);
     if (hash) {
+        IQ_CUDA(cudaMemcpyAsync(m->h_pin, m->d_tok, 4, cudaMemcpyDeviceToHost, m->s));
+        IQ_CUDA(cudaStreamSynchronize(m->s));
         out[total++] = m->h_pin[0];  // prefill's sample is appended unconditionally
         for (int i = 1; i <= steps; i++) {
             if ((rc = run_step(m, 1))) return rc;  // d_tok / d_pos advanced on the device
-            if ((rc = pull())) return rc;
-            int nx = m->h_pin[0];
+            IQ_CUDA(cudaMemcpyAsync(m->h_logits, m->logits, (size_t)V * 8, cudaMemcpyDeviceToHost, m->s));
+            IQ_CUDA(cudaMemcpyAsync(m->h_pin, m->d_arg, 4, cudaMemcpyDeviceToHost, m->s));
+            IQ_CUDA(cudaStreamSynchronize(m->s));
+            h = fnv_mix(h, m->h_logits, V);
+            const int nx = m->h_pin[0];
             if (nx == 2) break;  // LLAMA_EOS (llama_int.c:3046, 3110)
             out[total++] = nx;
         }
@@ -632,7 +757,7 @@ IQ_API int iq_generate(iq_model *m, const int *prompt, int plen, int max_new, in
         }
     }
     *n_out = total;
-    return IQ_OK;
+    return take_dev_error();
 }
 
 IQ_API int iq_generate_batch(iq_model *m, const int *prompts, int plen, int max_new, int *out, int *n_out) {
@@ -645,13 +770,9 @@ IQ_API int iq_generate_batch(iq_model *m, const int *prompts, int plen, int max_
     if (plen > c.max_seq_len) return IQ_ERR_RANGE;
     int rc;
     if ((rc = iq_model_reset(m))) return rc;
-    std::vector<int> tok(B), pos(B);
-    for (int p = 0; p < plen; p++) {
-        for (int b = 0; b < B; b++) { tok[b] = prompts[(size_t)b * plen + p]; pos[b] = p; }
-        if ((rc = set_tok_pos(m, tok.data(), pos.data(), B, p))) return rc;
-        if ((rc = run_step(m, B))) return rc;
-    }
-    int steps = std::min(max_new - 1, c.max_seq_len - plen);
+    for (int b = 0; b < B; b++)  // each sequence's prompt as batched rows
+        if ((rc = enqueue_prefill(m, b, prompts + (size_t)b * plen, plen, nullptr))) return rc;
+    const int steps = std::min(max_new - 1, c.max_seq_len - plen);
     for (int i = 1; i <= steps; i++)
         if ((rc = run_step(m, B))) return rc;
     const int stride = c.max_seq_len + 1;
@@ -671,7 +792,7 @@ IQ_API int iq_generate_batch(iq_model *m, const int *prompts, int plen, int max_
         }
         n_out[b] = total;
     }
-    return IQ_OK;
+    return take_dev_error();
 }
 
 IQ_API int iq_decode_steps_timed(iq_model *m, int pos0, int steps, float *ms) {

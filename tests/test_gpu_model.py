@@ -105,3 +105,20 @@ def test_cfg0_tinyllama_greedy_decode_golden():
     toks2, _ = m.generate(np.array(g["prompt"]), g["max_new"])
     assert toks2 == g["tokens"]
     m.close()
+
+
+def test_long_prompt_chunked_prefill_matches_sequential_oracle():
+    """A prompt longer than one prefill chunk (1024 rows): batched prefill with
+    per-row causal attention equals the reference's position-by-position loop,
+    every logit included (hash), then greedy decode continues identically."""
+    c = dict(configs.TINY_TEST, n_layers=1, max_seq=1100)
+    w = helpers.model_weights(9, c)
+    m = iq.Model(c)
+    m.load(w)
+    o = helpers.OracleModel(c, w)
+    pr = orc.synth_tokens(9, "prompt:long", 1030, c["vocab"])
+    t1, h1 = m.generate(pr, 12, logit_hash=True)
+    t2, h2 = o.generate(pr, 12)
+    t3, _ = m.generate(pr, 12)
+    assert t1 == t2 == t3 and h1 == h2
+    m.close(); o.close()
