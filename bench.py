@@ -337,6 +337,147 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ----------------------------------------------------- model workloads
+
+def _tp_setup():
+    """rank / world / local from torchrun, NCCL id shared from rank 0."""
+    import torch
+    import iq
+    rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    iq.set_device(local)
+    dist, nid = None, None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        obj = [iq.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nid = obj[0]
+    return rank, world, local, dist, nid
+
+
+def _max_over_ranks(dist, v):
+    import torch
+    if not dist:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+def run_model_workload(args):
+    """cfg0: TinyLlama greedy decode (B=1); cfg3: batch-64 decode after 2048-token
+    prefills; cfg4: Llama-2-7B shape, 2048-token prefill + 64 decode tokens.
+    N > 1: output-row tensor parallelism over the ranks (NCCL all-gathers)."""
+    import torch
+    import iq
+    rank, world, local, dist, nid = _tp_setup()
+    wl = args.workload
+    if wl == "cfg0":
+        cfg, ci, B, plen, dec, pos0 = dict(configs.TINYLLAMA), 0, 1, 8, max(args.steps, 32), 40
+    elif wl == "cfg3":
+        cfg, ci, B, plen, dec, pos0 = dict(configs.TINYLLAMA, max_seq=2176), 3, 64, 2048, 128, 2048
+    else:
+        cfg, ci, B, plen, dec, pos0 = dict(configs.LLAMA7B), 4, 1, 2048, 64, 2048
+    t0 = time.perf_counter()
+    m = iq.Model(cfg, max_batch=B, device=local, tp_rank=rank, tp_size=world, nccl_id=nid)
+    m.synth(ci, threads=max(1, (os.cpu_count() or 1) // world))
+    t_load = time.perf_counter() - t0
+    prompts = np.stack([iq.synth_tokens(ci, f"prompt:{b}", plen, cfg["vocab"]) for b in range(B)])
+    # e2e through the public API: prefill (+ first token) from host prompts
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    if B == 1:
+        toks, _ = m.generate(prompts[0], 1)
+    else:
+        outs = m.generate_batch(prompts, 1)
+    t_prefill = _max_over_ranks(dist, time.perf_counter() - t0)
+    # decode: graph replays of the whole step (all B sequences), device-timed
+    m.decode_steps_timed(pos0, 3)
+    clk = Clocks(local)
+    clk.start()
+    time.sleep(0.2)
+    ms = m.decode_steps_timed(pos0, dec)
+    clocks = clk.stop()
+    ms = _max_over_ranks(dist, ms)
+    # e2e decode through generate(): prompt in, tokens out (host buffers)
+    e2e = None
+    if wl == "cfg0":
+        t0 = time.perf_counter()
+        toks, _ = m.generate(prompts[0], 32)
+        e2e_s = _max_over_ranks(dist, time.perf_counter() - t0)
+        e2e = {"value": (len(toks) - plen) / e2e_s, "unit": "tokens/s",
+               "h2d_bytes_per_step": 4 * plen, "d2h_bytes_per_step": 4 * (plen + 32),
+               "api": "iq_generate (8-token prompt + 32 greedy tokens, per call)"}
+    tok_s = B * dec / (ms / 1e3)
+    d, L, V, it = cfg["dim"], cfg["n_layers"], cfg["vocab"], cfg["inter"]
+    kvd = cfg["n_kv_heads"] * cfg["head_dim"]
+    wbytes = 8 * (L * (d * (d + 2 * kvd) + d * d + 3 * d * it) + V * d)
+    kv_bytes = 8 * 2 * L * kvd * (pos0 + dec / 2) * B
+    peak, peak_kind = measured_peak()
+    step_s = ms / 1e3 / dec
+    ach = (wbytes / world + kv_bytes / world) / step_s / 1e9  # per GPU
+    line = {
+        "metric": {"cfg0": "TinyLlama greedy decode tokens/s (B=1), bit-exact",
+                   "cfg3": "TinyLlama batch-64 decode tokens/s after 2048-token prefills, bit-exact",
+                   "cfg4": "Llama-2-7B-shape decode tokens/s after a 2048-token prefill, bit-exact"}[wl],
+        "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": dec, "warmup": 3,
+        "ms_per_step": ms / dec, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int64", "data": "synthetic", "config": {"workload": wl, "batch": B, "prompt": plen,
+                                                          "decode_from_pos": pos0,
+                                                          "parallelism": f"tp{world}"},
+        "prefill_s": t_prefill, "prefill_tokens_per_s": B * plen / t_prefill, "load_s": t_load,
+        "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                     "peak_source": peak_kind, "kernel": "decode step (all kernels)",
+                     "bytes_per_step_per_gpu": (wbytes + kv_bytes) / world, "traffic": None},
+        "gpu_launches": None, "clocks": clocks,
+    }
+    if e2e:
+        line["e2e"] = e2e
+    if rank == 0:
+        print(json.dumps(line))
+    m.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+def run_gemm_workload(args):
+    """cfg2: M=512 prefill GEMM on the fused TinyLlama projections (tcgen05)."""
+    import torch
+    import iq
+    torch.cuda.set_device(0)
+    rows = configs.CFG2_ROWS
+    s = torch.cuda.Stream()
+    per, tot_mac, tot_ms = {}, 0, 0.0
+    for tag, K, N in configs.CFG2_SHAPES:
+        wn, xn = configs.gemm_names(tag, K, N, rows)
+        w = torch.from_numpy(iq.synth_weights(2, wn, (N, K))).cuda()
+        X = torch.from_numpy(iq.synth_acts(2, xn, (rows, K))).cuda()
+        pk = iq.PackedTC(w, N, K)
+        out = torch.empty((rows, N), dtype=torch.int64, device="cuda")
+        reps = max(10, args.steps // 100)
+        with torch.cuda.stream(s):
+            for _ in range(args.warmup):
+                iq.gemm_tc_dev(out, pk, X, rows, stream=s)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(reps):
+                iq.gemm_tc_dev(out, pk, X, rows, stream=s)
+            e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        macs = rows * K * N
+        per[tag] = {"K": K, "N": N, "ms": ms, "gmacs": macs / ms / 1e6, "int8_tops": 128 * macs / ms / 1e9}
+        tot_mac += macs
+        tot_ms += ms
+        pk.free()
+    print(json.dumps({"metric": "Q16.48 prefill GEMM GMAC/s, config 2 (M=512), bit-exact", "value": tot_mac / tot_ms / 1e6,
+                      "unit": "GMAC/s", "n_gpus": 1, "higher_is_better": True, "dtype": "int64",
+                      "data": "synthetic", "config": {"workload": "cfg2", "rows": rows}, "per_shape": per}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -344,13 +485,19 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg0", "cfg2", "cfg3", "cfg4"],
+                    help="cfg1 (default, the headline): M=1 matvec microbench")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    else:
+    elif args.workload == "cfg1":
         run_ours(args)
+    elif args.workload == "cfg2":
+        run_gemm_workload(args)
+    else:
+        run_model_workload(args)
 
 
 if __name__ == "__main__":

@@ -300,9 +300,27 @@ static int stream_bytes(cudaStream_t s, size_t bytes, uint8_t **out) {
     return IQ_OK;
 }
 
-// out[r][i] (+)= rows of matmul_vec for X [R][K]; digits: >= Rpad*8*Kpad bytes scratch
+// Split-K factor for a grid of `tiles` output tiles: enough CTAs for ~2 per SM.
+static int gemm_ksplit(const PackedTC &P, int R) {
+    const int Rpad = (R + TC_BR - 1) / TC_BR * TC_BR;
+    const int tiles = (P.Mpad / TC_BM) * (Rpad / TC_BR), KBall = P.Kpad / TC_BK;
+    int ks = (2 * dev_info().sms + tiles - 1) / tiles;
+    // each split keeps >= 8 K blocks: the per-plane epilogue fold is a fixed cost
+    // per CTA, so thin splits would make it, not the MMAs, the bottleneck
+    return std::max(1, std::min(ks, std::min(KBall / 8, 16)));
+}
+// bytes of split-K partial scratch launch_gemm_tc needs for (P, R)
+size_t gemm_tc_part_bytes(const PackedTC &P, int R) {
+    const int ks = gemm_ksplit(P, R);
+    if (ks <= 1) return 0;
+    const size_t Rpad = (size_t)(R + TC_BR - 1) / TC_BR * TC_BR;
+    return (size_t)ks * Rpad * P.Mpad * 16;
+}
+
+// out[r][i] (+)= rows of matmul_vec for X [R][K]; digits: >= Rpad*8*Kpad bytes scratch;
+// part: >= gemm_tc_part_bytes(P, R) bytes (unused when no split-K is needed)
 int launch_gemm_tc(int64_t *out, const PackedTC &P, const int64_t *X, int R, cudaStream_t s, int add,
-                   uint8_t *digits) {
+                   uint8_t *digits, int64_t *part) {
     const int Rpad = (R + TC_BR - 1) / TC_BR * TC_BR;
     int64_t n = (int64_t)Rpad * P.Kpad;
     k_x_digits<<<(int)std::min<int64_t>((n + 255) / 256, (int64_t)dev_info().sms * 64), 256, 0, s>>>(
@@ -312,9 +330,16 @@ int launch_gemm_tc(int64_t *out, const PackedTC &P, const int64_t *X, int R, cud
     int rc = encode_u8_map(&mapB, digits, (uint64_t)Rpad * 8, (uint64_t)P.Kpad, TC_BR * 8);
     if (rc) return rc;
     IQ_CUDA(cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
-    dim3 grid(P.Mpad / TC_BM, Rpad / TC_BR);
-    k_gemm_tc<<<grid, 192, TC_SMEM, s>>>(P.mapA, mapB, out, P.rowsum, P.M, R, P.Mpad, P.Kpad, add);
+    const int ks = part ? gemm_ksplit(P, R) : 1;
+    dim3 grid(P.Mpad / TC_BM, Rpad / TC_BR, ks);
+    k_gemm_tc<<<grid, 192, TC_SMEM, s>>>(P.mapA, mapB, out, P.rowsum, P.M, R, P.Mpad, P.Kpad, add, part, Rpad);
     IQ_CHECK_LAUNCH();
+    if (ks > 1) {
+        int64_t n = (int64_t)R * P.M;
+        k_gemm_reduce<<<(int)std::min<int64_t>((n + 255) / 256, (int64_t)dev_info().sms * 16), 256, 0, s>>>(
+            out, part, P.rowsum, P.M, R, P.Mpad, Rpad, ks, add);
+        IQ_CHECK_LAUNCH();
+    }
     return IQ_OK;
 }
 
@@ -580,9 +605,12 @@ IQ_API int iq_gemm_tc_dev(int64_t *d_out, const iq_packed_tc *w, const int64_t *
     if (dev != w->dev) return IQ_ERR_ARG;
     cudaStream_t s = pick(stream);
     const size_t Rpad = (size_t)(rows + TC_BR - 1) / TC_BR * TC_BR;
+    // one byte scratch: the digit matrix, then (16-byte aligned) the split-K partials
+    const size_t dbytes = (Rpad * 8 * (size_t)w->P.Kpad + 255) / 256 * 256;
+    const size_t pbytes = gemm_tc_part_bytes(w->P, rows);
     uint8_t *dg = nullptr;
-    if ((rc = stream_bytes(s, Rpad * 8 * (size_t)w->P.Kpad, &dg))) return rc;
-    return launch_gemm_tc(d_out, w->P, d_X, rows, s, 0, dg);
+    if ((rc = stream_bytes(s, dbytes + pbytes, &dg))) return rc;
+    return launch_gemm_tc(d_out, w->P, d_X, rows, s, 0, dg, pbytes ? (int64_t *)(dg + dbytes) : nullptr);
 }
 
 IQ_API int iq_device_status(void) {

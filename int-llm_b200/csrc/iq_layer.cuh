@@ -114,6 +114,180 @@ __global__ void k_attention(int64_t *__restrict__ out, const int64_t *__restrict
     }
 }
 
+// Exact attention with coalesced K tiles: one CTA per (row b, block of hpc
+// query heads that share one kv head; hpc divides nh / nkv). Keys are staged
+// ATT_TT positions at a time into shared memory with coalesced loads, and
+// each thread computes whole dots from there; V is read coalesced across d.
+// Heads of one kv group are adjacent CTAs, so their K/V re-reads hit L2.
+// Same arithmetic as k_attention (llama_int.c:1432-1529): int128 QK dots,
+// fp_mul by 1/sqrt(hd), integer softmax, int64 sum of fp_mul(p_t, v_t[d]).
+// Shared memory: q [hpc][hd] | scores [hpc][Tcap] | K tile [ATT_TT][hd + 1].
+#define ATT_TT 64
+__global__ void __launch_bounds__(256)
+k_attention_gqa(int64_t *__restrict__ out, const int64_t *__restrict__ qkv, const int64_t *__restrict__ kc,
+                const int64_t *__restrict__ vc, const int *__restrict__ pos_arr, const int *__restrict__ seq_arr,
+                int nh, int nkv, int hd, int max_seq, int Tcap, int hpc) {
+    extern __shared__ __align__(16) int64_t sm[];
+    __shared__ uint64_t red[64];
+    const int b = blockIdx.y, h0 = blockIdx.x * hpc;
+    const int grp = hpc, dim = nh * hd, kvd = nkv * hd, g = h0 / (nh / nkv);
+    const int T = pos_arr[b] + 1, sq = seq_arr[b];
+    int64_t *qs = sm;                       // [grp][hd]
+    int64_t *sc = qs + grp * hd;            // [grp][Tcap]
+    int64_t *kt = sc + (size_t)grp * Tcap;  // [ATT_TT][hd + 1]
+    const int kld = hd + 1;
+    const int64_t *q = qkv + (size_t)b * (dim + 2 * kvd) + (size_t)h0 * hd;
+    for (int e = threadIdx.x; e < grp * hd; e += blockDim.x) qs[e] = q[e];
+    const int64_t scale = d_inv_sqrt(d_from_int(hd));
+    const int64_t *kb = kc + (size_t)sq * max_seq * kvd + g * hd;
+    const int64_t *vb = vc + (size_t)sq * max_seq * kvd + g * hd;
+    for (int t0 = 0; t0 < T; t0 += ATT_TT) {
+        const int nt = min(ATT_TT, T - t0);
+        __syncthreads();
+        for (int e = threadIdx.x; e < nt * hd; e += blockDim.x) {  // coalesced K tile load
+            int tt = e / hd, dd = e % hd;
+            kt[tt * kld + dd] = kb[(size_t)(t0 + tt) * kvd + dd];
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < grp * ATT_TT; e += blockDim.x) {
+            int hh = e / ATT_TT, tt = e % ATT_TT;
+            if (tt < nt) {
+                const int64_t *qh = qs + hh * hd, *kr = kt + tt * kld;
+                i128 dot = 0;
+                for (int dd = 0; dd < hd; dd++) dot += d_mul128(qh[dd], kr[dd]);
+                sc[(size_t)hh * Tcap + t0 + tt] = d_mul((int64_t)(dot >> 48), scale);
+            }
+        }
+    }
+    __syncthreads();
+    for (int hh = 0; hh < grp; hh++) {
+        cta_softmax(sc + (size_t)hh * Tcap, T, red);
+        __syncthreads();
+    }
+    for (int e = threadIdx.x; e < grp * hd; e += blockDim.x) {
+        const int hh = e / hd, dd = e % hd;
+        const int64_t *p = sc + (size_t)hh * Tcap;
+        uint64_t acc = 0;
+        for (int t = 0; t < T; t++) acc += (uint64_t)d_mul(p[t], vb[(size_t)t * kvd + dd]);
+        out[(size_t)b * dim + (size_t)(h0 + hh) * hd + dd] = (int64_t)acc;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Phased exact attention (llama_int.c:1432-1529), parallel over (row, kv
+// group, 64-position tile). Per row b (sequence seq[b], position pos[b]) and
+// query head h the reference computes, in order:
+//   s_t = fp_mul((int64)(sum_d (i128)q_h[d] k_t[d] >> 48), fp_inv_sqrt(hd))
+//   m = max_t s_t;  e_t = fp_safe_exp(s_t - m);  S = sum_t e_t (int64, wrapping)
+//   p_t = S > 0 ? fp_div(e_t, S) : e_t;  out_h[d] = sum_t fp_mul(p_t, v_t[d]) (int64)
+// Every reduction here is exact and order-free: max, wrapping int64 sums.
+// scratch: sc [R][nh][Tcap] scores/numerators, mx [R][nh], sm_ [R][nh] (u64).
+#define ATT_TILE 64
+
+// zero the outputs and sums, max = INT64_MIN
+__global__ void k_attn_init(int64_t *__restrict__ out, int64_t *__restrict__ mx, uint64_t *__restrict__ sm_,
+                            int R, int nh, int hd) {
+    const int64_t n = (int64_t)R * nh * hd;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        out[e] = 0;
+        if (e < (int64_t)R * nh) { mx[e] = INT64_MIN; sm_[e] = 0; }
+    }
+}
+
+// phase 1: scores of one 64-position tile for the grp query heads of kv head g
+__global__ void __launch_bounds__(256)
+k_attn_scores(int64_t *__restrict__ sc, int64_t *__restrict__ mx, const int64_t *__restrict__ qkv,
+              const int64_t *__restrict__ kc, const int *__restrict__ pos_arr, const int *__restrict__ seq_arr,
+              int nh, int nkv, int hd, int max_seq, int Tcap) {
+    extern __shared__ __align__(16) int64_t smem[];
+    const int tile = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int T = pos_arr[b] + 1, t0 = tile * ATT_TILE;
+    if (t0 >= T) return;
+    const int nt = min(ATT_TILE, T - t0);
+    const int grp = nh / nkv, dim = nh * hd, kvd = nkv * hd, kld = hd + 1;
+    int64_t *qs = smem;               // [grp][hd]
+    int64_t *kt = qs + grp * hd;      // [ATT_TILE][hd + 1]
+    const int64_t *q = qkv + (size_t)b * (dim + 2 * kvd) + (size_t)g * grp * hd;
+    for (int e = threadIdx.x; e < grp * hd; e += blockDim.x) qs[e] = q[e];
+    const int64_t *kb = kc + ((size_t)seq_arr[b] * max_seq + t0) * kvd + g * hd;
+    for (int e = threadIdx.x; e < nt * hd; e += blockDim.x) kt[(e / hd) * kld + e % hd] = kb[(size_t)(e / hd) * kvd + e % hd];
+    __syncthreads();
+    const int64_t scale = d_inv_sqrt(d_from_int(hd));
+    for (int e = threadIdx.x; e < grp * ATT_TILE; e += blockDim.x) {
+        const int hh = e / ATT_TILE, tt = e % ATT_TILE;
+        int64_t v = INT64_MIN;
+        if (tt < nt) {
+            const int64_t *qh = qs + hh * hd, *kr = kt + tt * kld;
+            i128 dot = 0;
+#pragma unroll 8
+            for (int dd = 0; dd < hd; dd++) dot += d_mul128(qh[dd], kr[dd]);
+            v = d_mul((int64_t)(dot >> 48), scale);
+            sc[((size_t)b * nh + g * grp + hh) * Tcap + t0 + tt] = v;
+        }
+        // tile max per head: the 64 tt of one head are two consecutive warps
+        for (int m = 16; m >= 1; m >>= 1) v = max(v, (int64_t)__shfl_xor_sync(0xffffffffu, v, m));
+        if ((threadIdx.x & 31) == 0 && v != INT64_MIN)
+            atomicMax((long long *)&mx[(size_t)b * nh + g * grp + hh], (long long)v);
+    }
+}
+
+// phase 2: e_t = fp_safe_exp(s_t - max) in place, S = wrapping int64 sum
+__global__ void __launch_bounds__(256)
+k_attn_exp(int64_t *__restrict__ sc, const int64_t *__restrict__ mx, uint64_t *__restrict__ sm_,
+           const int *__restrict__ pos_arr, int nh, int Tcap) {
+    const int h = blockIdx.y, b = blockIdx.z;
+    const int T = pos_arr[b] + 1, t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (blockIdx.x * blockDim.x >= T) return;
+    const size_t base = ((size_t)b * nh + h) * Tcap;
+    const int64_t m = mx[(size_t)b * nh + h];
+    uint64_t e = 0;
+    if (t < T) {
+        int64_t v = d_safe_exp((int64_t)((uint64_t)sc[base + t] - (uint64_t)m));
+        sc[base + t] = v;
+        e = (uint64_t)v;
+    }
+    for (int k = 16; k >= 1; k >>= 1) e += __shfl_xor_sync(0xffffffffu, e, k);
+    if ((threadIdx.x & 31) == 0) atomicAdd((unsigned long long *)&sm_[(size_t)b * nh + h], (unsigned long long)e);
+}
+
+// phase 3: p_t = fp_div(e_t, S) (if S > 0) for the tile, then int64 partial
+// sums of fp_mul(p_t, v_t[d]) added atomically into out (wrapping, exact)
+__global__ void __launch_bounds__(256)
+k_attn_pv(int64_t *__restrict__ out, const int64_t *__restrict__ sc, const uint64_t *__restrict__ sm_,
+          const int64_t *__restrict__ vc, const int *__restrict__ pos_arr, const int *__restrict__ seq_arr,
+          int nh, int nkv, int hd, int max_seq, int Tcap) {
+    extern __shared__ __align__(16) int64_t smem[];
+    const int tile = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int T = pos_arr[b] + 1, t0 = tile * ATT_TILE;
+    if (t0 >= T) return;
+    const int nt = min(ATT_TILE, T - t0);
+    const int grp = nh / nkv, dim = nh * hd, kvd = nkv * hd;
+    int64_t *ps = smem;                // [grp][ATT_TILE]
+    int64_t *vt = ps + grp * ATT_TILE; // [ATT_TILE][hd]
+    for (int e = threadIdx.x; e < grp * ATT_TILE; e += blockDim.x) {
+        const int hh = e / ATT_TILE, tt = e % ATT_TILE;
+        int64_t p = 0;
+        if (tt < nt) {
+            const int h = g * grp + hh;
+            p = sc[((size_t)b * nh + h) * Tcap + t0 + tt];
+            const int64_t S = (int64_t)sm_[(size_t)b * nh + h];
+            if (S > 0) p = d_div(p, S);
+        }
+        ps[e] = p;
+    }
+    const int64_t *vb = vc + ((size_t)seq_arr[b] * max_seq + t0) * kvd + g * hd;
+    for (int e = threadIdx.x; e < nt * hd; e += blockDim.x) vt[e] = vb[(size_t)(e / hd) * kvd + e % hd];
+    __syncthreads();
+    for (int e = threadIdx.x; e < grp * hd; e += blockDim.x) {
+        const int hh = e / hd, dd = e % hd;
+        const int64_t *p = ps + hh * ATT_TILE;
+        uint64_t acc = 0;
+        for (int tt = 0; tt < nt; tt++) acc += (uint64_t)d_mul(p[tt], vt[tt * hd + dd]);
+        atomicAdd((unsigned long long *)&out[(size_t)b * dim + (size_t)(g * grp + hh) * hd + dd],
+                  (unsigned long long)acc);
+    }
+}
+
 // SwiGLU: out[i] = fp_mul(fp_silu(gate[i]), up[i]) with gu = [gate | up] (llama_int.c:1549-1552)
 __global__ void k_swiglu(int64_t *__restrict__ out, const int64_t *__restrict__ gu, int inter, int rows) {
     const int64_t n = (int64_t)inter * rows;

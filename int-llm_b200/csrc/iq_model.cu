@@ -75,6 +75,8 @@ struct iq_model {
     std::vector<PackedTC> tqkv, to, tgu, tdown;
     PackedTC tlm;
     uint8_t *digits = nullptr;  // x-digit scratch of the tcgen05 GEMM
+    int64_t *gpart = nullptr;   // split-K partial scratch of the tcgen05 GEMM
+    size_t gpart_bytes = 0;
     int rmax = 1;               // row capacity of the activation buffers
     int *d_seq = nullptr;       // sequence of each decode row (identity)
     int *d_ptok = nullptr, *d_ppos = nullptr, *d_pseq = nullptr;  // prefill rows
@@ -90,6 +92,12 @@ struct iq_model {
     int *h_rows = nullptr; // pinned host scratch: prefill rows (token, pos, seq) x max_seq
     int64_t *h_logits = nullptr;
     size_t attn_smem = 0;
+    size_t gqa_smem = 0;  // k_attention_gqa shared memory (0 = use k_attention)
+    int hpc = 1;          // query heads per attention CTA
+    int att_phased = 1;   // phased attention (k_attn_*), else one CTA per (row, head)
+    int64_t *asc = nullptr, *amx = nullptr;  // phased-attention scratch: scores, maxima
+    uint64_t *asum = nullptr;                // and sums
+    size_t att_s1 = 0, att_s3 = 0;           // its shared-memory sizes
     cudaGraphExec_t graph = nullptr;  // one decode step at batch max_batch
     bool loaded_globals = false;
     std::vector<bool> loaded_layer;
@@ -213,6 +221,9 @@ static int model_alloc(iq_model *m) {
         size_t kmax = std::max((size_t)d, (size_t)c.intermediate_dim);
         size_t kpad = (kmax + TC_BK - 1) / TC_BK * TC_BK, rpad = ((size_t)B + TC_BR - 1) / TC_BR * TC_BR;
         DALLOC(m->digits, rpad * 8 * kpad);
+        // split-K partials: KS * Rpad * Mpad * 16 with KS * tiles <= 2 * SMs + tiles
+        m->gpart_bytes = (size_t)(4 * dev_info().sms + 8) * TC_BM * TC_BR * 16;
+        DALLOC(m->gpart, m->gpart_bytes);
     }
     // pinned ints: [0, B) results, then (max_seq + 2) slots of 2*NB (token, pos)
     IQ_CUDA(cudaMallocHost(&m->h_pin, ((size_t)B + 16 + (size_t)2 * NB * (c.max_seq_len + 2)) * 4));
@@ -266,7 +277,8 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
     auto proj = [&](int64_t *out, const Packed &P, const PackedTC &T, const int64_t *x, int rows,
                     int add) -> int {
         if (rows == 1) return launch_matvec_planes(out, P, x, s, add, m->racc);
-        return launch_gemm_tc(out, T, x, rows, s, add, m->digits);
+        return launch_gemm_tc(out, T, x, rows, s, add, m->digits,
+                              gemm_tc_part_bytes(T, rows) <= m->gpart_bytes ? m->gpart : nullptr);
     };
     k_embed<<<dim3((d + 255) / 256, R), 256, 0, s>>>(m->hidden, m->embed, tok, d);
     IQ_CHECK_LAUNCH();
@@ -280,8 +292,29 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
         k_rope_kv<<<dim3((pairs + 255) / 256, R), 256, 0, s>>>(m->qkv, m->kc[l], m->vc[l], m->rcos, m->rsin,
                                                                pos, seq, S.nh_l, S.nkv_l, hd, c.max_seq_len);
         IQ_CHECK_LAUNCH();
-        k_attention<<<dim3(S.nh_l, R), 256, m->attn_smem, s>>>(att_out, m->qkv, m->kc[l], m->vc[l], pos, seq,
-                                                               S.nh_l, S.nkv_l, hd, c.max_seq_len);
+        if (m->att_phased) {
+            const int grid_t = (c.max_seq_len + ATT_TILE - 1) / ATT_TILE;
+            int64_t n = (int64_t)R * S.nh_l * hd;
+            k_attn_init<<<(int)std::min<int64_t>((n + 255) / 256, 4096), 256, 0, s>>>(att_out, m->amx, m->asum, R,
+                                                                                   S.nh_l, hd);
+            IQ_CHECK_LAUNCH();
+            k_attn_scores<<<dim3(grid_t, S.nkv_l, R), 256, m->att_s1, s>>>(m->asc, m->amx, m->qkv, m->kc[l], pos,
+                                                                            seq, S.nh_l, S.nkv_l, hd, c.max_seq_len,
+                                                                            c.max_seq_len);
+            IQ_CHECK_LAUNCH();
+            k_attn_exp<<<dim3((c.max_seq_len + 255) / 256, S.nh_l, R), 256, 0, s>>>(m->asc, m->amx, m->asum, pos,
+                                                                                   S.nh_l, c.max_seq_len);
+            IQ_CHECK_LAUNCH();
+            k_attn_pv<<<dim3(grid_t, S.nkv_l, R), 256, m->att_s3, s>>>(att_out, m->asc, m->asum, m->vc[l], pos, seq,
+                                                                        S.nh_l, S.nkv_l, hd, c.max_seq_len,
+                                                                        c.max_seq_len);
+        } else if (m->gqa_smem)
+            k_attention_gqa<<<dim3(S.nh_l / m->hpc, R), 256, m->gqa_smem, s>>>(
+                att_out, m->qkv, m->kc[l], m->vc[l], pos, seq, S.nh_l, S.nkv_l, hd, c.max_seq_len, c.max_seq_len,
+                m->hpc);
+        else
+            k_attention<<<dim3(S.nh_l, R), 256, m->attn_smem, s>>>(att_out, m->qkv, m->kc[l], m->vc[l], pos,
+                                                                   seq, S.nh_l, S.nkv_l, hd, c.max_seq_len);
         IQ_CHECK_LAUNCH();
         if (tp) {
             if ((rc = gather_rows(m, m->att_l, m->att, R, S.nh_l * hd))) return rc;
@@ -493,7 +526,35 @@ IQ_API int iq_model_create_tp(const iq_config *cfg, int max_batch, int device, i
             return IQ_ERR_NCCL;
         }
     }
-    if (m->attn_smem > 200 * 1024) { iq_model_destroy(m); return IQ_ERR_UNSUPPORTED; }
+    {
+        static int hpc_env = getenv("IQ_ATT_HPC") ? atoi(getenv("IQ_ATT_HPC")) : 1;
+        int grpl = sh.nh_l / sh.nkv_l;
+        m->hpc = (hpc_env >= 1 && grpl % hpc_env == 0) ? hpc_env : 1;
+        const size_t grp = (size_t)m->hpc;
+        size_t g = (grp * c.head_dim + grp * (size_t)c.max_seq_len + (size_t)ATT_TT * (c.head_dim + 1)) * 8;
+        if (hpc_env >= 1 && g <= 200 * 1024) {
+            e = cudaFuncSetAttribute(k_attention_gqa, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g);
+            if (e != cudaSuccess) { iq_model_destroy(m); return cuda_fail(e); }
+            m->gqa_smem = g;
+        }
+    }
+    {
+        static int att_env = getenv("IQ_ATT") ? atoi(getenv("IQ_ATT")) : 1;
+        const size_t grp = (size_t)sh.nh_l / sh.nkv_l, hd = c.head_dim;
+        m->att_s1 = (grp * hd + (size_t)ATT_TILE * (hd + 1)) * 8;
+        m->att_s3 = (grp * ATT_TILE + (size_t)ATT_TILE * hd) * 8;
+        m->att_phased = att_env == 1 && m->att_s1 <= 200 * 1024 && m->att_s3 <= 200 * 1024;
+        if (m->att_phased) {
+            size_t n = (size_t)m->rmax * sh.nh_l;
+            if ((rc = dalloc((void **)&m->asc, n * c.max_seq_len * 8)) || (rc = dalloc((void **)&m->amx, n * 8)) ||
+                (rc = dalloc((void **)&m->asum, n * 8))) { iq_model_destroy(m); return rc; }
+            e = cudaFuncSetAttribute(k_attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->att_s1);
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(k_attn_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->att_s3);
+            if (e != cudaSuccess) { iq_model_destroy(m); return cuda_fail(e); }
+        }
+    }
+    if (!m->att_phased && !m->gqa_smem && m->attn_smem > 200 * 1024) { iq_model_destroy(m); return IQ_ERR_UNSUPPORTED; }
     if (m->attn_smem > 48 * 1024) {
         e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->attn_smem);
         if (e != cudaSuccess) { iq_model_destroy(m); return cuda_fail(e); }
@@ -518,7 +579,7 @@ IQ_API int iq_model_destroy(iq_model *m) {
     if (m->comm) ncclCommDestroy(m->comm);
     void *bufs[] = {m->embed, m->fnorm, m->lm, m->rcos, m->rsin, m->hidden, m->normed, m->qkv, m->att,
                     m->gu, m->act, m->logits, m->att_l, m->proj_l, m->act_l, m->logits_l, m->gath,
-                    m->proj_full, m->d_tok, m->d_pos, m->d_arg, m->d_hist, m->racc, m->digits, m->d_seq,
+                    m->proj_full, m->d_tok, m->d_pos, m->d_arg, m->d_hist, m->racc, m->digits, m->gpart, m->asc, m->amx, m->asum, m->d_seq,
                     m->d_ptok, m->d_ppos, m->d_pseq};
     for (void *p : bufs) if (p) cudaFree(p);
     for (auto *v : {&m->norm1, &m->wqkv, &m->wo, &m->norm2, &m->wgu, &m->wdown, &m->kc, &m->vc})

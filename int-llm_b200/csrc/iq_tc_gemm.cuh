@@ -62,7 +62,7 @@ __global__ void k_x_digits(uint8_t *__restrict__ out, const int64_t *__restrict_
 __global__ void __launch_bounds__(192, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
           int64_t *__restrict__ out, const int64_t *__restrict__ rowsum, int M, int R, int Mpad, int Kpad,
-          int add) {
+          int add, int64_t *__restrict__ part, int Rpad) {
     extern __shared__ unsigned char smraw[];
     unsigned char *sm = smraw + ((1024 - (smem_u32(smraw) & 1023)) & 1023);  // 1024-aligned stages
     unsigned char *stage = sm;
@@ -74,7 +74,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUte
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * TC_BM, r0 = blockIdx.y * TC_BR;
-    const int KB = Kpad / TC_BK;
+    // split-K: this CTA covers K blocks [kb0, kb0 + KB) of every plane
+    const int KBall = Kpad / TC_BK, KS = gridDim.z, ks = blockIdx.z;
+    const int kb0 = (int)((int64_t)KBall * ks / KS), KB = (int)((int64_t)KBall * (ks + 1) / KS) - kb0;
     const int total = 8 * KB;
 
     if (threadIdx.x == 0) {
@@ -96,8 +98,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUte
                 if (it >= TC_STAGES && !mbar_wait(&empty[s], (uint32_t)((it / TC_STAGES) - 1) & 1u)) break;
                 mbar_expect_tx(&full[s], TC_STAGE_BYTES);
                 unsigned char *a = stage + (size_t)s * TC_STAGE_BYTES;
-                tma_load_2d(a, &mapA, kb * TC_BK, p * Mpad + m0, &full[s]);
-                tma_load_2d(a + TC_A_BYTES, &mapB, kb * TC_BK, r0 * 8, &full[s]);
+                tma_load_2d(a, &mapA, (kb0 + kb) * TC_BK, p * Mpad + m0, &full[s]);
+                tma_load_2d(a + TC_A_BYTES, &mapB, (kb0 + kb) * TC_BK, r0 * 8, &full[s]);
             }
             // drain: the last copies into each stage have landed before the CTA can exit
             for (int j = (it > TC_STAGES ? it - TC_STAGES : 0); j < it; j++)
@@ -153,7 +155,15 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUte
             __syncwarp();
             if (lane == 0) mbar_arrive(&aempty[buf]);
         }
-        if (ok && row < M) {
+        if (ok && KS > 1) {
+            // split-K: store this CTA's 128-bit partial sums; k_gemm_reduce finishes
+#pragma unroll
+            for (int r = 0; r < TC_BR; r++) {
+                int64_t *pp = part + (((size_t)ks * Rpad + r0 + r) * Mpad + row) * 2;
+                pp[0] = (int64_t)(uint64_t)acc[r];
+                pp[1] = (int64_t)(uint64_t)((u128)acc[r] >> 64);
+            }
+        } else if (ok && row < M) {
             const i128 ws = (i128)(((u128)(uint64_t)rowsum[2 * row + 1] << 64) | (uint64_t)rowsum[2 * row]);
             const u128 bias = (u128)ws << 63;
 #pragma unroll
@@ -171,6 +181,25 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUte
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, 512);
+    }
+}
+
+// split-K finish: out[r][m] (+)= low64((sum_ks part[ks][r][m] - 2^63 rowsum[m]) >> 48)
+__global__ void k_gemm_reduce(int64_t *__restrict__ out, const int64_t *__restrict__ part,
+                              const int64_t *__restrict__ rowsum, int M, int R, int Mpad, int Rpad, int KS,
+                              int add) {
+    const int64_t n = (int64_t)R * M;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        const int r = (int)(e / M), m = (int)(e % M);
+        u128 acc = 0;
+        for (int ks = 0; ks < KS; ks++) {
+            const int64_t *pp = part + (((size_t)ks * Rpad + r) * Mpad + m) * 2;
+            acc += ((u128)(uint64_t)pp[1] << 64) | (uint64_t)pp[0];
+        }
+        const u128 ws = ((u128)(uint64_t)rowsum[2 * m + 1] << 64) | (uint64_t)rowsum[2 * m];
+        int64_t v = (int64_t)((i128)(acc - (ws << 63)) >> 48);
+        int64_t *o = out + (size_t)r * M + m;
+        *o = add ? (int64_t)((uint64_t)*o + (uint64_t)v) : v;
     }
 }
 

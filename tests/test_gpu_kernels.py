@@ -232,11 +232,13 @@ def test_matvec_packed_vs_oracle(M, N, dist):
 # ------------------------------------------------------------- tcgen05 GEMM
 
 @pytest.mark.parametrize("rows,M,N", [(2, 5, 7), (31, 64, 129), (33, 130, 1000), (64, 256, 2048),
-                                      (100, 300, 5632), (512, 128, 256)])
+                                      (100, 300, 5632), (512, 128, 256), (512, 2560, 300)])
 @pytest.mark.parametrize("dist", ["full", "cfg"])
 def test_gemm_tc_vs_oracle(rows, M, N, dist):
     """tcgen05 kind::i8 byte-plane GEMM: exact on full-range int64 and on
-    config-distributed inputs; padding of rows (128), x-rows (32) and K (128)."""
+    config-distributed inputs; padding of rows (128), x-rows (32) and K (128);
+    split-K with 128-bit partials (small grids) and the single-pass epilogue
+    (512 x 2560: enough tiles to fill the GPU without splitting)."""
     import torch
     rng = np.random.default_rng(rows * 7 + M + N)
     if dist == "full":
