@@ -26,6 +26,7 @@
 // resident warp; row tiles split between warps meet in RowAcc scratch through
 // exact 128-bit atomics, and the warp that completes a row writes it.
 #pragma once
+#include <cuda/atomic>
 #include "iq_matvec.cuh"
 
 namespace iq {
@@ -164,6 +165,21 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
                 const int64_t *__restrict__ xg, int M, int N, int Kp, int add, RowAcc *__restrict__ racc) {
     extern __shared__ __align__(16) unsigned char xd[];  // [8][Kp + 16] digit rows
     const int ld = Kp + 16;
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int KT = Kp / 32, RT = (M + 15) / 16;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int64_t total = (int64_t)RT * KT;
+    const int64_t u0 = total * gw / nwarps, u1 = total * (gw + 1) / nwarps;
+    // the first weight tile is requested before the x digits are staged, so the
+    // two latencies overlap
+    uint4 pre[8];
+    bool have_pre = u0 < u1;
+    if (have_pre) {
+        const uint4 *tp0 = planes + (size_t)u0 * 256 + lane;
+#pragma unroll
+        for (int p = 0; p < 8; p++) pre[p] = ld_stream_u4(tp0 + p * 32);
+    }
     if (XSMEM) {
         // each thread: 4 consecutive x values -> 8 digit words (one per digit row)
         for (int k = 4 * threadIdx.x; k < Kp; k += 4 * blockDim.x) {
@@ -182,12 +198,6 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
         __syncthreads();
     }
 
-    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int KT = Kp / 32, RT = (M + 15) / 16;
-    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-    const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int64_t total = (int64_t)RT * KT;
-    const int64_t u0 = total * gw / nwarps, u1 = total * (gw + 1) / nwarps;
     const unsigned char *xb = xd + g * ld + 4 * t;
 
     int64_t u = u0;
@@ -206,10 +216,16 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
         for (int kt = k0; kt < k1; kt += UNROLL) {
             uint4 a[UNROLL][8];
 #pragma unroll
-            for (int v = 0; v < UNROLL; v++)
-                if (kt + v < k1)
+            for (int v = 0; v < UNROLL; v++) {
+                if (v == 0 && have_pre) {
+#pragma unroll
+                    for (int p = 0; p < 8; p++) a[0][p] = pre[p];
+                    have_pre = false;
+                } else if (kt + v < k1) {
 #pragma unroll
                     for (int p = 0; p < 8; p++) a[v][p] = ld_stream_u4(tp + (size_t)(kt + v) * 256 + p * 32);
+                }
+            }
 #pragma unroll
             for (int v = 0; v < UNROLL; v++) {
                 if (kt + v < k1) {
@@ -249,10 +265,10 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
                 else {
                     RowAcc *ra = racc + row;
                     atomic_add_i128(ra, part);
-                    __threadfence();
-                    unsigned int prev = atomicAdd(&ra->done, (unsigned int)(k1 - k0));
+                    // release our partial / acquire everyone else's with the counter
+                    cuda::atomic_ref<unsigned int, cuda::thread_scope_device> done(ra->done);
+                    unsigned int prev = done.fetch_add((unsigned int)(k1 - k0), cuda::memory_order_acq_rel);
                     if (prev + (unsigned int)(k1 - k0) == (unsigned int)KT) {
-                        __threadfence();
                         unsigned long long lo = atomicExch(&ra->lo, 0ull);
                         unsigned long long hi = atomicExch(&ra->hi, 0ull);
                         atomicExch(&ra->done, 0u);
