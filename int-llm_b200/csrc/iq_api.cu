@@ -174,7 +174,19 @@ int launch_matvec_planes(int64_t *out, const Packed &P, const int64_t *x, cudaSt
     int64_t need = (units + 7) / 8;
     if (grid > need) grid = need;
     if (grid < 1) grid = 1;
-    kern<<<(int)grid, 256, smem, s>>>(out, P.planes, P.rowsum, x, P.M, P.N, P.Kp, add, racc);
+    // launched with programmatic stream serialisation (see k_matvec_planes)
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    IQ_CUDA(cudaLaunchKernelEx(&cfg, kern, out, (const uint4 *)P.planes, (const int64_t *)P.rowsum, x, P.M, P.N,
+                               P.Kp, add, racc));
     IQ_CHECK_LAUNCH();
     return IQ_OK;
 }

@@ -171,15 +171,19 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
     const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int64_t total = (int64_t)RT * KT;
     const int64_t u0 = total * gw / nwarps, u1 = total * (gw + 1) / nwarps;
-    // the first weight tile is requested before the x digits are staged, so the
-    // two latencies overlap
+    // Programmatic dependent launch: let the next kernel in the stream start its
+    // own prologue now; it waits (griddepcontrol.wait) for this grid's results.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // the first weight tile (static data) is requested before waiting for the
+    // previous kernel and before the x digits are staged, so the latencies overlap
     uint4 pre[8];
-    bool have_pre = u0 < u1;
-    if (have_pre) {
+    if (u0 < u1) {
         const uint4 *tp0 = planes + (size_t)u0 * 256 + lane;
 #pragma unroll
         for (int p = 0; p < 8; p++) pre[p] = ld_stream_u4(tp0 + p * 32);
     }
+    // x and (with add) out are produced by the previous kernel
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (XSMEM) {
         // each thread: 4 consecutive x values -> 8 digit words (one per digit row)
         for (int k = 4 * threadIdx.x; k < Kp; k += 4 * blockDim.x) {
@@ -200,92 +204,91 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
 
     const unsigned char *xb = xd + g * ld + 4 * t;
 
-    int64_t u = u0;
-    while (u < u1) {
-        const int rt = (int)(u / KT);
-        const int k0 = (int)(u - (int64_t)rt * KT);
-        const int k1 = (int)min((int64_t)KT, (int64_t)k0 + (u1 - u));
-        int c[8][4];
+    // Linear walk over this warp's units (row tile-major, the packed layout's
+    // order): the next unit's 8 loads are issued before the current unit's MMAs,
+    // so every warp keeps two 4 KB tiles in flight.
+    int c[8][4];
 #pragma unroll
-        for (int p = 0; p < 8; p++)
+    for (int p = 0; p < 8; p++)
 #pragma unroll
-            for (int q = 0; q < 4; q++) c[p][q] = 0;
-        i128 r0 = 0, r1 = 0;
-        const uint4 *tp = planes + (size_t)rt * KT * 256 + lane;
-        int since_fold = 0;
-        for (int kt = k0; kt < k1; kt += UNROLL) {
-            uint4 a[UNROLL][8];
+        for (int q = 0; q < 4; q++) c[p][q] = 0;
+    i128 r0 = 0, r1 = 0;
+    int since_fold = 0;
+    int rt = (int)(u0 / KT), k0 = (int)(u0 - (int64_t)rt * KT);
+    uint4 cur[8];
 #pragma unroll
-            for (int v = 0; v < UNROLL; v++) {
-                if (v == 0 && have_pre) {
+    for (int p = 0; p < 8; p++) cur[p] = pre[p];
+    for (int64_t u = u0; u < u1; u++) {
+        uint4 nxt[8];
+        if (u + 1 < u1) {
+            const uint4 *tn = planes + (size_t)(u + 1) * 256 + lane;
 #pragma unroll
-                    for (int p = 0; p < 8; p++) a[0][p] = pre[p];
-                    have_pre = false;
-                } else if (kt + v < k1) {
+            for (int p = 0; p < 8; p++) nxt[p] = ld_stream_u4(tn + p * 32);
+        }
+        const int kt = (int)(u - (int64_t)rt * KT);
+        const int kk = kt * 32;
+        uint32_t b0, b1;
+        if (XSMEM) {
+            b0 = *reinterpret_cast<const uint32_t *>(xb + kk);
+            b1 = *reinterpret_cast<const uint32_t *>(xb + kk + 16);
+        } else {
+            b0 = digit_word(xg, N, kk + 4 * t, g);
+            b1 = digit_word(xg, N, kk + 16 + 4 * t, g);
+        }
 #pragma unroll
-                    for (int p = 0; p < 8; p++) a[v][p] = ld_stream_u4(tp + (size_t)(kt + v) * 256 + p * 32);
-                }
+        for (int p = 0; p < 7; p++) mma_i8<false>(c[p], cur[p], b0, b1);
+        mma_i8<true>(c[7], cur[7], b0, b1);
+        if (++since_fold >= 1024) { fold_planes(c, t, r0, r1); since_fold = 0; }
+        const bool seg_end = (u + 1 == u1) || (kt + 1 == KT);
+        if (seg_end) {
+            const int k1 = kt + 1;
+            fold_planes(c, t, r0, r1);
+            since_fold = 0;
+            // the 4 lanes of a row group hold the 8 digits: reduce over t
+#pragma unroll
+            for (int m = 1; m <= 2; m <<= 1) {
+                r0 += shfl_xor_i128(r0, m);
+                r1 += shfl_xor_i128(r1, m);
             }
+            if (t == 0) {
 #pragma unroll
-            for (int v = 0; v < UNROLL; v++) {
-                if (kt + v < k1) {
-                    const int kk = (kt + v) * 32;
-                    uint32_t b0, b1;
-                    if (XSMEM) {
-                        b0 = *reinterpret_cast<const uint32_t *>(xb + kk);
-                        b1 = *reinterpret_cast<const uint32_t *>(xb + kk + 16);
-                    } else {
-                        b0 = digit_word(xg, N, kk + 4 * t, g);
-                        b1 = digit_word(xg, N, kk + 16 + 4 * t, g);
+                for (int h = 0; h < 2; h++) {
+                    const int row = rt * 16 + g + 8 * h;
+                    if (row >= M) continue;
+                    i128 part = h ? r1 : r0;
+                    i128 fin = 0;
+                    bool write = false;
+                    if (k0 == 0 && k1 == KT) { fin = part; write = true; }
+                    else {
+                        RowAcc *ra = racc + row;
+                        atomic_add_i128(ra, part);
+                        // release our partial / acquire everyone else's with the counter
+                        cuda::atomic_ref<unsigned int, cuda::thread_scope_device> done(ra->done);
+                        unsigned int prev = done.fetch_add((unsigned int)(k1 - k0), cuda::memory_order_acq_rel);
+                        if (prev + (unsigned int)(k1 - k0) == (unsigned int)KT) {
+                            unsigned long long lo = atomicExch(&ra->lo, 0ull);
+                            unsigned long long hi = atomicExch(&ra->hi, 0ull);
+                            atomicExch(&ra->done, 0u);
+                            fin = (i128)(((u128)hi << 64) | lo);
+                            write = true;
+                        }
                     }
-#pragma unroll
-                    for (int p = 0; p < 7; p++) mma_i8<false>(c[p], a[v][p], b0, b1);
-                    mma_i8<true>(c[7], a[v][7], b0, b1);
-                }
-            }
-            since_fold += UNROLL;
-            if (since_fold >= 1024) { fold_planes(c, t, r0, r1); since_fold = 0; }
-        }
-        fold_planes(c, t, r0, r1);
-        // the 4 lanes of a row group hold the 8 digits: reduce over t
-#pragma unroll
-        for (int m = 1; m <= 2; m <<= 1) {
-            r0 += shfl_xor_i128(r0, m);
-            r1 += shfl_xor_i128(r1, m);
-        }
-        if (t == 0) {
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const int row = rt * 16 + g + 8 * h;
-                if (row >= M) continue;
-                i128 part = h ? r1 : r0;
-                i128 fin = 0;
-                bool write = false;
-                if (k0 == 0 && k1 == KT) { fin = part; write = true; }
-                else {
-                    RowAcc *ra = racc + row;
-                    atomic_add_i128(ra, part);
-                    // release our partial / acquire everyone else's with the counter
-                    cuda::atomic_ref<unsigned int, cuda::thread_scope_device> done(ra->done);
-                    unsigned int prev = done.fetch_add((unsigned int)(k1 - k0), cuda::memory_order_acq_rel);
-                    if (prev + (unsigned int)(k1 - k0) == (unsigned int)KT) {
-                        unsigned long long lo = atomicExch(&ra->lo, 0ull);
-                        unsigned long long hi = atomicExch(&ra->hi, 0ull);
-                        atomicExch(&ra->done, 0u);
-                        fin = (i128)(((u128)hi << 64) | lo);
-                        write = true;
+                    if (write) {
+                        i128 ws = (i128)(((u128)(uint64_t)rowsum[2 * row + 1] << 64) | (uint64_t)rowsum[2 * row]);
+                        i128 sres = (i128)((u128)fin - ((u128)ws << 63));
+                        // add != 0: residual epilogue out += result (int64 wrap, llama_int.c:1535, 1556)
+                        int64_t val = (int64_t)(sres >> 48);
+                        out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)val) : val;
                     }
                 }
-                if (write) {
-                    i128 ws = (i128)(((u128)(uint64_t)rowsum[2 * row + 1] << 64) | (uint64_t)rowsum[2 * row]);
-                    i128 s = (i128)((u128)fin - ((u128)ws << 63));
-                    // add != 0: residual epilogue out += result (int64 wrap, llama_int.c:1535, 1556)
-                    int64_t val = (int64_t)(s >> 48);
-                    out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)val) : val;
-                }
             }
+            r0 = 0;
+            r1 = 0;
+            rt += 1;
+            k0 = 0;
         }
-        u += k1 - k0;
+#pragma unroll
+        for (int p = 0; p < 8; p++) cur[p] = nxt[p];
     }
 }
 
