@@ -316,7 +316,8 @@ static int stream_bytes(cudaStream_t s, size_t bytes, uint8_t **out) {
 static int gemm_ksplit(const PackedTC &P, int R) {
     const int Rpad = (R + TC_BR - 1) / TC_BR * TC_BR;
     const int tiles = (P.Mpad / TC_BM) * (Rpad / TC_BR), KBall = P.Kpad / TC_BK;
-    int ks = (2 * dev_info().sms + tiles - 1) / tiles;
+    if (tiles >= dev_info().sms) return 1;  // the grid already fills the GPU
+    int ks = (dev_info().sms + tiles - 1) / tiles;
     // each split keeps >= 8 K blocks: the per-plane epilogue fold is a fixed cost
     // per CTA, so thin splits would make it, not the MMAs, the bottleneck
     return std::max(1, std::min(ks, std::min(KBall / 8, 16)));
