@@ -131,11 +131,29 @@ int launch_gemm_add(int64_t *out, const int64_t *W, const int64_t *X, int rows, 
 
 // ------------------------------------------------- byte-plane matvec
 
+// Number of byte planes a matrix needs (1..8), see bytes_needed. Synchronises s.
+static int count_planes(const int64_t *d_w, int64_t n, cudaStream_t s, int *np) {
+    int *d = nullptr;
+    IQ_CUDA(cudaMalloc(&d, sizeof(int)));
+    int one = 1;
+    cudaError_t e = cudaMemcpyAsync(d, &one, sizeof(int), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) {
+        k_plane_count<<<(int)std::min<int64_t>((n + 255) / 256, (int64_t)dev_info().sms * 16), 256, 0, s>>>(d, d_w, n);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(np, d, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    cudaFree(d);
+    return e == cudaSuccess ? IQ_OK : cuda_fail(e);
+}
+
 static int pack_weights(const int64_t *d_w, int M, int N, cudaStream_t s, Packed *P) {
     P->M = M; P->N = N;
     P->Mp = (M + 15) / 16 * 16;
     P->Kp = (N + 31) / 32 * 32;
-    size_t nbytes = (size_t)P->Mp * P->Kp * 8;
+    int rc = count_planes(d_w, (int64_t)M * N, s, &P->np);
+    if (rc) return rc;
+    size_t nbytes = (size_t)P->Mp * P->Kp * P->np;
     IQ_CUDA(cudaMalloc(&P->planes, nbytes));
     cudaError_t e = cudaMalloc(&P->rowsum, (size_t)P->Mp * 16);
     if (e != cudaSuccess) { cudaFree(P->planes); P->planes = nullptr; return cuda_fail(e); }
@@ -143,7 +161,7 @@ static int pack_weights(const int64_t *d_w, int M, int N, cudaStream_t s, Packed
     int64_t total = (int64_t)(P->Mp / 16) * KT * 32;
     int64_t blocks = (total + 255) / 256;
     k_pack_planes<<<(int)std::min<int64_t>(blocks, (int64_t)dev_info().sms * 32), 256, 0, s>>>(
-        P->planes, d_w, M, N, KT, total);
+        P->planes, d_w, M, N, KT, total, P->np);
     IQ_CHECK_LAUNCH();
     k_row_sums<<<std::min(P->Mp / 8 + 1, dev_info().sms * 16), 256, 0, s>>>(P->rowsum, d_w, M, N, P->Mp);
     IQ_CHECK_LAUNCH();
@@ -159,11 +177,26 @@ static void free_packed(Packed *P) {
 
 // racc: RowAcc scratch with >= M zeroed entries (zero again on completion).
 
+typedef void (*PlanesKernel)(int64_t *, const uint4 *, const int64_t *, const int64_t *, int, int, int, int,
+                             RowAcc *);
+template <bool XS>
+static PlanesKernel planes_kernel(int np) {
+    switch (np) {
+    case 1: return k_matvec_planes<1, XS>;
+    case 2: return k_matvec_planes<2, XS>;
+    case 3: return k_matvec_planes<3, XS>;
+    case 4: return k_matvec_planes<4, XS>;
+    case 5: return k_matvec_planes<5, XS>;
+    case 6: return k_matvec_planes<6, XS>;
+    case 7: return k_matvec_planes<7, XS>;
+    default: return k_matvec_planes<8, XS>;
+    }
+}
+
 int launch_matvec_planes(int64_t *out, const Packed &P, const int64_t *x, cudaStream_t s, int add, RowAcc *racc) {
     size_t smem = (size_t)8 * (P.Kp + 16);
     bool xs = smem <= 100 * 1024;
-    // one column tile per loop trip measured fastest (more warps resident)
-    auto kern = xs ? k_matvec_planes<1, true> : k_matvec_planes<1, false>;
+    PlanesKernel kern = xs ? planes_kernel<true>(P.np) : planes_kernel<false>(P.np);
     if (!xs) smem = 0;
     if (smem > 48 * 1024) IQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int occ = 0;
@@ -258,7 +291,7 @@ static int encode_u8_map(CUtensorMap *map, const void *base, uint64_t rows, uint
 }
 
 struct PackedTC {
-    int M = 0, K = 0, Mpad = 0, Kpad = 0;
+    int M = 0, K = 0, Mpad = 0, Kpad = 0, np = 8;
     uint8_t *planes = nullptr;   // [8][Mpad][Kpad]
     int64_t *rowsum = nullptr;   // [Mpad][2]
     CUtensorMap mapA;
@@ -276,16 +309,18 @@ static int pack_weights_tc(const int64_t *d_w, int M, int K, cudaStream_t s, Pac
     P->M = M; P->K = K;
     P->Mpad = (M + TC_BM - 1) / TC_BM * TC_BM;
     P->Kpad = (K + TC_BK - 1) / TC_BK * TC_BK;
+    int rc = count_planes(d_w, (int64_t)M * K, s, &P->np);
+    if (rc) return rc;
     size_t n = (size_t)P->Mpad * P->Kpad;
-    IQ_CUDA(cudaMalloc(&P->planes, 8 * n));
+    IQ_CUDA(cudaMalloc(&P->planes, (size_t)P->np * n));
     cudaError_t e = cudaMalloc(&P->rowsum, (size_t)P->Mpad * 16);
     if (e != cudaSuccess) { free_packed_tc(P); return cuda_fail(e); }
     k_pack_rowplanes<<<(int)std::min<size_t>((n + 255) / 256, (size_t)dev_info().sms * 64), 256, 0, s>>>(
-        P->planes, d_w, M, K, P->Mpad, P->Kpad);
+        P->planes, d_w, M, K, P->Mpad, P->Kpad, P->np);
     IQ_CHECK_LAUNCH();
     k_row_sums<<<std::min(P->Mpad / 8 + 1, dev_info().sms * 16), 256, 0, s>>>(P->rowsum, d_w, M, K, P->Mpad);
     IQ_CHECK_LAUNCH();
-    int rc = encode_u8_map(&P->mapA, P->planes, (uint64_t)8 * P->Mpad, (uint64_t)P->Kpad, TC_BM);
+    rc = encode_u8_map(&P->mapA, P->planes, (uint64_t)P->np * P->Mpad, (uint64_t)P->Kpad, TC_BM);
     if (rc) { free_packed_tc(P); return rc; }
     return IQ_OK;
 }
@@ -345,7 +380,8 @@ int launch_gemm_tc(int64_t *out, const PackedTC &P, const int64_t *X, int R, cud
     IQ_CUDA(cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
     const int ks = part ? gemm_ksplit(P, R) : 1;
     dim3 grid(P.Mpad / TC_BM, Rpad / TC_BR, ks);
-    k_gemm_tc<<<grid, 192, TC_SMEM, s>>>(P.mapA, mapB, out, P.rowsum, P.M, R, P.Mpad, P.Kpad, add, part, Rpad);
+    k_gemm_tc<<<grid, 192, TC_SMEM, s>>>(P.mapA, mapB, out, P.rowsum, P.M, R, P.Mpad, P.Kpad, add, part, Rpad,
+                                         P.np);
     IQ_CHECK_LAUNCH();
     if (ks > 1) {
         int64_t n = (int64_t)R * P.M;

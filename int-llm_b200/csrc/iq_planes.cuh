@@ -14,8 +14,11 @@
 // computed when the weights are packed. out = low64(sum >> 48) exactly as
 // matmul_vec (llama_int.c:1014-1046); every step is exact integer arithmetic.
 //
-// Packed layout (same 8 bytes per weight as the int64 matrix): for each
-// 16-row x 32-column tile, 8 planes x 32 lanes x 16 bytes, where lane l holds
+// Only the np planes the matrix needs are kept (np = the most bytes any weight
+// needs as a signed integer; bf16-derived weights need 6): the top plane is
+// read as signed, the bytes above it being its sign extension.
+// Packed layout (np bytes per weight, 8 for arbitrary int64): for each
+// 16-row x 32-column tile, np planes x 32 lanes x 16 bytes, where lane l holds
 // exactly its A fragment of mma.m16n8k32 (rows l/4 and l/4+8, columns
 // 4(l%4)..+3 and 16+4(l%4)..+3), so one 16-byte load per plane per lane
 // streams the tile. Rows are padded to 16 and columns to 32 with zeros.
@@ -34,6 +37,7 @@ namespace iq {
 struct Packed {
     int M = 0, N = 0;       // logical shape: M rows of N columns
     int Mp = 0, Kp = 0;     // padded to 16 rows / 32 columns
+    int np = 8;             // byte planes stored (top plane signed), see plane_count
     uint4 *planes = nullptr;
     int64_t *rowsum = nullptr;  // [Mp][2] = 128-bit sum_k w[row][k] (lo, hi)
 };
@@ -56,10 +60,27 @@ __device__ __forceinline__ void atomic_add_i128(RowAcc *a, i128 v) {
 
 // ---------------------------------------------------------------- packing
 
+// Bytes needed to hold w as a signed (two's complement) integer, 1..8: the
+// smallest n with -2^(8n-1) <= w < 2^(8n-1). A matrix whose weights all need
+// <= n bytes is exactly sum_{p<n} B_p 2^{8p} with B_{n-1} read as signed (the
+// bytes above it are its sign extension), so only n planes are stored.
+__device__ __forceinline__ int bytes_needed(int64_t w) {
+    uint64_t m = w < 0 ? ~(uint64_t)w : (uint64_t)w;  // magnitude bits below the sign
+    int bits = 64 - __clzll((long long)m) + 1;          // + sign bit
+    return (bits + 7) / 8;
+}
+__global__ void k_plane_count(int *__restrict__ np, const int64_t *__restrict__ W, int64_t n) {
+    int mx = 1;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x)
+        mx = max(mx, bytes_needed(W[e]));
+    for (int m = 16; m >= 1; m >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, m));
+    if ((threadIdx.x & 31) == 0) atomicMax(np, mx);
+}
+
 // One thread per (row tile, column tile, lane): gathers the 16 weights of the
-// lane's A fragment and writes its 16 bytes in each of the 8 planes.
+// lane's A fragment and writes its 16 bytes in each of the np planes.
 __global__ void k_pack_planes(uint4 *__restrict__ planes, const int64_t *__restrict__ W, int M, int N,
-                              int KT, int64_t total) {
+                              int KT, int64_t total, int np) {
     for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
          e += (int64_t)gridDim.x * blockDim.x) {
         const int lane = (int)(e & 31);
@@ -77,9 +98,10 @@ __global__ void k_pack_planes(uint4 *__restrict__ planes, const int64_t *__restr
                 w[r][j] = (row < M && col < N) ? (uint64_t)W[(size_t)row * N + col] : 0ull;
             }
         }
-        uint4 *dst = planes + (size_t)tile * 8 * 32 + lane;
+        uint4 *dst = planes + (size_t)tile * np * 32 + lane;
 #pragma unroll
         for (int p = 0; p < 8; p++) {
+            if (p >= np) break;
             uint32_t v[4];
 #pragma unroll
             for (int r = 0; r < 4; r++) {
@@ -135,9 +157,10 @@ __device__ __forceinline__ void mma_i8(int (&d)[4], const uint4 &a, uint32_t b0,
 
 // Folds the 8 plane accumulators of this lane into its two rows' 128-bit
 // partials: lane (g, t) holds digits 2t, 2t+1 of rows g (c0, c1) and g+8 (c2, c3).
-__device__ __forceinline__ void fold_planes(int (&c)[8][4], int t, i128 &r0, i128 &r1) {
+template <int NP>
+__device__ __forceinline__ void fold_planes(int (&c)[NP][4], int t, i128 &r0, i128 &r1) {
 #pragma unroll
-    for (int p = 0; p < 8; p++) {
+    for (int p = 0; p < NP; p++) {
         const int s0 = 8 * (p + 2 * t);
         r0 += ((i128)c[p][0] << s0) + ((i128)c[p][1] << (s0 + 8));
         r1 += ((i128)c[p][2] << s0) + ((i128)c[p][3] << (s0 + 8));
@@ -159,7 +182,7 @@ __device__ __forceinline__ uint32_t digit_word(const int64_t *__restrict__ xg, i
 
 // XSMEM: digits staged in shared memory (Kp small enough), else gathered from
 // x in global memory (L1-cached) per column tile.
-template <int UNROLL, bool XSMEM>
+template <int NP, bool XSMEM>
 __global__ void __launch_bounds__(256, 2)
 k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const int64_t *__restrict__ rowsum,
                 const int64_t *__restrict__ xg, int M, int N, int Kp, int add, RowAcc *__restrict__ racc) {
@@ -176,11 +199,12 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // the first weight tile (static data) is requested before waiting for the
     // previous kernel and before the x digits are staged, so the latencies overlap
-    uint4 pre[8];
+    constexpr int TS = NP * 32;  // uint4 per packed tile
+    uint4 pre[NP];
     if (u0 < u1) {
-        const uint4 *tp0 = planes + (size_t)u0 * 256 + lane;
+        const uint4 *tp0 = planes + (size_t)u0 * TS + lane;
 #pragma unroll
-        for (int p = 0; p < 8; p++) pre[p] = ld_stream_u4(tp0 + p * 32);
+        for (int p = 0; p < NP; p++) pre[p] = ld_stream_u4(tp0 + p * 32);
     }
     // x and (with add) out are produced by the previous kernel
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -207,23 +231,23 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
     // Linear walk over this warp's units (row tile-major, the packed layout's
     // order): the next unit's 8 loads are issued before the current unit's MMAs,
     // so every warp keeps two 4 KB tiles in flight.
-    int c[8][4];
+    int c[NP][4];
 #pragma unroll
-    for (int p = 0; p < 8; p++)
+    for (int p = 0; p < NP; p++)
 #pragma unroll
         for (int q = 0; q < 4; q++) c[p][q] = 0;
     i128 r0 = 0, r1 = 0;
     int since_fold = 0;
     int rt = (int)(u0 / KT), k0 = (int)(u0 - (int64_t)rt * KT);
-    uint4 cur[8];
+    uint4 cur[NP];
 #pragma unroll
-    for (int p = 0; p < 8; p++) cur[p] = pre[p];
+    for (int p = 0; p < NP; p++) cur[p] = pre[p];
     for (int64_t u = u0; u < u1; u++) {
-        uint4 nxt[8];
+        uint4 nxt[NP];
         if (u + 1 < u1) {
-            const uint4 *tn = planes + (size_t)(u + 1) * 256 + lane;
+            const uint4 *tn = planes + (size_t)(u + 1) * TS + lane;
 #pragma unroll
-            for (int p = 0; p < 8; p++) nxt[p] = ld_stream_u4(tn + p * 32);
+            for (int p = 0; p < NP; p++) nxt[p] = ld_stream_u4(tn + p * 32);
         }
         const int kt = (int)(u - (int64_t)rt * KT);
         const int kk = kt * 32;
@@ -236,8 +260,8 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
             b1 = digit_word(xg, N, kk + 16 + 4 * t, g);
         }
 #pragma unroll
-        for (int p = 0; p < 7; p++) mma_i8<false>(c[p], cur[p], b0, b1);
-        mma_i8<true>(c[7], cur[7], b0, b1);
+        for (int p = 0; p < NP - 1; p++) mma_i8<false>(c[p], cur[p], b0, b1);
+        mma_i8<true>(c[NP - 1], cur[NP - 1], b0, b1);  // top plane: signed
         if (++since_fold >= 1024) { fold_planes(c, t, r0, r1); since_fold = 0; }
         const bool seg_end = (u + 1 == u1) || (kt + 1 == KT);
         if (seg_end) {
@@ -288,7 +312,7 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
             k0 = 0;
         }
 #pragma unroll
-        for (int p = 0; p < 8; p++) cur[p] = nxt[p];
+        for (int p = 0; p < NP; p++) cur[p] = nxt[p];
     }
 }
 

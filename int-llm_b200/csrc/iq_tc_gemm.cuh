@@ -6,6 +6,8 @@
 // and the unsigned digits D_j of x_u = x + 2^63,
 //   out[r][i] = low64( (sum_{p,j} 2^{8(p+j)} P_pj[r][i] - 2^63 sum_k W[i][k]) >> 48 )
 //   P_pj[r][i] = sum_k B_p(W[i][k]) * D_j(x_u[r][k])       (exact int32)
+// Only the np planes the weights need are stored (see bytes_needed in
+// iq_planes.cuh; the top stored plane is the signed one).
 // For plane p the products for all digits are one GEMM: A = plane p of W
 // ([Mpad][Kpad] bytes, K-major) times B = the digit matrix
 // ([(row, digit)][Kpad] bytes, K-major, row = 8*r + j), so the MMA's N
@@ -35,15 +37,14 @@ constexpr int TC_B_BYTES = TC_BR * 8 * TC_BK;        // 32 KB
 constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
 constexpr size_t TC_SMEM = 1024 + (size_t)TC_STAGES * TC_STAGE_BYTES + 256;
 
-// W [M][K] int64 -> planes [8][Mpad][Kpad] bytes (zero padded)
+// W [M][K] int64 -> planes [np][Mpad][Kpad] bytes (zero padded; top plane signed)
 __global__ void k_pack_rowplanes(uint8_t *__restrict__ out, const int64_t *__restrict__ W, int M, int K,
-                                 int Mpad, int Kpad) {
+                                 int Mpad, int Kpad, int np) {
     const int64_t n = (int64_t)Mpad * Kpad;
     for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
         int m = (int)(e / Kpad), k = (int)(e % Kpad);
         uint64_t w = (m < M && k < K) ? (uint64_t)W[(size_t)m * K + k] : 0ull;
-#pragma unroll
-        for (int p = 0; p < 8; p++) out[(size_t)p * n + e] = (uint8_t)(w >> (8 * p));
+        for (int p = 0; p < np; p++) out[(size_t)p * n + e] = (uint8_t)(w >> (8 * p));
     }
 }
 
@@ -62,7 +63,7 @@ __global__ void k_x_digits(uint8_t *__restrict__ out, const int64_t *__restrict_
 __global__ void __launch_bounds__(192, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
           int64_t *__restrict__ out, const int64_t *__restrict__ rowsum, int M, int R, int Mpad, int Kpad,
-          int add, int64_t *__restrict__ part, int Rpad) {
+          int add, int64_t *__restrict__ part, int Rpad, int np) {
     extern __shared__ unsigned char smraw[];
     unsigned char *sm = smraw + ((1024 - (smem_u32(smraw) & 1023)) & 1023);  // 1024-aligned stages
     unsigned char *stage = sm;
@@ -77,7 +78,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUte
     // split-K: this CTA covers K blocks [kb0, kb0 + KB) of every plane
     const int KBall = Kpad / TC_BK, KS = gridDim.z, ks = blockIdx.z;
     const int kb0 = (int)((int64_t)KBall * ks / KS), KB = (int)((int64_t)KBall * (ks + 1) / KS) - kb0;
-    const int total = 8 * KB;
+    const int total = np * KB;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < TC_STAGES; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
@@ -108,11 +109,11 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUte
     } else if (warp == 1) {
         if (lane == 0) {
             bool ok = true;
-            for (int p = 0; p < 8 && ok; p++) {
+            for (int p = 0; p < np && ok; p++) {
                 const int buf = p & 1;
                 if (p >= 2 && !mbar_wait(&aempty[buf], (uint32_t)((p / 2) - 1) & 1u)) break;
                 tc_fence_after();
-                const uint32_t idesc = idesc_i8(p == 7, false, TC_BM, TC_BR * 8);
+                const uint32_t idesc = idesc_i8(p == np - 1, false, TC_BM, TC_BR * 8);  // top plane signed
                 const uint32_t d = tmem + (uint32_t)(buf * 256);
                 for (int kb = 0; kb < KB; kb++) {
                     const int it = p * KB + kb, s = it % TC_STAGES;
@@ -136,7 +137,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUte
 #pragma unroll
         for (int r = 0; r < TC_BR; r++) acc[r] = 0;
         bool ok = true;
-        for (int p = 0; p < 8 && ok; p++) {
+        for (int p = 0; p < np && ok; p++) {
             const int buf = p & 1;
             if (!mbar_wait(&afull[buf], (uint32_t)(p / 2) & 1u)) { ok = false; break; }
             tc_fence_after();

@@ -254,3 +254,32 @@ def test_gemm_tc_vs_oracle(rows, M, N, dist):
     assert iq.device_status() == 0
     assert (got == want).all()
     pk.free()
+
+
+def _weights_with_planes(rng, n, shape):
+    """int64 weights that need exactly n bytes as signed integers, boundaries included."""
+    lo, hi = -(1 << (8 * n - 1)), (1 << (8 * n - 1)) - 1
+    w = rng.integers(lo, hi, shape, dtype=np.int64, endpoint=True)
+    flat = w.reshape(-1)
+    flat[0], flat[-1] = lo, hi
+    return w
+
+
+@pytest.mark.parametrize("n", list(range(1, 9)))
+def test_plane_count_matvec_and_gemm(n):
+    """Packing keeps only the byte planes the weights need (top one signed);
+    results stay exact for every plane count, at the signed range boundaries."""
+    import torch
+    rng = np.random.default_rng(100 + n)
+    M, N, rows = 37, 1000, 5
+    w = _weights_with_planes(rng, n, (M, N))
+    x, X = rand_full(rng, (N,)), rand_full(rng, (rows, N))
+    pk = iq.Packed(dev(w), M, N)
+    do = torch.zeros(M, dtype=torch.int64, device="cuda")
+    iq.matvec_packed_dev(do, pk, dev(x))
+    assert (host(do) == orc.matmul_vec(w, x)).all()
+    pt = iq.PackedTC(dev(w), M, N)
+    dg = torch.zeros((rows, M), dtype=torch.int64, device="cuda")
+    iq.gemm_tc_dev(dg, pt, dev(X), rows)
+    assert (host(dg) == orc.matmul_rows(w, X)).all()
+    pk.free(); pt.free()
