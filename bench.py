@@ -322,7 +322,11 @@ def run_ours(args):
                           for (K, N), t in zip(SHAPES, per_shape_ms)},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)",
-                     "kernel": "k_matvec" if raw else "k_matvec_planes", "traffic": traffic},
+                     "kernel": "k_matvec" if raw else "k_matvec_planes", "traffic": traffic,
+                     "note": "achieved = algorithmic int64 bytes 8*(K*N+K+N) per step / step time; the packed "
+                             "format stores only the byte planes the weights need (6 of 8 here), so DRAM "
+                             "traffic per step is ~0.75x the algorithmic bytes",
+                     "dram_gbs": (traffic / (ms_total / args.steps / 1e3) / 1e9) if traffic else None},
         "e2e": {"value": MACS_PER_STEP * e2e_steps * world / e2e_s / 1e9, "unit": UNIT,
                 "h2d_bytes_per_step": sum(8 * K for K, N in SHAPES),
                 "d2h_bytes_per_step": sum(8 * N for K, N in SHAPES),
