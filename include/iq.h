@@ -221,6 +221,13 @@ IQ_API int iq_generate_batch(iq_model *m, const int *prompts, int prompt_len, in
  * stream). The cache must hold valid entries below pos0. */
 IQ_API int iq_decode_steps_timed(iq_model *m, int pos0, int steps, float *ms);
 
+/* Attention kernel choice (no reference counterpart: the arithmetic is the same
+ * either way). Decode steps whose context length T = pos + 1 is at most
+ * short_max use one CTA per (row, head); longer ones use the phased kernels
+ * (tiles of 64 positions). 0 = always phased. Returns IQ_ERR_UNSUPPORTED if
+ * the single-kernel form does not fit shared memory at this max_seq_len. */
+IQ_API int iq_model_set_attention(iq_model *m, int short_max);
+
 /* ------------------------------------------------ synthetic inputs (host) */
 
 /* Seeded inputs of the synthetic benchmark configurations. No reference

@@ -178,7 +178,7 @@ static void free_packed(Packed *P) {
 // racc: RowAcc scratch with >= M zeroed entries (zero again on completion).
 
 typedef void (*PlanesKernel)(int64_t *, const uint4 *, const int64_t *, const int64_t *, int, int, int, int,
-                             RowAcc *);
+                             RowAcc *, const int64_t *);
 template <bool XS>
 static PlanesKernel planes_kernel(int np) {
     switch (np) {
@@ -193,9 +193,13 @@ static PlanesKernel planes_kernel(int np) {
     }
 }
 
-int launch_matvec_planes(int64_t *out, const Packed &P, const int64_t *x, cudaStream_t s, int add, RowAcc *racc) {
+// nrm_w != nullptr: x is un-normalised and rmsnorm with weights nrm_w is fused
+// into the digit staging; returns IQ_ERR_UNSUPPORTED if x is too long to stage.
+int launch_matvec_planes(int64_t *out, const Packed &P, const int64_t *x, cudaStream_t s, int add, RowAcc *racc,
+                         const int64_t *nrm_w = nullptr) {
     size_t smem = (size_t)8 * (P.Kp + 16);
     bool xs = smem <= 100 * 1024;
+    if (nrm_w && !xs) return IQ_ERR_UNSUPPORTED;
     PlanesKernel kern = xs ? planes_kernel<true>(P.np) : planes_kernel<false>(P.np);
     if (!xs) smem = 0;
     if (smem > 48 * 1024) IQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -219,7 +223,7 @@ int launch_matvec_planes(int64_t *out, const Packed &P, const int64_t *x, cudaSt
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     IQ_CUDA(cudaLaunchKernelEx(&cfg, kern, out, (const uint4 *)P.planes, (const int64_t *)P.rowsum, x, P.M, P.N,
-                               P.Kp, add, racc));
+                               P.Kp, add, racc, nrm_w));
     IQ_CHECK_LAUNCH();
     return IQ_OK;
 }

@@ -88,11 +88,22 @@ __global__ void k_attention(int64_t *__restrict__ out, const int64_t *__restrict
     const int sq = seq_arr[b];
     const int64_t *kb = kc + (size_t)sq * max_seq * kvd + kvh * hd;
     const int64_t *vb = vc + (size_t)sq * max_seq * kvd + kvh * hd;
-    for (int t = threadIdx.x; t < T; t += blockDim.x) {
-        const int64_t *kt = kb + (size_t)t * kvd;
-        i128 dot = 0;
-        for (int d = 0; d < hd; d++) dot += d_mul128(qs[d], kt[d]);
-        sc[t] = d_mul((int64_t)(dot >> 48), scale);
+    // scores: groups of 8 lanes share one position and split its dims, so a
+    // warp reads four key rows in 64-byte coalesced pieces; the int128 partial
+    // dots combine exactly (addition mod 2^128)
+    {
+        const int sl = threadIdx.x & 7, nsg = blockDim.x >> 3;
+        for (int tb = 0; tb < T; tb += nsg) {  // uniform trip count: every lane shuffles
+            const int t0 = tb + (threadIdx.x >> 3);
+            const bool act = t0 < T;
+            const int64_t *kt = kb + (size_t)(act ? t0 : 0) * kvd;
+            i128 dot = 0;
+            if (act)
+                for (int d = sl; d < hd; d += 8) dot += d_mul128(qs[d], kt[d]);
+#pragma unroll
+            for (int m = 4; m >= 1; m >>= 1) dot += shfl_xor_i128(dot, m);
+            if (act && sl == 0) sc[t0] = d_mul((int64_t)(dot >> 48), scale);
+        }
     }
     __syncthreads();
     cta_softmax(sc, T, red);

@@ -98,7 +98,9 @@ struct iq_model {
     int64_t *asc = nullptr, *amx = nullptr;  // phased-attention scratch: scores, maxima
     uint64_t *asum = nullptr;                // and sums
     size_t att_s1 = 0, att_s3 = 0;           // its shared-memory sizes
-    cudaGraphExec_t graph = nullptr;  // one decode step at batch max_batch
+    cudaGraphExec_t graph = nullptr;    // one decode step at batch max_batch (phased attention)
+    cudaGraphExec_t graph_s = nullptr;  // the same step with single-kernel attention
+    int att_short = 0;  // steps whose positions all lie below this use k_attention
     bool loaded_globals = false;
     std::vector<bool> loaded_layer;
 };
@@ -267,7 +269,10 @@ static int add_into(iq_model *m, int64_t *x, const int64_t *y, int64_t n) {
 // lm: 0 = LM head on every row (logits [R][V]); 1 = only the last row (prefill
 // sampling, logits [1][V]); 2 = no LM head (an inner prefill chunk). decode != 0: argmax advances d_tok / d_pos and
 // records the token in d_hist.
-static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, const int *seq, int lm, int decode) {
+// tmax: a host-known bound on pos[r] + 1 over the rows (0 = unknown); short
+// contexts (tmax <= att_short) take the single-kernel attention.
+static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, const int *seq, int lm, int decode,
+                        int tmax = 0) {
     const iq_config &c = m->c;
     const Shard &S = m->sh;
     const bool tp = S.P > 1;
@@ -280,19 +285,29 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
         return launch_gemm_tc(out, T, x, rows, s, add, m->digits,
                               gemm_tc_part_bytes(T, rows) <= m->gpart_bytes ? m->gpart : nullptr);
     };
+    // rmsnorm(x, nw) followed by a projection. A single row goes through the
+    // packed matvec with the norm fused into its digit staging (each CTA
+    // normalises x itself); several rows are normalised once into m->normed.
+    auto norm_proj = [&](int64_t *out, const Packed &P, const PackedTC &T, const int64_t *x, const int64_t *nw,
+                         int rows) -> int {
+        if (rows == 1 && (size_t)8 * (P.Kp + 16) <= 100 * 1024)
+            return launch_matvec_planes(out, P, x, s, 0, m->racc, nw);
+        k_rmsnorm<<<rows, 256, 0, s>>>(m->normed, x, nw, d);
+        IQ_CHECK_LAUNCH();
+        return proj(out, P, T, m->normed, rows, 0);
+    };
     k_embed<<<dim3((d + 255) / 256, R), 256, 0, s>>>(m->hidden, m->embed, tok, d);
     IQ_CHECK_LAUNCH();
     const int pairs = (S.nh_l + S.nkv_l) * (hd / 2) + m->kvd_l;
     int64_t *att_out = tp ? m->att_l : m->att;
     int64_t *act_out = tp ? m->act_l : m->act;
     for (int l = 0; l < c.num_layers; l++) {
-        k_rmsnorm<<<R, 256, 0, s>>>(m->normed, m->hidden, m->norm1[l], d);
-        IQ_CHECK_LAUNCH();
-        if ((rc = proj(m->qkv, m->pqkv[l], m->tqkv[l], m->normed, R, 0))) return rc;
+        if ((rc = norm_proj(m->qkv, m->pqkv[l], m->tqkv[l], m->hidden, m->norm1[l], R))) return rc;
         k_rope_kv<<<dim3((pairs + 255) / 256, R), 256, 0, s>>>(m->qkv, m->kc[l], m->vc[l], m->rcos, m->rsin,
                                                                pos, seq, S.nh_l, S.nkv_l, hd, c.max_seq_len);
         IQ_CHECK_LAUNCH();
-        if (m->att_phased) {
+        const bool att_short = tmax > 0 && tmax <= m->att_short;
+        if (m->att_phased && !att_short) {
             const int grid_t = (c.max_seq_len + ATT_TILE - 1) / ATT_TILE;
             int64_t n = (int64_t)R * S.nh_l * hd;
             k_attn_init<<<(int)std::min<int64_t>((n + 255) / 256, 4096), 256, 0, s>>>(att_out, m->amx, m->asum, R,
@@ -308,7 +323,7 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
             k_attn_pv<<<dim3(grid_t, S.nkv_l, R), 256, m->att_s3, s>>>(att_out, m->asc, m->asum, m->vc[l], pos, seq,
                                                                         S.nh_l, S.nkv_l, hd, c.max_seq_len,
                                                                         c.max_seq_len);
-        } else if (m->gqa_smem)
+        } else if (m->gqa_smem && !att_short)
             k_attention_gqa<<<dim3(S.nh_l / m->hpc, R), 256, m->gqa_smem, s>>>(
                 att_out, m->qkv, m->kc[l], m->vc[l], pos, seq, S.nh_l, S.nkv_l, hd, c.max_seq_len, c.max_seq_len,
                 m->hpc);
@@ -324,9 +339,7 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
         } else if ((rc = proj(m->hidden, m->po[l], m->to[l], m->att, R, 1))) {
             return rc;
         }
-        k_rmsnorm<<<R, 256, 0, s>>>(m->normed, m->hidden, m->norm2[l], d);
-        IQ_CHECK_LAUNCH();
-        if ((rc = proj(m->gu, m->pgu[l], m->tgu[l], m->normed, R, 0))) return rc;
+        if ((rc = norm_proj(m->gu, m->pgu[l], m->tgu[l], m->hidden, m->norm2[l], R))) return rc;
         k_swiglu<<<(R * S.it_l + 255) / 256, 256, 0, s>>>(act_out, m->gu, S.it_l, R);
         IQ_CHECK_LAUNCH();
         if (tp) {
@@ -340,13 +353,11 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
     }
     if (lm == 2) return IQ_OK;                                  // no LM head wanted
     const int LR = lm ? 1 : R;                                  // rows through the LM head
-    const int64_t *fin = m->normed + (size_t)(R - LR) * d;
-    k_rmsnorm<<<R, 256, 0, s>>>(m->normed, m->hidden, m->fnorm, d);
-    IQ_CHECK_LAUNCH();
+    const int64_t *fin = m->hidden + (size_t)(R - LR) * d;   // the rows the LM head reads
     if (tp) {
-        if ((rc = proj(m->logits_l, m->plm, m->tlm, fin, LR, 0))) return rc;
+        if ((rc = norm_proj(m->logits_l, m->plm, m->tlm, fin, m->fnorm, LR))) return rc;
         if ((rc = gather_rows(m, m->logits_l, m->logits, LR, S.v_l))) return rc;
-    } else if ((rc = proj(m->logits, m->plm, m->tlm, fin, LR, 0))) {
+    } else if ((rc = norm_proj(m->logits, m->plm, m->tlm, fin, m->fnorm, LR))) {
         return rc;
     }
     if (decode) {
@@ -360,19 +371,25 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
     return IQ_OK;
 }
 
-static int enqueue_step(iq_model *m, int B) {
-    return enqueue_rows(m, B, m->d_tok, m->d_pos, m->d_seq, 0, 1);
+static int enqueue_step(iq_model *m, int B, int tmax) {
+    return enqueue_rows(m, B, m->d_tok, m->d_pos, m->d_seq, 0, 1, tmax);
 }
 
-static int ensure_graph(iq_model *m) {
-    if (m->graph) return IQ_OK;
+// the decode-step graph for contexts up to tmax (0 = any length)
+static cudaGraphExec_t &step_graph(iq_model *m, int tmax) {
+    return tmax > 0 && tmax <= m->att_short ? m->graph_s : m->graph;
+}
+static int ensure_graph(iq_model *m, int tmax) {
+    cudaGraphExec_t &gx = step_graph(m, tmax);
+    if (gx) return IQ_OK;
+    const int tcap = tmax > 0 && tmax <= m->att_short ? m->att_short : 0;
     cudaGraph_t g;
     IQ_CUDA(cudaStreamBeginCapture(m->s, cudaStreamCaptureModeThreadLocal));
-    int rc = enqueue_step(m, m->max_batch);
+    int rc = enqueue_step(m, m->max_batch, tcap);
     cudaError_t e = cudaStreamEndCapture(m->s, &g);
     if (rc) { if (e == cudaSuccess) cudaGraphDestroy(g); return rc; }
     if (e != cudaSuccess) return cuda_fail(e);
-    e = cudaGraphInstantiate(&m->graph, g, 0);
+    e = cudaGraphInstantiate(&gx, g, 0);
     cudaGraphDestroy(g);
     if (e != cudaSuccess) return cuda_fail(e);
     return IQ_OK;
@@ -555,9 +572,15 @@ IQ_API int iq_model_create_tp(const iq_config *cfg, int max_batch, int device, i
         }
     }
     if (!m->att_phased && !m->gqa_smem && m->attn_smem > 200 * 1024) { iq_model_destroy(m); return IQ_ERR_UNSUPPORTED; }
-    if (m->attn_smem > 48 * 1024) {
+    if (m->attn_smem > 48 * 1024 && m->attn_smem <= 200 * 1024) {
         e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->attn_smem);
         if (e != cudaSuccess) { iq_model_destroy(m); return cuda_fail(e); }
+    }
+    {
+        // contexts up to this length use one CTA per (row, head): fewer launches
+        // than the phased kernels and enough parallelism while T is short
+        static int short_env = getenv("IQ_ATT_SHORT") ? atoi(getenv("IQ_ATT_SHORT")) : 384;
+        m->att_short = m->attn_smem <= 200 * 1024 ? short_env : 0;
     }
     k_rope_init<<<256, 128, 0, m->s>>>(m->rcos, m->rsin, c.head_dim, c.max_seq_len, c.rope_theta);
     e = cudaStreamSynchronize(m->s);
@@ -576,6 +599,7 @@ IQ_API int iq_model_destroy(iq_model *m) {
     cudaSetDevice(m->dev);
     if (m->s) cudaStreamSynchronize(m->s);
     if (m->graph) cudaGraphExecDestroy(m->graph);
+    if (m->graph_s) cudaGraphExecDestroy(m->graph_s);
     if (m->comm) ncclCommDestroy(m->comm);
     void *bufs[] = {m->embed, m->fnorm, m->lm, m->rcos, m->rsin, m->hidden, m->normed, m->qkv, m->att,
                     m->gu, m->act, m->logits, m->att_l, m->proj_l, m->act_l, m->logits_l, m->gath,
@@ -740,7 +764,7 @@ IQ_API int iq_forward(iq_model *m, int token, int pos, int64_t *logits, int *arg
     IQ_CUDA(cudaMemcpyAsync(m->d_ptok, h, 4, cudaMemcpyHostToDevice, m->s));
     IQ_CUDA(cudaMemcpyAsync(m->d_ppos, h + 1, 4, cudaMemcpyHostToDevice, m->s));
     IQ_CUDA(cudaMemcpyAsync(m->d_pseq, h + 2, 4, cudaMemcpyHostToDevice, m->s));
-    if ((rc = enqueue_rows(m, 1, m->d_ptok, m->d_ppos, m->d_pseq, 0, 0))) return rc;
+    if ((rc = enqueue_rows(m, 1, m->d_ptok, m->d_ppos, m->d_pseq, 0, 0, pos + 1))) return rc;
     if (logits) IQ_CUDA(cudaMemcpyAsync(m->h_logits, m->logits, (size_t)m->c.vocab_size * 8, cudaMemcpyDeviceToHost, m->s));
     IQ_CUDA(cudaMemcpyAsync(m->h_pin, m->d_arg, 4, cudaMemcpyDeviceToHost, m->s));
     IQ_CUDA(cudaStreamSynchronize(m->s));
@@ -757,15 +781,16 @@ static uint64_t fnv_mix(uint64_t h, const int64_t *v, size_t n) {
     return h;
 }
 
-// one step for B sequences: the captured graph when B == max_batch
-static int run_step(iq_model *m, int B) {
+// one step for B sequences whose positions are all below tmax: a captured
+// graph when B == max_batch
+static int run_step(iq_model *m, int B, int tmax) {
     if (B == m->max_batch) {
-        int rc = ensure_graph(m);
+        int rc = ensure_graph(m, tmax);
         if (rc) return rc;
-        IQ_CUDA(cudaGraphLaunch(m->graph, m->s));
+        IQ_CUDA(cudaGraphLaunch(step_graph(m, tmax), m->s));
         return IQ_OK;
     }
-    return enqueue_step(m, B);
+    return enqueue_step(m, B, tmax);
 }
 
 IQ_API int iq_generate(iq_model *m, const int *prompt, int plen, int max_new, int *out, int *n_out,
@@ -795,7 +820,7 @@ IQ_API int iq_generate(iq_model *m, const int *prompt, int plen, int max_new, in
         IQ_CUDA(cudaStreamSynchronize(m->s));
         out[total++] = m->h_pin[0];  // prefill's sample is appended unconditionally
         for (int i = 1; i <= steps; i++) {
-            if ((rc = run_step(m, 1))) return rc;  // d_tok / d_pos advanced on the device
+            if ((rc = run_step(m, 1, plen + i))) return rc;  // d_tok / d_pos advanced on the device
             IQ_CUDA(cudaMemcpyAsync(m->h_logits, m->logits, (size_t)V * 8, cudaMemcpyDeviceToHost, m->s));
             IQ_CUDA(cudaMemcpyAsync(m->h_pin, m->d_arg, 4, cudaMemcpyDeviceToHost, m->s));
             IQ_CUDA(cudaStreamSynchronize(m->s));
@@ -807,7 +832,7 @@ IQ_API int iq_generate(iq_model *m, const int *prompt, int plen, int max_new, in
         *logit_hash = h;
     } else {
         for (int i = 1; i <= steps; i++)
-            if ((rc = run_step(m, 1))) return rc;
+            if ((rc = run_step(m, 1, plen + i))) return rc;
         std::vector<int> hist(steps + 1);
         IQ_CUDA(cudaMemcpyAsync(hist.data(), m->d_hist + plen, (size_t)(steps + 1) * 4, cudaMemcpyDeviceToHost, m->s));
         IQ_CUDA(cudaStreamSynchronize(m->s));
@@ -835,7 +860,7 @@ IQ_API int iq_generate_batch(iq_model *m, const int *prompts, int plen, int max_
         if ((rc = enqueue_prefill(m, b, prompts + (size_t)b * plen, plen, nullptr))) return rc;
     const int steps = std::min(max_new - 1, c.max_seq_len - plen);
     for (int i = 1; i <= steps; i++)
-        if ((rc = run_step(m, B))) return rc;
+        if ((rc = run_step(m, B, plen + i))) return rc;
     const int stride = c.max_seq_len + 1;
     std::vector<int> hist((size_t)B * stride);
     IQ_CUDA(cudaMemcpyAsync(hist.data(), m->d_hist, hist.size() * 4, cudaMemcpyDeviceToHost, m->s));
@@ -856,6 +881,16 @@ IQ_API int iq_generate_batch(iq_model *m, const int *prompts, int plen, int max_
     return take_dev_error();
 }
 
+IQ_API int iq_model_set_attention(iq_model *m, int short_max) {
+    if (!m || short_max < 0) return IQ_ERR_ARG;
+    if (short_max > 0 && m->attn_smem > 200 * 1024) return IQ_ERR_UNSUPPORTED;
+    IQ_CUDA(cudaSetDevice(m->dev));
+    IQ_CUDA(cudaStreamSynchronize(m->s));
+    if (m->graph_s) { cudaGraphExecDestroy(m->graph_s); m->graph_s = nullptr; }
+    m->att_short = short_max;
+    return IQ_OK;
+}
+
 IQ_API int iq_decode_steps_timed(iq_model *m, int pos0, int steps, float *ms) {
     if (!m || !ms || steps < 1 || pos0 < 0 || pos0 + steps > m->c.max_seq_len) return IQ_ERR_ARG;
     if (!model_ready(m)) return IQ_ERR_STATE;
@@ -865,12 +900,12 @@ IQ_API int iq_decode_steps_timed(iq_model *m, int pos0, int steps, float *ms) {
     IQ_CUDA(cudaStreamSynchronize(m->s));
     IQ_CUDA(cudaMemcpy(tok.data(), m->d_tok, tok.size() * 4, cudaMemcpyDeviceToHost));
     if ((rc = set_tok_pos(m, tok.data(), pos.data(), m->max_batch, 0))) return rc;
-    if ((rc = ensure_graph(m))) return rc;
+    if ((rc = ensure_graph(m, pos0 + 1)) || (rc = ensure_graph(m, pos0 + steps))) return rc;
     cudaEvent_t e0, e1;
     IQ_CUDA(cudaEventCreate(&e0));
     IQ_CUDA(cudaEventCreate(&e1));
     IQ_CUDA(cudaEventRecord(e0, m->s));
-    for (int i = 0; i < steps; i++) IQ_CUDA(cudaGraphLaunch(m->graph, m->s));
+    for (int i = 0; i < steps; i++) IQ_CUDA(cudaGraphLaunch(step_graph(m, pos0 + i + 1), m->s));
     IQ_CUDA(cudaEventRecord(e1, m->s));
     IQ_CUDA(cudaEventSynchronize(e1));
     IQ_CUDA(cudaEventElapsedTime(ms, e0, e1));

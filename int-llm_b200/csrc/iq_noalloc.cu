@@ -23,7 +23,8 @@ namespace iq {
 
 static __device__ __align__(256) RowAcc g_noalloc_rows[IQ_NOALLOC_MAX_ROWS];
 
-int launch_matvec_planes(int64_t *out, const Packed &P, const int64_t *x, cudaStream_t s, int add, RowAcc *racc);
+int launch_matvec_planes(int64_t *out, const Packed &P, const int64_t *x, cudaStream_t s, int add, RowAcc *racc,
+                         const int64_t *nrm_w);
 int ensure_device_pub(int dev);
 
 static std::mutex g_noalloc_mu;

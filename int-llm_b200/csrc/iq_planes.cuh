@@ -30,7 +30,7 @@
 // exact 128-bit atomics, and the warp that completes a row writes it.
 #pragma once
 #include <cuda/atomic>
-#include "iq_matvec.cuh"
+#include "iq_elem.cuh"
 
 namespace iq {
 
@@ -185,7 +185,8 @@ __device__ __forceinline__ uint32_t digit_word(const int64_t *__restrict__ xg, i
 template <int NP, bool XSMEM>
 __global__ void __launch_bounds__(256, 2)
 k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const int64_t *__restrict__ rowsum,
-                const int64_t *__restrict__ xg, int M, int N, int Kp, int add, RowAcc *__restrict__ racc) {
+                const int64_t *__restrict__ xg, int M, int N, int Kp, int add, RowAcc *__restrict__ racc,
+                const int64_t *__restrict__ nrm_w) {
     extern __shared__ __align__(16) unsigned char xd[];  // [8][Kp + 16] digit rows
     const int ld = Kp + 16;
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -209,12 +210,20 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
     // x and (with add) out are produced by the previous kernel
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (XSMEM) {
+        // Fused rmsnorm (llama_int.c:1048-1058) when nrm_w is given: every CTA
+        // computes the inverse rms of x itself (its first weight tile is already
+        // in flight) and stages the digits of fp_mul(fp_mul(x, inv), w).
+        __shared__ uint64_t red[64];
+        const int64_t inv = nrm_w ? cta_rms_inv(xg, N, red) : 0;
         // each thread: 4 consecutive x values -> 8 digit words (one per digit row)
         for (int k = 4 * threadIdx.x; k < Kp; k += 4 * blockDim.x) {
             uint64_t xu[4];
 #pragma unroll
-            for (int i = 0; i < 4; i++)
-                xu[i] = (k + i < N ? (uint64_t)__ldg(xg + k + i) : 0ull) ^ 0x8000000000000000ull;
+            for (int i = 0; i < 4; i++) {
+                int64_t xv = k + i < N ? __ldg(xg + k + i) : 0;
+                if (nrm_w && k + i < N) xv = d_mul(d_mul(xv, inv), __ldg(nrm_w + k + i));
+                xu[i] = (uint64_t)xv ^ 0x8000000000000000ull;
+            }
 #pragma unroll
             for (int j = 0; j < 8; j++) {
                 uint32_t v = 0;

@@ -58,6 +58,7 @@ SIGNATURES = {
     "iq_generate": (_I, [_P, _P, _I, _I, _P, _P, _P]),
     "iq_generate_batch": (_I, [_P, _P, _I, _I, _P, _P]),
     "iq_decode_steps_timed": (_I, [_P, _I, _I, _P]),
+    "iq_model_set_attention": (_I, [_P, _I]),
     "iq_tensor_seed": (ctypes.c_uint64, [_I, ctypes.c_char_p]),
     "iq_synth_weights": (_I, [ctypes.c_uint64, _P, _I64]),
     "iq_synth_acts": (_I, [ctypes.c_uint64, _P, _I64]),
@@ -337,6 +338,10 @@ class Model:
         n = np.zeros(B, dtype=np.int32)
         _call("iq_generate_batch", self.h, _hp(pr), L, max_new, _hp(out), _hp(n))
         return [out[b, :n[b]].tolist() for b in range(B)]
+
+    def set_attention(self, short_max):
+        """Contexts up to short_max use the single-kernel attention (0 = phased only)."""
+        _call("iq_model_set_attention", self.h, short_max)
 
     def decode_steps_timed(self, pos0, steps):
         ms = ctypes.c_float(0)

@@ -39,6 +39,21 @@ def test_tiny_generate_matches_reference_golden(tiny):
     assert toks2 == g["tokens"]
 
 
+@pytest.mark.parametrize("short_max", [0, 9, 1 << 20])
+def test_attention_kernel_choice_is_bit_identical(tiny, short_max):
+    """Phased attention only (0), a switch from single-kernel to phased in the
+    middle of decoding (9), single-kernel only: same tokens and logit hash."""
+    g, c, w, m = tiny
+    m.set_attention(short_max)
+    try:
+        toks, lh = m.generate(np.array(g["prompt"]), g["max_new"], logit_hash=True)
+        toks2, _ = m.generate(np.array(g["prompt"]), g["max_new"])
+    finally:
+        m.set_attention(384)
+    assert toks == toks2 == g["tokens"]
+    assert lh == g["logit_hash"]
+
+
 def test_tiny_forward_every_logit_vs_oracle(tiny):
     g, c, w, m = tiny
     o = helpers.OracleModel(c, w)
@@ -104,6 +119,9 @@ def test_cfg0_tinyllama_greedy_decode_golden():
     assert lh == g["logit_hash"]
     toks2, _ = m.generate(np.array(g["prompt"]), g["max_new"])
     assert toks2 == g["tokens"]
+    m.set_attention(0)  # phased attention kernels on the same golden
+    toks3, lh3 = m.generate(np.array(g["prompt"]), g["max_new"], logit_hash=True)
+    assert toks3 == g["tokens"] and lh3 == g["logit_hash"]
     m.close()
 
 
