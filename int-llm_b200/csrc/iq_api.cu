@@ -80,7 +80,8 @@ template <int WPR, int UNROLL, bool VEC, bool XSMEM>
 static int launch_mv_t(int64_t *out, const int64_t *W, const int64_t *x, int M, int N, int add, cudaStream_t s) {
     auto kern = k_matvec<WPR, UNROLL, VEC, XSMEM>;
     size_t smem = XSMEM ? (size_t)N * sizeof(int64_t) : 0;
-    if (smem > 48 * 1024) IQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    // static shared memory counts against the 48 KB default too
+    if (smem > 40 * 1024) IQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int occ = 0;
     IQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 256, smem));
     if (occ < 1) occ = 1;
@@ -193,6 +194,72 @@ static PlanesKernel planes_kernel(int np) {
     }
 }
 
+typedef void (*RowsKernel)(int64_t *, const uint4 *, const int64_t *, const int64_t *, int, int, int, int,
+                           const int64_t *);
+// Once per device and plane count: allow the largest staged-digit buffer
+// (the 48 KB default covers static + dynamic shared memory together) and
+// record the occupancy at that size.
+template <int NP>
+static int rows_setup(RowsKernel *k, int *occ) {
+    static int occs[64] = {0};
+    int dev = 0;
+    IQ_CUDA(cudaGetDevice(&dev));
+    *k = k_matvec_rows<NP>;
+    if (dev >= 0 && dev < 64 && occs[dev]) { *occ = occs[dev]; return IQ_OK; }
+    const int smax = 100 * 1024;
+    IQ_CUDA(cudaFuncSetAttribute(*k, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    IQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, *k, 256, smax));
+    if (*occ < 1) *occ = 1;
+    if (dev >= 0 && dev < 64) occs[dev] = *occ;
+    return IQ_OK;
+}
+
+// Row-owned matvec (k_matvec_rows) when one wave of CTAs covers every row tile:
+// cluster size S = the largest of 1, 2, 4, 8 with rows * S CTAs still one wave
+// and at least two column tiles per warp. IQ_ERR_UNSUPPORTED = use the
+// stream-K kernel. IQ_MV_ROWS=0 in the environment disables this path.
+int launch_matvec_rows(int64_t *out, const Packed &P, const int64_t *x, cudaStream_t s, int add,
+                       const int64_t *nrm_w, size_t smem) {
+    static const bool enabled = !getenv("IQ_MV_ROWS") || atoi(getenv("IQ_MV_ROWS")) != 0;
+    if (!enabled) return IQ_ERR_UNSUPPORTED;
+    RowsKernel kern = nullptr;
+    int occ = 0, rc = IQ_OK;
+    switch (P.np) {
+    case 1: rc = rows_setup<1>(&kern, &occ); break;
+    case 2: rc = rows_setup<2>(&kern, &occ); break;
+    case 3: rc = rows_setup<3>(&kern, &occ); break;
+    case 4: rc = rows_setup<4>(&kern, &occ); break;
+    case 5: rc = rows_setup<5>(&kern, &occ); break;
+    case 6: rc = rows_setup<6>(&kern, &occ); break;
+    case 7: rc = rows_setup<7>(&kern, &occ); break;
+    default: rc = rows_setup<8>(&kern, &occ); break;
+    }
+    if (rc) return rc;
+    const int64_t slots = (int64_t)dev_info().sms * (occ < 1 ? 1 : occ);
+    const int RT = P.Mp / 16, KT = P.Kp / 32;
+    if (RT > slots) return IQ_ERR_UNSUPPORTED;
+    int S = 1;
+    while (S < 8 && (int64_t)RT * S * 2 <= slots && KT >= 2 * 8 * S * 2) S *= 2;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)S;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.gridDim = dim3((unsigned)(RT * S));
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = S > 1 ? 2 : 1;
+    IQ_CUDA(cudaLaunchKernelEx(&cfg, kern, out, (const uint4 *)P.planes, (const int64_t *)P.rowsum, x, P.M, P.N,
+                               P.Kp, add, nrm_w));
+    IQ_CHECK_LAUNCH();
+    return IQ_OK;
+}
+
 // nrm_w != nullptr: x is un-normalised and rmsnorm with weights nrm_w is fused
 // into the digit staging; returns IQ_ERR_UNSUPPORTED if x is too long to stage.
 int launch_matvec_planes(int64_t *out, const Packed &P, const int64_t *x, cudaStream_t s, int add, RowAcc *racc,
@@ -200,9 +267,14 @@ int launch_matvec_planes(int64_t *out, const Packed &P, const int64_t *x, cudaSt
     size_t smem = (size_t)8 * (P.Kp + 16);
     bool xs = smem <= 100 * 1024;
     if (nrm_w && !xs) return IQ_ERR_UNSUPPORTED;
+    if (xs) {
+        int rc = launch_matvec_rows(out, P, x, s, add, nrm_w, smem);
+        if (rc != IQ_ERR_UNSUPPORTED) return rc;
+    }
     PlanesKernel kern = xs ? planes_kernel<true>(P.np) : planes_kernel<false>(P.np);
     if (!xs) smem = 0;
-    if (smem > 48 * 1024) IQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    // static shared memory counts against the 48 KB default too
+    if (smem > 40 * 1024) IQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int occ = 0;
     IQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 256, smem));
     if (occ < 1) occ = 1;

@@ -180,6 +180,35 @@ __device__ __forceinline__ uint32_t digit_word(const int64_t *__restrict__ xg, i
     return v;
 }
 
+// Stages the 8 unsigned digit rows of x_u = x + 2^63 into shared memory
+// (row j = byte j of every element, ld bytes apart; columns N..Kp are zero).
+// Fused rmsnorm (llama_int.c:1048-1058) when nrm_w is given: the CTA computes
+// the inverse rms of x itself and stages the digits of
+// fp_mul(fp_mul(x, inv), w) instead of x.
+__device__ __forceinline__ void stage_digits(unsigned char *xd, int ld, const int64_t *__restrict__ xg, int N, int Kp,
+                                             const int64_t *__restrict__ nrm_w) {
+    __shared__ uint64_t red[64];
+    const int64_t inv = nrm_w ? cta_rms_inv(xg, N, red) : 0;
+    // each thread: 4 consecutive x values -> 8 digit words (one per digit row)
+    for (int k = 4 * threadIdx.x; k < Kp; k += 4 * blockDim.x) {
+        uint64_t xu[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            int64_t xv = k + i < N ? __ldg(xg + k + i) : 0;
+            if (nrm_w && k + i < N) xv = d_mul(d_mul(xv, inv), __ldg(nrm_w + k + i));
+            xu[i] = (uint64_t)xv ^ 0x8000000000000000ull;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            uint32_t v = 0;
+#pragma unroll
+            for (int i = 0; i < 4; i++) v |= (uint32_t)((xu[i] >> (8 * j)) & 0xff) << (8 * i);
+            *reinterpret_cast<uint32_t *>(xd + j * ld + k) = v;
+        }
+    }
+    __syncthreads();
+}
+
 // XSMEM: digits staged in shared memory (Kp small enough), else gathered from
 // x in global memory (L1-cached) per column tile.
 template <int NP, bool XSMEM>
@@ -209,31 +238,7 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
     }
     // x and (with add) out are produced by the previous kernel
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (XSMEM) {
-        // Fused rmsnorm (llama_int.c:1048-1058) when nrm_w is given: every CTA
-        // computes the inverse rms of x itself (its first weight tile is already
-        // in flight) and stages the digits of fp_mul(fp_mul(x, inv), w).
-        __shared__ uint64_t red[64];
-        const int64_t inv = nrm_w ? cta_rms_inv(xg, N, red) : 0;
-        // each thread: 4 consecutive x values -> 8 digit words (one per digit row)
-        for (int k = 4 * threadIdx.x; k < Kp; k += 4 * blockDim.x) {
-            uint64_t xu[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                int64_t xv = k + i < N ? __ldg(xg + k + i) : 0;
-                if (nrm_w && k + i < N) xv = d_mul(d_mul(xv, inv), __ldg(nrm_w + k + i));
-                xu[i] = (uint64_t)xv ^ 0x8000000000000000ull;
-            }
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                uint32_t v = 0;
-#pragma unroll
-                for (int i = 0; i < 4; i++) v |= (uint32_t)((xu[i] >> (8 * j)) & 0xff) << (8 * i);
-                *reinterpret_cast<uint32_t *>(xd + j * ld + k) = v;
-            }
-        }
-        __syncthreads();
-    }
+    if (XSMEM) stage_digits(xd, ld, xg, N, Kp, nrm_w);
 
     const unsigned char *xb = xd + g * ld + 4 * t;
 
@@ -322,6 +327,108 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
         }
 #pragma unroll
         for (int p = 0; p < NP; p++) cur[p] = nxt[p];
+    }
+}
+
+// Row-owned variant for matrices of at most one wave of row tiles: a cluster
+// of S CTAs (S = 1, 2, 4 or 8) owns one 16-row tile, its 8*S warps split the
+// column tiles evenly, the warps' 128-bit partials are summed in shared
+// memory and the S CTA sums in rank 0's shared memory (distributed shared
+// memory), which writes the 16 outputs. No global atomics and no scratch; the
+// result is the same integer (addition mod 2^128 is associative).
+template <int NP>
+__global__ void __launch_bounds__(256, 2)
+k_matvec_rows(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const int64_t *__restrict__ rowsum,
+              const int64_t *__restrict__ xg, int M, int N, int Kp, int add, const int64_t *__restrict__ nrm_w) {
+    extern __shared__ __align__(16) unsigned char xd[];  // [8][Kp + 16] digit rows
+    __shared__ __align__(16) unsigned long long wpart[8][16][2];  // per warp: 16 row partials (lo, hi)
+    __shared__ __align__(16) unsigned long long cpart[8][16][2];  // per cluster rank (read in rank 0)
+    const int ld = Kp + 16;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
+    const int KT = Kp / 32;
+    uint32_t S, crank;
+    asm("mov.u32 %0, %%cluster_nctarank;" : "=r"(S));
+    asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
+    const int rt = blockIdx.x / S;
+    const int wi = crank * 8 + warp, nwi = S * 8;
+    const int k0 = KT * wi / nwi, k1 = KT * (wi + 1) / nwi;
+    constexpr int TS = NP * 32;  // uint4 per packed tile
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // every CTA of the cluster must be running before rank 0's shared memory is
+    // written: arrive now, wait just before the write
+    if (S > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+    const uint4 *tb = planes + (size_t)rt * KT * TS + lane;
+    uint4 cur[NP];
+    if (k0 < k1) {
+#pragma unroll
+        for (int p = 0; p < NP; p++) cur[p] = ld_stream_u4(tb + (size_t)k0 * TS + p * 32);
+    }
+    // x and (with add) out are produced by the previous kernel
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    stage_digits(xd, ld, xg, N, Kp, nrm_w);
+    const unsigned char *xb = xd + g * ld + 4 * t;
+    int c[NP][4];
+#pragma unroll
+    for (int p = 0; p < NP; p++)
+#pragma unroll
+        for (int q = 0; q < 4; q++) c[p][q] = 0;
+    i128 r0 = 0, r1 = 0;
+    int since_fold = 0;
+    for (int kt = k0; kt < k1; kt++) {
+        uint4 nxt[NP];
+        if (kt + 1 < k1) {
+#pragma unroll
+            for (int p = 0; p < NP; p++) nxt[p] = ld_stream_u4(tb + (size_t)(kt + 1) * TS + p * 32);
+        }
+        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(xb + kt * 32);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t *>(xb + kt * 32 + 16);
+#pragma unroll
+        for (int p = 0; p < NP - 1; p++) mma_i8<false>(c[p], cur[p], b0, b1);
+        mma_i8<true>(c[NP - 1], cur[NP - 1], b0, b1);  // top plane: signed
+        if (++since_fold >= 1024) { fold_planes(c, t, r0, r1); since_fold = 0; }
+#pragma unroll
+        for (int p = 0; p < NP; p++) cur[p] = nxt[p];
+    }
+    fold_planes(c, t, r0, r1);
+#pragma unroll
+    for (int m = 1; m <= 2; m <<= 1) {  // the 4 lanes of a row group hold the 8 digits
+        r0 += shfl_xor_i128(r0, m);
+        r1 += shfl_xor_i128(r1, m);
+    }
+    if (t == 0) {
+        wpart[warp][g][0] = (uint64_t)r0; wpart[warp][g][1] = (uint64_t)((u128)r0 >> 64);
+        wpart[warp][g + 8][0] = (uint64_t)r1; wpart[warp][g + 8][1] = (uint64_t)((u128)r1 >> 64);
+    }
+    __syncthreads();
+    i128 v = 0;
+    if (threadIdx.x < 16) {
+#pragma unroll
+        for (int w = 0; w < 8; w++)
+            v += (i128)(((u128)wpart[w][threadIdx.x][1] << 64) | wpart[w][threadIdx.x][0]);
+    }
+    if (S > 1) {
+        asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+        if (threadIdx.x < 16) {
+            uint32_t remote;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, 0;"
+                         : "=r"(remote) : "r"((uint32_t)__cvta_generic_to_shared(&cpart[crank][threadIdx.x][0])));
+            asm volatile("st.shared::cluster.v2.u64 [%0], {%1, %2};"
+                         :: "r"(remote), "l"((uint64_t)v), "l"((uint64_t)((u128)v >> 64)) : "memory");
+        }
+        asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+        asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+        if (crank != 0) return;
+        if (threadIdx.x < 16) {
+            v = 0;
+            for (uint32_t r = 0; r < S; r++)
+                v += (i128)(((u128)cpart[r][threadIdx.x][1] << 64) | cpart[r][threadIdx.x][0]);
+        }
+    }
+    const int row = rt * 16 + (int)threadIdx.x;
+    if (threadIdx.x < 16 && row < M) {
+        i128 ws = (i128)(((u128)(uint64_t)rowsum[2 * row + 1] << 64) | (uint64_t)rowsum[2 * row]);
+        int64_t val = (int64_t)((i128)((u128)v - ((u128)ws << 63)) >> 48);
+        out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)val) : val;
     }
 }
 
