@@ -14,7 +14,7 @@ import os
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libiq.so")
+LIB_PATH = os.environ.get("IQ_LIB") or os.path.join(HERE, "libiq.so")  # IQ_LIB: another build
 
 IQ_FN = dict(mul=0, div=1, sqrt=2, sqrt_fast=3, inv_sqrt=4, exp=5, log=6, cos=7, sin=8,
              sigmoid=9, silu=10, safe_exp=11, exp_dyadic=12)
