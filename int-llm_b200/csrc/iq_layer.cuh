@@ -73,7 +73,7 @@ __device__ __forceinline__ i128 d_mul128(int64_t a, int64_t b) {
 __global__ void k_attention(int64_t *__restrict__ out, const int64_t *__restrict__ qkv,
                             const int64_t *__restrict__ kc, const int64_t *__restrict__ vc,
                             const int *__restrict__ pos_arr, const int *__restrict__ seq_arr, int nh, int nkv,
-                            int hd, int max_seq) {
+                            int hd, int max_seq, int64_t scale) {
     extern __shared__ __align__(16) int64_t sm[];
     __shared__ uint64_t red[64];
     const int h = blockIdx.x, b = blockIdx.y;
@@ -84,39 +84,69 @@ __global__ void k_attention(int64_t *__restrict__ out, const int64_t *__restrict
     const int64_t *q = qkv + (size_t)b * (dim + 2 * kvd) + h * hd;
     for (int d = threadIdx.x; d < hd; d += blockDim.x) qs[d] = q[d];
     __syncthreads();
-    const int64_t scale = d_inv_sqrt(d_from_int(hd));
     const int sq = seq_arr[b];
     const int64_t *kb = kc + (size_t)sq * max_seq * kvd + kvh * hd;
     const int64_t *vb = vc + (size_t)sq * max_seq * kvd + kvh * hd;
     // scores: groups of 8 lanes share one position and split its dims, so a
     // warp reads four key rows in 64-byte coalesced pieces; the int128 partial
-    // dots combine exactly (addition mod 2^128)
+    // dots combine exactly (addition mod 2^128). Each lane issues all its key
+    // loads for two positions before multiplying, so the L2 latencies overlap.
     {
         const int sl = threadIdx.x & 7, nsg = blockDim.x >> 3;
-        for (int tb = 0; tb < T; tb += nsg) {  // uniform trip count: every lane shuffles
-            const int t0 = tb + (threadIdx.x >> 3);
-            const bool act = t0 < T;
-            const int64_t *kt = kb + (size_t)(act ? t0 : 0) * kvd;
-            i128 dot = 0;
-            if (act)
-                for (int d = sl; d < hd; d += 8) dot += d_mul128(qs[d], kt[d]);
+        for (int tb = 0; tb < T; tb += 2 * nsg) {  // uniform trip count: every lane shuffles
+            const int ta = tb + (threadIdx.x >> 3), tc = ta + nsg;
+            const bool aa = ta < T, ac = tc < T;
+            const int64_t *ka = kb + (size_t)(aa ? ta : 0) * kvd, *kc2 = kb + (size_t)(ac ? tc : 0) * kvd;
+            i128 da = 0, dc = 0;
+            for (int d0 = 0; d0 < hd; d0 += 64) {
+                int64_t va[8], vc2[8];
 #pragma unroll
-            for (int m = 4; m >= 1; m >>= 1) dot += shfl_xor_i128(dot, m);
-            if (act && sl == 0) sc[t0] = d_mul((int64_t)(dot >> 48), scale);
+                for (int j = 0; j < 8; j++) {
+                    const int d = d0 + sl + 8 * j;
+                    va[j] = aa && d < hd ? ka[d] : 0;
+                    vc2[j] = ac && d < hd ? kc2[d] : 0;
+                }
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int d = d0 + sl + 8 * j;
+                    const int64_t qv = d < hd ? qs[d] : 0;
+                    da += d_mul128(qv, va[j]);
+                    dc += d_mul128(qv, vc2[j]);
+                }
+            }
+#pragma unroll
+            for (int m = 4; m >= 1; m >>= 1) {
+                da += shfl_xor_i128(da, m);
+                dc += shfl_xor_i128(dc, m);
+            }
+            if (sl == 0) {
+                if (aa) sc[ta] = d_mul((int64_t)(da >> 48), scale);
+                if (ac) sc[tc] = d_mul((int64_t)(dc >> 48), scale);
+            }
         }
     }
     __syncthreads();
     cta_softmax(sc, T, red);
     __syncthreads();
-    // PV: thread groups of hd threads split t; int64 partial sums combine exactly (mod 2^64)
+    // PV: thread groups of hd threads split t; int64 partial sums combine
+    // exactly (mod 2^64). Eight value loads are issued before their multiplies.
     const int groups = blockDim.x / hd;
     const int g = threadIdx.x / hd, d = threadIdx.x % hd;
-    int64_t acc = 0;
-    if (g < groups)
-        for (int t = g; t < T; t += groups) acc += d_mul(sc[t], vb[(size_t)t * kvd + d]);
+    uint64_t acc = 0;
+    if (g < groups) {
+        int t = g;
+        for (; t + 7 * groups < T; t += 8 * groups) {
+            int64_t vv[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) vv[j] = vb[(size_t)(t + j * groups) * kvd + d];
+#pragma unroll
+            for (int j = 0; j < 8; j++) acc += (uint64_t)d_mul(sc[t + j * groups], vv[j]);
+        }
+        for (; t < T; t += groups) acc += (uint64_t)d_mul(sc[t], vb[(size_t)t * kvd + d]);
+    }
     __syncthreads();
     int64_t *part = sm + hd;  // reuse the score area: [groups][hd]
-    if (g < groups) part[g * hd + d] = acc;
+    if (g < groups) part[g * hd + d] = (int64_t)acc;
     __syncthreads();
     for (int dd = threadIdx.x; dd < hd; dd += blockDim.x) {
         uint64_t s = 0;
@@ -124,6 +154,10 @@ __global__ void k_attention(int64_t *__restrict__ out, const int64_t *__restrict
         out[(size_t)b * dim + h * hd + dd] = (int64_t)s;
     }
 }
+
+// fp_inv_sqrt(fp_from_int(hd)): the attention score scale (llama_int.c:1433),
+// computed once per model on the device.
+__global__ void k_att_scale(int64_t *out, int hd) { *out = d_inv_sqrt(d_from_int(hd)); }
 
 // Exact attention with coalesced K tiles: one CTA per (row b, block of hpc
 // query heads that share one kv head; hpc divides nh / nkv). Keys are staged
@@ -209,7 +243,8 @@ __global__ void k_attn_init(int64_t *__restrict__ out, int64_t *__restrict__ mx,
 __global__ void __launch_bounds__(256)
 k_attn_scores(int64_t *__restrict__ sc, int64_t *__restrict__ mx, const int64_t *__restrict__ qkv,
               const int64_t *__restrict__ kc, const int *__restrict__ pos_arr, const int *__restrict__ seq_arr,
-              int nh, int nkv, int hd, int max_seq, int Tcap) {
+              int nh, int nkv, int hd, int max_seq, int Tcap,
+              int64_t scale) {
     extern __shared__ __align__(16) int64_t smem[];
     const int tile = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int T = pos_arr[b] + 1, t0 = tile * ATT_TILE;
@@ -223,7 +258,6 @@ k_attn_scores(int64_t *__restrict__ sc, int64_t *__restrict__ mx, const int64_t 
     const int64_t *kb = kc + ((size_t)seq_arr[b] * max_seq + t0) * kvd + g * hd;
     for (int e = threadIdx.x; e < nt * hd; e += blockDim.x) kt[(e / hd) * kld + e % hd] = kb[(size_t)(e / hd) * kvd + e % hd];
     __syncthreads();
-    const int64_t scale = d_inv_sqrt(d_from_int(hd));
     for (int e = threadIdx.x; e < grp * ATT_TILE; e += blockDim.x) {
         const int hh = e / ATT_TILE, tt = e % ATT_TILE;
         int64_t v = INT64_MIN;

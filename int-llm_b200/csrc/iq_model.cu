@@ -101,6 +101,7 @@ struct iq_model {
     cudaGraphExec_t graph = nullptr;    // one decode step at batch max_batch (phased attention)
     cudaGraphExec_t graph_s = nullptr;  // the same step with single-kernel attention
     int att_short = 0;  // steps whose positions all lie below this use k_attention
+    int64_t att_scale = 0;  // fp_inv_sqrt(fp_from_int(head_dim))
     bool loaded_globals = false;
     std::vector<bool> loaded_layer;
 };
@@ -315,7 +316,7 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
             IQ_CHECK_LAUNCH();
             k_attn_scores<<<dim3(grid_t, S.nkv_l, R), 256, m->att_s1, s>>>(m->asc, m->amx, m->qkv, m->kc[l], pos,
                                                                             seq, S.nh_l, S.nkv_l, hd, c.max_seq_len,
-                                                                            c.max_seq_len);
+                                                                            c.max_seq_len, m->att_scale);
             IQ_CHECK_LAUNCH();
             k_attn_exp<<<dim3((c.max_seq_len + 255) / 256, S.nh_l, R), 256, 0, s>>>(m->asc, m->amx, m->asum, pos,
                                                                                    S.nh_l, c.max_seq_len);
@@ -329,7 +330,8 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
                 m->hpc);
         else
             k_attention<<<dim3(S.nh_l, R), 256, m->attn_smem, s>>>(att_out, m->qkv, m->kc[l], m->vc[l], pos,
-                                                                   seq, S.nh_l, S.nkv_l, hd, c.max_seq_len);
+                                                                   seq, S.nh_l, S.nkv_l, hd, c.max_seq_len,
+                                                                   m->att_scale);
         IQ_CHECK_LAUNCH();
         if (tp) {
             if ((rc = gather_rows(m, m->att_l, m->att, R, S.nh_l * hd))) return rc;
@@ -583,7 +585,9 @@ IQ_API int iq_model_create_tp(const iq_config *cfg, int max_batch, int device, i
         m->att_short = m->attn_smem <= 200 * 1024 ? short_env : 0;
     }
     k_rope_init<<<256, 128, 0, m->s>>>(m->rcos, m->rsin, c.head_dim, c.max_seq_len, c.rope_theta);
-    e = cudaStreamSynchronize(m->s);
+    k_att_scale<<<1, 1, 0, m->s>>>(m->hidden, c.head_dim);  // hidden is scratch until reset
+    e = cudaMemcpyAsync(&m->att_scale, m->hidden, 8, cudaMemcpyDeviceToHost, m->s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->s);
     if (e != cudaSuccess) { iq_model_destroy(m); return cuda_fail(e); }
     if ((rc = iq_model_reset(m))) { iq_model_destroy(m); return rc; }
     *out = m;
