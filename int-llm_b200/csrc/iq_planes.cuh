@@ -330,8 +330,8 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
     }
 }
 
-// Row-owned variant for matrices of at most one wave of row tiles: a cluster
-// of S CTAs (S = 1, 2, 4 or 8) owns one 16-row tile, its 8*S warps split the
+// Row-owned variant: a cluster of S CTAs (S = 1, 2, 4 or 8) owns one 16-row
+// tile (S = 1: a CTA owns every gridDim-th tile in turn), its 8*S warps split the
 // column tiles evenly, the warps' 128-bit partials are summed in shared
 // memory and the S CTA sums in rank 0's shared memory (distributed shared
 // memory), which writes the 16 outputs. No global atomics and no scratch; the
@@ -345,11 +345,13 @@ k_matvec_rows(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const
     __shared__ __align__(16) unsigned long long cpart[8][16][2];  // per cluster rank (read in rank 0)
     const int ld = Kp + 16;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
-    const int KT = Kp / 32;
+    const int KT = Kp / 32, RT = (M + 15) / 16;
     uint32_t S, crank;
     asm("mov.u32 %0, %%cluster_nctarank;" : "=r"(S));
     asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
-    const int rt = blockIdx.x / S;
+    // row tiles rt0, rt0 + stride, ... (one tile per cluster when S > 1)
+    const int rt0 = blockIdx.x / S, stride = gridDim.x / S;
+    const int ntiles = rt0 < RT ? (RT - 1 - rt0) / stride + 1 : 0;
     const int wi = crank * 8 + warp, nwi = S * 8;
     const int k0 = KT * wi / nwi, k1 = KT * (wi + 1) / nwi;
     constexpr int TS = NP * 32;  // uint4 per packed tile
@@ -357,78 +359,93 @@ k_matvec_rows(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const
     // every CTA of the cluster must be running before rank 0's shared memory is
     // written: arrive now, wait just before the write
     if (S > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-    const uint4 *tb = planes + (size_t)rt * KT * TS + lane;
+    const uint4 *pl = planes + lane;
     uint4 cur[NP];
-    if (k0 < k1) {
+    if (ntiles > 0 && k0 < k1) {
+        const uint4 *tp0 = pl + ((size_t)rt0 * KT + k0) * TS;
 #pragma unroll
-        for (int p = 0; p < NP; p++) cur[p] = ld_stream_u4(tb + (size_t)k0 * TS + p * 32);
+        for (int p = 0; p < NP; p++) cur[p] = ld_stream_u4(tp0 + p * 32);
     }
     // x and (with add) out are produced by the previous kernel
     asm volatile("griddepcontrol.wait;" ::: "memory");
     stage_digits(xd, ld, xg, N, Kp, nrm_w);
     const unsigned char *xb = xd + g * ld + 4 * t;
-    int c[NP][4];
+    for (int i = 0; i < ntiles; i++) {
+        const int rt = rt0 + i * stride;
+        int c[NP][4];
 #pragma unroll
-    for (int p = 0; p < NP; p++)
+        for (int p = 0; p < NP; p++)
 #pragma unroll
-        for (int q = 0; q < 4; q++) c[p][q] = 0;
-    i128 r0 = 0, r1 = 0;
-    int since_fold = 0;
-    for (int kt = k0; kt < k1; kt++) {
-        uint4 nxt[NP];
-        if (kt + 1 < k1) {
+            for (int q = 0; q < 4; q++) c[p][q] = 0;
+        i128 r0 = 0, r1 = 0;
+        int since_fold = 0;
+        for (int kt = k0; kt < k1; kt++) {
+            // the next unit: this tile's next column tile, else the next tile's first
+            uint4 nxt[NP];
+            const bool more = kt + 1 < k1 || i + 1 < ntiles;
+            if (more) {
+                const size_t un = kt + 1 < k1 ? (size_t)rt * KT + kt + 1 : (size_t)(rt + stride) * KT + k0;
+                const uint4 *tn = pl + un * TS;
 #pragma unroll
-            for (int p = 0; p < NP; p++) nxt[p] = ld_stream_u4(tb + (size_t)(kt + 1) * TS + p * 32);
+                for (int p = 0; p < NP; p++) nxt[p] = ld_stream_u4(tn + p * 32);
+            }
+            const uint32_t b0 = *reinterpret_cast<const uint32_t *>(xb + kt * 32);
+            const uint32_t b1 = *reinterpret_cast<const uint32_t *>(xb + kt * 32 + 16);
+#pragma unroll
+            for (int p = 0; p < NP - 1; p++) mma_i8<false>(c[p], cur[p], b0, b1);
+            mma_i8<true>(c[NP - 1], cur[NP - 1], b0, b1);  // top plane: signed
+            if (++since_fold >= 1024) { fold_planes(c, t, r0, r1); since_fold = 0; }
+#pragma unroll
+            for (int p = 0; p < NP; p++) cur[p] = nxt[p];
         }
-        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(xb + kt * 32);
-        const uint32_t b1 = *reinterpret_cast<const uint32_t *>(xb + kt * 32 + 16);
+        fold_planes(c, t, r0, r1);
 #pragma unroll
-        for (int p = 0; p < NP - 1; p++) mma_i8<false>(c[p], cur[p], b0, b1);
-        mma_i8<true>(c[NP - 1], cur[NP - 1], b0, b1);  // top plane: signed
-        if (++since_fold >= 1024) { fold_planes(c, t, r0, r1); since_fold = 0; }
-#pragma unroll
-        for (int p = 0; p < NP; p++) cur[p] = nxt[p];
-    }
-    fold_planes(c, t, r0, r1);
-#pragma unroll
-    for (int m = 1; m <= 2; m <<= 1) {  // the 4 lanes of a row group hold the 8 digits
-        r0 += shfl_xor_i128(r0, m);
-        r1 += shfl_xor_i128(r1, m);
-    }
-    if (t == 0) {
-        wpart[warp][g][0] = (uint64_t)r0; wpart[warp][g][1] = (uint64_t)((u128)r0 >> 64);
-        wpart[warp][g + 8][0] = (uint64_t)r1; wpart[warp][g + 8][1] = (uint64_t)((u128)r1 >> 64);
-    }
-    __syncthreads();
-    i128 v = 0;
-    if (threadIdx.x < 16) {
-#pragma unroll
-        for (int w = 0; w < 8; w++)
-            v += (i128)(((u128)wpart[w][threadIdx.x][1] << 64) | wpart[w][threadIdx.x][0]);
-    }
-    if (S > 1) {
-        asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+        for (int m = 1; m <= 2; m <<= 1) {  // the 4 lanes of a row group hold the 8 digits
+            r0 += shfl_xor_i128(r0, m);
+            r1 += shfl_xor_i128(r1, m);
+        }
+        if (t == 0) {
+            wpart[warp][g][0] = (uint64_t)r0; wpart[warp][g][1] = (uint64_t)((u128)r0 >> 64);
+            wpart[warp][g + 8][0] = (uint64_t)r1; wpart[warp][g + 8][1] = (uint64_t)((u128)r1 >> 64);
+        }
+        __syncthreads();
+        i128 v = 0;
         if (threadIdx.x < 16) {
-            uint32_t remote;
-            asm volatile("mapa.shared::cluster.u32 %0, %1, 0;"
-                         : "=r"(remote) : "r"((uint32_t)__cvta_generic_to_shared(&cpart[crank][threadIdx.x][0])));
-            asm volatile("st.shared::cluster.v2.u64 [%0], {%1, %2};"
-                         :: "r"(remote), "l"((uint64_t)v), "l"((uint64_t)((u128)v >> 64)) : "memory");
+#pragma unroll
+            for (int w = 0; w < 8; w++)
+                v += (i128)(((u128)wpart[w][threadIdx.x][1] << 64) | wpart[w][threadIdx.x][0]);
         }
+        if (S > 1) {
+            asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+            if (threadIdx.x < 16) {
+                uint32_t remote;
+                asm volatile("mapa.shared::cluster.u32 %0, %1, 0;"
+                             : "=r"(remote)
+                             : "r"((uint32_t)__cvta_generic_to_shared(&cpart[crank][threadIdx.x][0])));
+                asm volatile("st.shared::cluster.v2.u64 [%0], {%1, %2};"
+                             :: "r"(remote), "l"((uint64_t)v), "l"((uint64_t)((u128)v >> 64)) : "memory");
+            }
+            asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+            asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+            if (crank != 0) return;  // one tile per cluster
+            if (threadIdx.x < 16) {
+                v = 0;
+                for (uint32_t r = 0; r < S; r++)
+                    v += (i128)(((u128)cpart[r][threadIdx.x][1] << 64) | cpart[r][threadIdx.x][0]);
+            }
+        }
+        const int row = rt * 16 + (int)threadIdx.x;
+        if (threadIdx.x < 16 && row < M) {
+            i128 ws = (i128)(((u128)(uint64_t)rowsum[2 * row + 1] << 64) | (uint64_t)rowsum[2 * row]);
+            int64_t val = (int64_t)((i128)((u128)v - ((u128)ws << 63)) >> 48);
+            out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)val) : val;
+        }
+        __syncthreads();  // wpart is rewritten by the next tile
+    }
+    if (S > 1 && ntiles == 0) {  // keep the cluster barrier phases matched
+        asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
         asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
         asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-        if (crank != 0) return;
-        if (threadIdx.x < 16) {
-            v = 0;
-            for (uint32_t r = 0; r < S; r++)
-                v += (i128)(((u128)cpart[r][threadIdx.x][1] << 64) | cpart[r][threadIdx.x][0]);
-        }
-    }
-    const int row = rt * 16 + (int)threadIdx.x;
-    if (threadIdx.x < 16 && row < M) {
-        i128 ws = (i128)(((u128)(uint64_t)rowsum[2 * row + 1] << 64) | (uint64_t)rowsum[2 * row]);
-        int64_t val = (int64_t)((i128)((u128)v - ((u128)ws << 63)) >> 48);
-        out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)val) : val;
     }
 }
 

@@ -208,15 +208,16 @@ def test_rmsnorm_softmax_vs_oracle():
 
 @pytest.mark.parametrize("M,N", [(1, 1), (3, 17), (5, 64), (16, 32), (17, 33), (64, 1000), (33, 2048),
                                  (1000, 63), (129, 4097), (7, 40000), (2048, 2048), (256, 2048),
-                                 (2560, 2048), (5000, 300)])
+                                 (2560, 2048), (5000, 300), (9600, 64)])
 @pytest.mark.parametrize("dist", ["full", "cfg"])
 def test_matvec_packed_vs_oracle(M, N, dist):
     """Byte-plane tensor-core matvec: exact on full-range int64 (mod 2^128 wrap)
     and on config-distributed inputs; repeated launches (row scratch resets).
     Shapes reach the row-owned kernel with clusters of 1 (1000x63, 2560x2048),
-    2 (2048x2048), 4 (256x2048) and 8 CTAs (129x4097), the stream-K kernel
-    with staged digits (5000 rows: more row tiles than one wave) and with
-    digits read from global memory (7x40000)."""
+    2 (2048x2048), 4 (256x2048) and 8 CTAs (129x4097), row-owned over two
+    waves (5000x300), the stream-K kernel with staged digits (9600 rows: more
+    than two waves of row tiles) and with digits read from global memory
+    (7x40000)."""
     import torch
     rng = np.random.default_rng(M * 31 + N)
     if dist == "full":
