@@ -132,53 +132,122 @@ int launch_gemm_add(int64_t *out, const int64_t *W, const int64_t *X, int rows, 
 
 // ------------------------------------------------- byte-plane matvec
 
-// Number of byte planes a matrix needs (1..8), see bytes_needed. Synchronises s.
-static int count_planes(const int64_t *d_w, int64_t n, cudaStream_t s, int *np) {
-    int *d = nullptr;
-    IQ_CUDA(cudaMalloc(&d, sizeof(int)));
-    int one = 1;
-    cudaError_t e = cudaMemcpyAsync(d, &one, sizeof(int), cudaMemcpyHostToDevice, s);
+// Plane statistics of a matrix (see k_plane_count): top = bytes needed as a
+// signed integer, low[b] = weights whose lowest nonzero byte is b. Synchronises s.
+static int plane_stats(const int64_t *d_w, int64_t n, cudaStream_t s, int *top, unsigned long long low[8]) {
+    unsigned long long *d = nullptr, h[9] = {1, 0, 0, 0, 0, 0, 0, 0, 0};
+    IQ_CUDA(cudaMalloc(&d, sizeof(h)));
+    cudaError_t e = cudaMemcpyAsync(d, h, sizeof(h), cudaMemcpyHostToDevice, s);
     if (e == cudaSuccess) {
         k_plane_count<<<(int)std::min<int64_t>((n + 255) / 256, (int64_t)dev_info().sms * 16), 256, 0, s>>>(d, d_w, n);
         e = cudaGetLastError();
     }
-    if (e == cudaSuccess) e = cudaMemcpyAsync(np, d, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(h, d, sizeof(h), cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     cudaFree(d);
-    return e == cudaSuccess ? IQ_OK : cuda_fail(e);
+    if (e != cudaSuccess) return cuda_fail(e);
+    *top = (int)h[0];
+    for (int b = 0; b < 8; b++) low[b] = h[1 + b];
+    return IQ_OK;
 }
+
+// Number of byte planes a matrix needs when all are kept from plane 0.
+static int count_planes(const int64_t *d_w, int64_t n, cudaStream_t s, int *np) {
+    unsigned long long low[8];
+    return plane_stats(d_w, n, s, np, low);
+}
+
+// Lowest stored plane: the p0 that saves the most bytes, counting each
+// residual entry (4-byte column + 8-byte value + its share of row offsets)
+// as 16 bytes against Mp*Kp bytes per dropped plane, among the p0 whose
+// residual stays at most one entry per 1024 weights (one thread adds a row's
+// entries serially when the row is written, so density costs latency).
+// IQ_PLANE_P0 (0..7) in the environment caps it (0 = keep every plane).
+static int choose_p0(int top, const unsigned long long low[8], int64_t plane_bytes) {
+    static const int cap = getenv("IQ_PLANE_P0") ? atoi(getenv("IQ_PLANE_P0")) : 8;
+    int best = 0;
+    long double best_gain = 0, below = 0;
+    for (int p0 = 1; p0 < top && p0 <= cap; p0++) {
+        below += (long double)low[p0 - 1];
+        const long double gain = (long double)p0 * plane_bytes - 16.0L * below;
+        if (below * 1024.0L > (long double)plane_bytes) break;
+        if (gain > best_gain) { best_gain = gain; best = p0; }
+    }
+    return best;
+}
+
+static void free_packed(Packed *P);
 
 static int pack_weights(const int64_t *d_w, int M, int N, cudaStream_t s, Packed *P) {
     P->M = M; P->N = N;
     P->Mp = (M + 15) / 16 * 16;
     P->Kp = (N + 31) / 32 * 32;
-    int rc = count_planes(d_w, (int64_t)M * N, s, &P->np);
+    int top = 8;
+    unsigned long long low[8];
+    int rc = plane_stats(d_w, (int64_t)M * N, s, &top, low);
     if (rc) return rc;
+    P->p0 = choose_p0(top, low, (int64_t)P->Mp * P->Kp);
+    P->np = top - P->p0;
+    P->nnz = 0;
+    for (int b = 0; b < P->p0; b++) P->nnz += (int)low[b];
+    const uint64_t mask = P->p0 ? (~0ull >> (64 - 8 * P->p0)) : 0ull;
     size_t nbytes = (size_t)P->Mp * P->Kp * P->np;
-    IQ_CUDA(cudaMalloc(&P->planes, nbytes));
-    cudaError_t e = cudaMalloc(&P->rowsum, (size_t)P->Mp * 16);
-    if (e != cudaSuccess) { cudaFree(P->planes); P->planes = nullptr; return cuda_fail(e); }
+    cudaError_t e = cudaMalloc(&P->planes, nbytes);
+    if (e == cudaSuccess) e = cudaMalloc(&P->rowsum, (size_t)P->Mp * 16);
+    if (e == cudaSuccess && P->nnz > 0) {
+        e = cudaMalloc(&P->res_ptr, (size_t)(P->Mp + 1) * sizeof(int));
+        if (e == cudaSuccess) e = cudaMalloc(&P->res_col, (size_t)P->nnz * sizeof(int));
+        if (e == cudaSuccess) e = cudaMalloc(&P->res_val, (size_t)P->nnz * sizeof(int64_t));
+    }
+    if (e != cudaSuccess) { free_packed(P); return cuda_fail(e); }
     const int KT = P->Kp / 32;
     int64_t total = (int64_t)(P->Mp / 16) * KT * 32;
     int64_t blocks = (total + 255) / 256;
     k_pack_planes<<<(int)std::min<int64_t>(blocks, (int64_t)dev_info().sms * 32), 256, 0, s>>>(
-        P->planes, d_w, M, N, KT, total, P->np);
+        P->planes, d_w, M, N, KT, total, P->np, P->p0);
     IQ_CHECK_LAUNCH();
-    k_row_sums<<<std::min(P->Mp / 8 + 1, dev_info().sms * 16), 256, 0, s>>>(P->rowsum, d_w, M, N, P->Mp);
+    k_row_sums<<<std::min(P->Mp / 8 + 1, dev_info().sms * 16), 256, 0, s>>>(P->rowsum, d_w, M, N, P->Mp, mask);
     IQ_CHECK_LAUNCH();
+    if (P->nnz > 0) {
+        // CSR offsets: per-row counts on the device, exclusive scan on the host
+        std::vector<int> cnt(P->Mp + 1, 0);
+        IQ_CUDA(cudaMemsetAsync(P->res_ptr, 0, (size_t)(P->Mp + 1) * sizeof(int), s));
+        const int g = std::min((M + 7) / 8, dev_info().sms * 16);
+        k_res_count<<<g, 256, 0, s>>>(P->res_ptr, d_w, M, N, mask);
+        IQ_CHECK_LAUNCH();
+        IQ_CUDA(cudaMemcpyAsync(cnt.data(), P->res_ptr, (size_t)P->Mp * sizeof(int), cudaMemcpyDeviceToHost, s));
+        IQ_CUDA(cudaStreamSynchronize(s));
+        int run = 0;
+        for (int r = 0; r <= P->Mp; r++) { int c = r < P->Mp ? cnt[r] : 0; cnt[r] = run; run += c; }
+        if (run != P->nnz) { free_packed(P); return IQ_ERR_STATE; }
+        IQ_CUDA(cudaMemcpyAsync(P->res_ptr, cnt.data(), (size_t)(P->Mp + 1) * sizeof(int), cudaMemcpyHostToDevice, s));
+        k_res_fill<<<g, 256, 0, s>>>(P->res_col, P->res_val, P->res_ptr, d_w, M, N, mask);
+        IQ_CHECK_LAUNCH();
+        IQ_CUDA(cudaStreamSynchronize(s));  // cnt is a host buffer that goes out of scope
+    }
     return IQ_OK;
+}
+
+static PackedRes packed_res(const Packed &P) {
+    return PackedRes{P.p0, P.rowsum, P.res_ptr, P.res_col, P.res_val};
 }
 
 static void free_packed(Packed *P) {
     if (P->planes) cudaFree(P->planes);
     if (P->rowsum) cudaFree(P->rowsum);
+    if (P->res_ptr) cudaFree(P->res_ptr);
+    if (P->res_col) cudaFree(P->res_col);
+    if (P->res_val) cudaFree(P->res_val);
     P->planes = nullptr;
     P->rowsum = nullptr;
+    P->res_ptr = P->res_col = nullptr;
+    P->res_val = nullptr;
+    P->nnz = 0;
 }
 
 // racc: RowAcc scratch with >= M zeroed entries (zero again on completion).
 
-typedef void (*PlanesKernel)(int64_t *, const uint4 *, const int64_t *, const int64_t *, int, int, int, int,
+typedef void (*PlanesKernel)(int64_t *, const uint4 *, const PackedRes, const int64_t *, int, int, int, int,
                              RowAcc *, const int64_t *);
 template <bool XS>
 static PlanesKernel planes_kernel(int np) {
@@ -194,7 +263,7 @@ static PlanesKernel planes_kernel(int np) {
     }
 }
 
-typedef void (*RowsKernel)(int64_t *, const uint4 *, const int64_t *, const int64_t *, int, int, int, int,
+typedef void (*RowsKernel)(int64_t *, const uint4 *, const PackedRes, const int64_t *, int, int, int, int,
                            const int64_t *);
 // Once per device and plane count: allow the largest staged-digit buffer
 // (the 48 KB default covers static + dynamic shared memory together) and
@@ -260,8 +329,8 @@ int launch_matvec_rows(int64_t *out, const Packed &P, const int64_t *x, cudaStre
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = S > 1 ? 2 : 1;
-    IQ_CUDA(cudaLaunchKernelEx(&cfg, kern, out, (const uint4 *)P.planes, (const int64_t *)P.rowsum, x, P.M, P.N,
-                               P.Kp, add, nrm_w));
+    IQ_CUDA(cudaLaunchKernelEx(&cfg, kern, out, (const uint4 *)P.planes, packed_res(P), x, P.M, P.N, P.Kp, add,
+                               nrm_w));
     IQ_CHECK_LAUNCH();
     return IQ_OK;
 }
@@ -300,8 +369,8 @@ int launch_matvec_planes(int64_t *out, const Packed &P, const int64_t *x, cudaSt
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    IQ_CUDA(cudaLaunchKernelEx(&cfg, kern, out, (const uint4 *)P.planes, (const int64_t *)P.rowsum, x, P.M, P.N,
-                               P.Kp, add, racc, nrm_w));
+    IQ_CUDA(cudaLaunchKernelEx(&cfg, kern, out, (const uint4 *)P.planes, packed_res(P), x, P.M, P.N, P.Kp, add,
+                               racc, nrm_w));
     IQ_CHECK_LAUNCH();
     return IQ_OK;
 }

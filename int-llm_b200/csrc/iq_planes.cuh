@@ -14,9 +14,17 @@
 // computed when the weights are packed. out = low64(sum >> 48) exactly as
 // matmul_vec (llama_int.c:1014-1046); every step is exact integer arithmetic.
 //
-// Only the np planes the matrix needs are kept (np = the most bytes any weight
-// needs as a signed integer; bf16-derived weights need 6): the top plane is
-// read as signed, the bytes above it being its sign extension.
+// Only a window of np planes p0 .. p0+np-1 is stored. The top is the most
+// bytes any weight needs as a signed integer (bf16-derived weights need 6),
+// read as signed, the bytes above it being its sign extension. Below, planes
+// p0 > 0 are dropped when few weights use them: each weight splits exactly
+// into w = w_hi + w_lo with w_lo = w & (2^(8 p0) - 1) (unsigned) and w_hi
+// having zero low bytes, so
+//   sum_k x_k w_k = 2^(8 p0) sum_{i,j} 2^{8(i+j)} P_ij - 2^63 sum_k w_hi,k
+//                   + sum_{k: w_lo,k != 0} x_k w_lo,k                 (mod 2^128)
+// with P_ij over the stored planes of w_hi; the last sum is a sparse per-row
+// residual (CSR) that the row's writer adds. Config weights (bf16-derived,
+// N(0, 0.02)) keep bytes 3..5: 3 bytes per weight, residual ~0.02% of them.
 // Packed layout (np bytes per weight, 8 for arbitrary int64): for each
 // 16-row x 32-column tile, np planes x 32 lanes x 16 bytes, where lane l holds
 // exactly its A fragment of mma.m16n8k32 (rows l/4 and l/4+8, columns
@@ -37,9 +45,22 @@ namespace iq {
 struct Packed {
     int M = 0, N = 0;       // logical shape: M rows of N columns
     int Mp = 0, Kp = 0;     // padded to 16 rows / 32 columns
-    int np = 8;             // byte planes stored (top plane signed), see plane_count
+    int np = 8;             // byte planes stored (top plane signed)
+    int p0 = 0;             // lowest stored plane
+    int nnz = 0;            // weights with nonzero bytes below p0 (residual entries)
     uint4 *planes = nullptr;
-    int64_t *rowsum = nullptr;  // [Mp][2] = 128-bit sum_k w[row][k] (lo, hi)
+    int64_t *rowsum = nullptr;  // [Mp][2] = 128-bit sum_k w_hi[row][k] (lo, hi)
+    int *res_ptr = nullptr;     // [Mp + 1] CSR row offsets (nullptr when nnz == 0)
+    int *res_col = nullptr;     // [nnz] column
+    int64_t *res_val = nullptr; // [nnz] w_lo
+};
+
+// What a kernel needs of a Packed beyond the planes (passed by value).
+struct PackedRes {
+    int p0;
+    const int64_t *rowsum;
+    const int *ptr, *col;
+    const int64_t *val;
 };
 
 // Per-row scratch for rows whose columns are split between warps: a 128-bit
@@ -69,18 +90,60 @@ __device__ __forceinline__ int bytes_needed(int64_t w) {
     int bits = 64 - __clzll((long long)m) + 1;          // + sign bit
     return (bits + 7) / 8;
 }
-__global__ void k_plane_count(int *__restrict__ np, const int64_t *__restrict__ W, int64_t n) {
+// Plane statistics: st[0] = max bytes_needed; st[1 + b] (b = 0..7) = number of
+// weights whose lowest nonzero byte is b (zero weights are not counted).
+__global__ void k_plane_count(unsigned long long *__restrict__ st, const int64_t *__restrict__ W, int64_t n) {
+    __shared__ unsigned long long hist[8];
+    if (threadIdx.x < 8) hist[threadIdx.x] = 0;
+    __syncthreads();
     int mx = 1;
-    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x)
-        mx = max(mx, bytes_needed(W[e]));
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t w = W[e];
+        mx = max(mx, bytes_needed(w));
+        if (w != 0) atomicAdd(&hist[(__ffsll(w) - 1) >> 3], 1ull);
+    }
     for (int m = 16; m >= 1; m >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, m));
-    if ((threadIdx.x & 31) == 0) atomicMax(np, mx);
+    if ((threadIdx.x & 31) == 0) atomicMax(&st[0], (unsigned long long)mx);
+    __syncthreads();
+    if (threadIdx.x < 8 && hist[threadIdx.x]) atomicAdd(&st[1 + threadIdx.x], hist[threadIdx.x]);
+}
+
+// Residual entries per row (weights with nonzero bytes below p0), one warp per row.
+__global__ void k_res_count(int *__restrict__ cnt, const int64_t *__restrict__ W, int M, int N, uint64_t mask) {
+    const int lane = threadIdx.x & 31;
+    for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < M;
+         row += gridDim.x * (blockDim.x >> 5)) {
+        int c = 0;
+        for (int k = lane; k < N; k += 32) c += ((uint64_t)W[(size_t)row * N + k] & mask) != 0;
+        for (int m = 16; m >= 1; m >>= 1) c += __shfl_xor_sync(0xffffffffu, c, m);
+        if (lane == 0) cnt[row] = c;
+    }
+}
+// Fills the CSR residual in column order (warp ballot per 32 columns).
+__global__ void k_res_fill(int *__restrict__ col, int64_t *__restrict__ val, const int *__restrict__ ptr,
+                           const int64_t *__restrict__ W, int M, int N, uint64_t mask) {
+    const int lane = threadIdx.x & 31;
+    for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < M;
+         row += gridDim.x * (blockDim.x >> 5)) {
+        int o = ptr[row];
+        for (int k0 = 0; k0 < N; k0 += 32) {
+            const int k = k0 + lane;
+            const uint64_t lo = k < N ? (uint64_t)W[(size_t)row * N + k] & mask : 0;
+            const unsigned b = __ballot_sync(0xffffffffu, lo != 0);
+            if (lo) {
+                const int at = o + __popc(b & ((1u << lane) - 1));
+                col[at] = k;
+                val[at] = (int64_t)lo;
+            }
+            o += __popc(b);
+        }
+    }
 }
 
 // One thread per (row tile, column tile, lane): gathers the 16 weights of the
 // lane's A fragment and writes its 16 bytes in each of the np planes.
 __global__ void k_pack_planes(uint4 *__restrict__ planes, const int64_t *__restrict__ W, int M, int N,
-                              int KT, int64_t total, int np) {
+                              int KT, int64_t total, int np, int p0) {
     for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
          e += (int64_t)gridDim.x * blockDim.x) {
         const int lane = (int)(e & 31);
@@ -107,7 +170,7 @@ __global__ void k_pack_planes(uint4 *__restrict__ planes, const int64_t *__restr
             for (int r = 0; r < 4; r++) {
                 uint32_t b = 0;
 #pragma unroll
-                for (int j = 0; j < 4; j++) b |= (uint32_t)((w[r][j] >> (8 * p)) & 0xff) << (8 * j);
+                for (int j = 0; j < 4; j++) b |= (uint32_t)((w[r][j] >> (8 * (p0 + p))) & 0xff) << (8 * j);
                 v[r] = b;
             }
             dst[p * 32] = make_uint4(v[0], v[1], v[2], v[3]);
@@ -115,14 +178,15 @@ __global__ void k_pack_planes(uint4 *__restrict__ planes, const int64_t *__restr
     }
 }
 
-// 128-bit row sums of W (one warp per row).
-__global__ void k_row_sums(int64_t *__restrict__ rs, const int64_t *__restrict__ W, int M, int N, int Mp) {
+// 128-bit row sums of W with the bits in lo_mask cleared (one warp per row).
+__global__ void k_row_sums(int64_t *__restrict__ rs, const int64_t *__restrict__ W, int M, int N, int Mp,
+                           uint64_t lo_mask = 0) {
     const int lane = threadIdx.x & 31;
     for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < Mp;
          row += gridDim.x * (blockDim.x >> 5)) {
         i128 s = 0;
         if (row < M)
-            for (int k = lane; k < N; k += 32) s += (i128)W[(size_t)row * N + k];
+            for (int k = lane; k < N; k += 32) s += (i128)(int64_t)((uint64_t)W[(size_t)row * N + k] & ~lo_mask);
         s = warp_sum_i128(s);
         if (lane == 0) {
             rs[2 * row] = (int64_t)(uint64_t)s;
@@ -169,6 +233,32 @@ __device__ __forceinline__ void fold_planes(int (&c)[NP][4], int t, i128 &r0, i1
     }
 }
 
+// The row's result from its 128-bit plane sum `acc` (stored planes, before the
+// 2^(8 p0) scale): scale, subtract 2^63 sum w_hi, add the sparse residual
+// sum x_k w_lo,k (x from the staged digits when xd != nullptr, else from xg),
+// then low64(>> 48) (llama_int.c:1044).
+__device__ __forceinline__ int64_t finish_row(i128 acc, int row, const PackedRes &R,
+                                              const unsigned char *xd, int ld, const int64_t *__restrict__ xg) {
+    i128 ws = (i128)(((u128)(uint64_t)R.rowsum[2 * row + 1] << 64) | (uint64_t)R.rowsum[2 * row]);
+    u128 v = ((u128)acc << (8 * R.p0)) - ((u128)ws << 63);
+    if (R.ptr) {
+        for (int e = R.ptr[row], e1 = R.ptr[row + 1]; e < e1; e++) {
+            const int k = R.col[e];
+            int64_t xk;
+            if (xd) {
+                uint64_t xu = 0;
+#pragma unroll
+                for (int j = 0; j < 8; j++) xu |= (uint64_t)xd[j * ld + k] << (8 * j);
+                xk = (int64_t)(xu ^ 0x8000000000000000ull);
+            } else {
+                xk = xg[k];
+            }
+            v += (u128)((i128)xk * R.val[e]);
+        }
+    }
+    return (int64_t)((i128)v >> 48);
+}
+
 // 4 digits j of x_u[k..k+3] packed into one word (byte i = element k+i)
 __device__ __forceinline__ uint32_t digit_word(const int64_t *__restrict__ xg, int N, int k, int j) {
     uint32_t v = 0;
@@ -213,7 +303,7 @@ __device__ __forceinline__ void stage_digits(unsigned char *xd, int ld, const in
 // x in global memory (L1-cached) per column tile.
 template <int NP, bool XSMEM>
 __global__ void __launch_bounds__(256, 2)
-k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const int64_t *__restrict__ rowsum,
+k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const PackedRes R,
                 const int64_t *__restrict__ xg, int M, int N, int Kp, int add, RowAcc *__restrict__ racc,
                 const int64_t *__restrict__ nrm_w) {
     extern __shared__ __align__(16) unsigned char xd[];  // [8][Kp + 16] digit rows
@@ -312,10 +402,8 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
                         }
                     }
                     if (write) {
-                        i128 ws = (i128)(((u128)(uint64_t)rowsum[2 * row + 1] << 64) | (uint64_t)rowsum[2 * row]);
-                        i128 sres = (i128)((u128)fin - ((u128)ws << 63));
+                        int64_t val = finish_row(fin, row, R, XSMEM ? xd : nullptr, ld, xg);
                         // add != 0: residual epilogue out += result (int64 wrap, llama_int.c:1535, 1556)
-                        int64_t val = (int64_t)(sres >> 48);
                         out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)val) : val;
                     }
                 }
@@ -338,7 +426,7 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
 // result is the same integer (addition mod 2^128 is associative).
 template <int NP>
 __global__ void __launch_bounds__(256, 2)
-k_matvec_rows(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const int64_t *__restrict__ rowsum,
+k_matvec_rows(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const PackedRes R,
               const int64_t *__restrict__ xg, int M, int N, int Kp, int add, const int64_t *__restrict__ nrm_w) {
     extern __shared__ __align__(16) unsigned char xd[];  // [8][Kp + 16] digit rows
     __shared__ __align__(16) unsigned long long wpart[8][16][2];  // per warp: 16 row partials (lo, hi)
@@ -436,8 +524,7 @@ k_matvec_rows(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const
         }
         const int row = rt * 16 + (int)threadIdx.x;
         if (threadIdx.x < 16 && row < M) {
-            i128 ws = (i128)(((u128)(uint64_t)rowsum[2 * row + 1] << 64) | (uint64_t)rowsum[2 * row]);
-            int64_t val = (int64_t)((i128)((u128)v - ((u128)ws << 63)) >> 48);
+            const int64_t val = finish_row(v, row, R, xd, ld, xg);
             out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)val) : val;
         }
         __syncthreads();  // wpart is rewritten by the next tile
