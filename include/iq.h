@@ -86,13 +86,19 @@ IQ_API int iq_matvec_dev(int64_t *d_out, const int64_t *d_w, const int64_t *d_in
                          int M, int N, void *stream);
 
 /* Weights repacked for the int8 tensor cores: each int64 weight split into
- * its 8 bytes (byte planes), stored in mma fragment order, plus 128-bit row
- * sums; 8 bytes per weight as before. No reference counterpart: the
- * reference multiplies the int64 matrix directly (llama_int.c:1014-1046).
- * iq_matvec_packed_dev gives results bit-identical to matmul_vec. */
+ * its bytes (byte planes), stored in mma fragment order, plus 128-bit row
+ * sums. Only a window of planes is stored: the bytes no weight needs at the
+ * top, and low bytes that few weights use, whose values go to an exact sparse
+ * per-row residual (at most 8 bytes per weight in all). No reference
+ * counterpart: the reference multiplies the int64 matrix directly
+ * (llama_int.c:1014-1046). iq_matvec_packed_dev gives results bit-identical
+ * to matmul_vec. */
 typedef struct iq_packed iq_packed;
 IQ_API int iq_pack_weights_dev(const int64_t *d_w, int M, int N, void *stream, iq_packed **out);
 IQ_API int iq_packed_free(iq_packed *p);
+/* The stored window: planes p0 .. p0 + np - 1 (bytes of each weight), and
+ * the number of residual entries (weights with nonzero bytes below p0). */
+IQ_API int iq_packed_info(const iq_packed *p, int *np, int *p0, int *residual_entries);
 IQ_API int iq_matvec_packed_dev(int64_t *d_out, const iq_packed *w, const int64_t *d_in, void *stream);
 
 /* Same result as iq_matvec_packed_dev, but allocates no device memory: for

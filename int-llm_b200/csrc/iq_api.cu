@@ -765,6 +765,14 @@ IQ_API int iq_packed_free(iq_packed *p) {
     return IQ_OK;
 }
 
+IQ_API int iq_packed_info(const iq_packed *p, int *np, int *p0, int *residual_entries) {
+    if (!p || !np || !p0 || !residual_entries) return IQ_ERR_ARG;
+    *np = p->P.np;
+    *p0 = p->P.p0;
+    *residual_entries = p->P.nnz;
+    return IQ_OK;
+}
+
 IQ_API int iq_matvec_packed_dev(int64_t *d_out, const iq_packed *w, const int64_t *d_in, void *stream) {
     if (!d_out || !w || !d_in || d_out == d_in) return IQ_ERR_ARG;
     int dev, rc;

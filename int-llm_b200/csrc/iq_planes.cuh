@@ -299,14 +299,41 @@ __device__ __forceinline__ void stage_digits(unsigned char *xd, int ld, const in
     __syncthreads();
 }
 
-// XSMEM: digits staged in shared memory (Kp small enough), else gathered from
-// x in global memory (L1-cached) per column tile.
+// Weight tiles in flight per warp: a register ring of D tiles, deeper when a
+// tile is smaller (fewer planes), so the bytes in flight stay about constant.
+// The ring is indexed statically (the unit loop is unrolled by D).
+template <int NP>
+__host__ __device__ constexpr int ring_depth() {
+    return NP <= 2 ? 6 : NP == 3 ? 4 : NP == 4 ? 3 : 2;
+}
+
+template <int NP>
+__device__ __forceinline__ void load_tile(uint4 (&dst)[NP], const uint4 *src) {
+#pragma unroll
+    for (int p = 0; p < NP; p++) dst[p] = ld_stream_u4(src + p * 32);
+}
+
+template <int NP>
+__device__ __forceinline__ void mma_tile(int (&c)[NP][4], const uint4 (&a)[NP], uint32_t b0, uint32_t b1) {
+#pragma unroll
+    for (int p = 0; p < NP - 1; p++) mma_i8<false>(c[p], a[p], b0, b1);
+    mma_i8<true>(c[NP - 1], a[NP - 1], b0, b1);  // top plane: signed
+}
+
+// Stream-K kernel. XSMEM: digits staged in shared memory (Kp small enough),
+// else gathered from x in global memory (L1-cached) per column tile.
+// Each warp walks its units linearly (row tile-major, the packed layout's
+// order) with ring_depth<NP>() tiles in flight; the first D-1 are requested
+// before griddepcontrol.wait (weights are static), overlapping the previous
+// kernel's tail and the digit staging.
 template <int NP, bool XSMEM>
 __global__ void __launch_bounds__(256, 2)
 k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const PackedRes R,
                 const int64_t *__restrict__ xg, int M, int N, int Kp, int add, RowAcc *__restrict__ racc,
                 const int64_t *__restrict__ nrm_w) {
     extern __shared__ __align__(16) unsigned char xd[];  // [8][Kp + 16] digit rows
+    constexpr int D = ring_depth<NP>();
+    constexpr int TS = NP * 32;  // uint4 per packed tile
     const int ld = Kp + 16;
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int KT = Kp / 32, RT = (M + 15) / 16;
@@ -317,24 +344,16 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
     // Programmatic dependent launch: let the next kernel in the stream start its
     // own prologue now; it waits (griddepcontrol.wait) for this grid's results.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    // the first weight tile (static data) is requested before waiting for the
-    // previous kernel and before the x digits are staged, so the latencies overlap
-    constexpr int TS = NP * 32;  // uint4 per packed tile
-    uint4 pre[NP];
-    if (u0 < u1) {
-        const uint4 *tp0 = planes + (size_t)u0 * TS + lane;
+    const uint4 *pl = planes + lane;
+    uint4 buf[D][NP];
 #pragma unroll
-        for (int p = 0; p < NP; p++) pre[p] = ld_stream_u4(tp0 + p * 32);
-    }
+    for (int s = 0; s < D - 1; s++)
+        if (u0 + s < u1) load_tile<NP>(buf[s], pl + (size_t)(u0 + s) * TS);
     // x and (with add) out are produced by the previous kernel
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (XSMEM) stage_digits(xd, ld, xg, N, Kp, nrm_w);
-
     const unsigned char *xb = xd + g * ld + 4 * t;
 
-    // Linear walk over this warp's units (row tile-major, the packed layout's
-    // order): the next unit's 8 loads are issued before the current unit's MMAs,
-    // so every warp keeps two 4 KB tiles in flight.
     int c[NP][4];
 #pragma unroll
     for (int p = 0; p < NP; p++)
@@ -343,87 +362,83 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
     i128 r0 = 0, r1 = 0;
     int since_fold = 0;
     int rt = (int)(u0 / KT), k0 = (int)(u0 - (int64_t)rt * KT);
-    uint4 cur[NP];
+    for (int64_t ub = u0; ub < u1; ub += D) {
 #pragma unroll
-    for (int p = 0; p < NP; p++) cur[p] = pre[p];
-    for (int64_t u = u0; u < u1; u++) {
-        uint4 nxt[NP];
-        if (u + 1 < u1) {
-            const uint4 *tn = planes + (size_t)(u + 1) * TS + lane;
-#pragma unroll
-            for (int p = 0; p < NP; p++) nxt[p] = ld_stream_u4(tn + p * 32);
-        }
-        const int kt = (int)(u - (int64_t)rt * KT);
-        const int kk = kt * 32;
-        uint32_t b0, b1;
-        if (XSMEM) {
-            b0 = *reinterpret_cast<const uint32_t *>(xb + kk);
-            b1 = *reinterpret_cast<const uint32_t *>(xb + kk + 16);
-        } else {
-            b0 = digit_word(xg, N, kk + 4 * t, g);
-            b1 = digit_word(xg, N, kk + 16 + 4 * t, g);
-        }
-#pragma unroll
-        for (int p = 0; p < NP - 1; p++) mma_i8<false>(c[p], cur[p], b0, b1);
-        mma_i8<true>(c[NP - 1], cur[NP - 1], b0, b1);  // top plane: signed
-        if (++since_fold >= 1024) { fold_planes(c, t, r0, r1); since_fold = 0; }
-        const bool seg_end = (u + 1 == u1) || (kt + 1 == KT);
-        if (seg_end) {
-            const int k1 = kt + 1;
-            fold_planes(c, t, r0, r1);
-            since_fold = 0;
-            // the 4 lanes of a row group hold the 8 digits: reduce over t
-#pragma unroll
-            for (int m = 1; m <= 2; m <<= 1) {
-                r0 += shfl_xor_i128(r0, m);
-                r1 += shfl_xor_i128(r1, m);
+        for (int s = 0; s < D; s++) {
+            const int64_t u = ub + s;
+            if (u >= u1) break;
+            if (u + D - 1 < u1) load_tile<NP>(buf[(s + D - 1) % D], pl + (size_t)(u + D - 1) * TS);
+            const int kt = (int)(u - (int64_t)rt * KT);
+            const int kk = kt * 32;
+            uint32_t b0, b1;
+            if (XSMEM) {
+                b0 = *reinterpret_cast<const uint32_t *>(xb + kk);
+                b1 = *reinterpret_cast<const uint32_t *>(xb + kk + 16);
+            } else {
+                b0 = digit_word(xg, N, kk + 4 * t, g);
+                b1 = digit_word(xg, N, kk + 16 + 4 * t, g);
             }
-            if (t == 0) {
+            mma_tile<NP>(c, buf[s], b0, b1);
+            if (++since_fold >= 1024) { fold_planes(c, t, r0, r1); since_fold = 0; }
+            if ((u + 1 == u1) || (kt + 1 == KT)) {  // segment end: flush this row tile's part
+                const int k1 = kt + 1;
+                fold_planes(c, t, r0, r1);
+                since_fold = 0;
+                // the 4 lanes of a row group hold the 8 digits: reduce over t
 #pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    const int row = rt * 16 + g + 8 * h;
-                    if (row >= M) continue;
-                    i128 part = h ? r1 : r0;
-                    i128 fin = 0;
-                    bool write = false;
-                    if (k0 == 0 && k1 == KT) { fin = part; write = true; }
-                    else {
-                        RowAcc *ra = racc + row;
-                        atomic_add_i128(ra, part);
-                        // release our partial / acquire everyone else's with the counter
-                        cuda::atomic_ref<unsigned int, cuda::thread_scope_device> done(ra->done);
-                        unsigned int prev = done.fetch_add((unsigned int)(k1 - k0), cuda::memory_order_acq_rel);
-                        if (prev + (unsigned int)(k1 - k0) == (unsigned int)KT) {
-                            unsigned long long lo = atomicExch(&ra->lo, 0ull);
-                            unsigned long long hi = atomicExch(&ra->hi, 0ull);
-                            atomicExch(&ra->done, 0u);
-                            fin = (i128)(((u128)hi << 64) | lo);
-                            write = true;
+                for (int m = 1; m <= 2; m <<= 1) {
+                    r0 += shfl_xor_i128(r0, m);
+                    r1 += shfl_xor_i128(r1, m);
+                }
+                if (t == 0) {
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        const int row = rt * 16 + g + 8 * h;
+                        if (row >= M) continue;
+                        i128 part = h ? r1 : r0;
+                        i128 fin = 0;
+                        bool write = false;
+                        if (k0 == 0 && k1 == KT) { fin = part; write = true; }
+                        else {
+                            RowAcc *ra = racc + row;
+                            atomic_add_i128(ra, part);
+                            // release our partial / acquire everyone else's with the counter
+                            cuda::atomic_ref<unsigned int, cuda::thread_scope_device> done(ra->done);
+                            unsigned int prev = done.fetch_add((unsigned int)(k1 - k0), cuda::memory_order_acq_rel);
+                            if (prev + (unsigned int)(k1 - k0) == (unsigned int)KT) {
+                                unsigned long long lo = atomicExch(&ra->lo, 0ull);
+                                unsigned long long hi = atomicExch(&ra->hi, 0ull);
+                                atomicExch(&ra->done, 0u);
+                                fin = (i128)(((u128)hi << 64) | lo);
+                                write = true;
+                            }
+                        }
+                        if (write) {
+                            int64_t val = finish_row(fin, row, R, XSMEM ? xd : nullptr, ld, xg);
+                            // add != 0: residual epilogue out += result (int64 wrap, llama_int.c:1535, 1556)
+                            out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)val) : val;
                         }
                     }
-                    if (write) {
-                        int64_t val = finish_row(fin, row, R, XSMEM ? xd : nullptr, ld, xg);
-                        // add != 0: residual epilogue out += result (int64 wrap, llama_int.c:1535, 1556)
-                        out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)val) : val;
-                    }
                 }
+                r0 = 0;
+                r1 = 0;
+                rt += 1;
+                k0 = 0;
             }
-            r0 = 0;
-            r1 = 0;
-            rt += 1;
-            k0 = 0;
         }
-#pragma unroll
-        for (int p = 0; p < NP; p++) cur[p] = nxt[p];
     }
 }
 
 // Row-owned variant: a cluster of S CTAs (S = 1, 2, 4 or 8) owns one 16-row
-// tile (S = 1: a CTA owns every gridDim-th tile in turn), its 8*S warps split the
-// column tiles evenly, the warps' 128-bit partials are summed in shared
-// memory and the S CTA sums in rank 0's shared memory (distributed shared
-// memory), which writes the 16 outputs. No global atomics and no scratch; the
-// result is the same integer (addition mod 2^128 is associative).
+// tile (S = 1: a CTA owns every gridDim-th tile in turn), its 8*S warps split
+// the column tiles evenly (nk each; the last ones may hold fewer or none),
+// the warps' 128-bit partials are summed in shared memory and the S CTA sums
+// in rank 0's shared memory (distributed shared memory), which writes the 16
+// outputs. No global atomics and no scratch; the result is the same integer
+// (addition mod 2^128 is associative). Every warp runs the same number of
+// unit steps (ntiles * nk, empty ones skipped), so the per-tile barriers are
+// reached in step. Staged digits only (Kp <= 12784: fewer than 1024 column
+// tiles per warp, so the int32 plane sums cannot overflow before the fold).
 template <int NP>
 __global__ void __launch_bounds__(256, 2)
 k_matvec_rows(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const PackedRes R,
@@ -431,6 +446,8 @@ k_matvec_rows(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const
     extern __shared__ __align__(16) unsigned char xd[];  // [8][Kp + 16] digit rows
     __shared__ __align__(16) unsigned long long wpart[8][16][2];  // per warp: 16 row partials (lo, hi)
     __shared__ __align__(16) unsigned long long cpart[8][16][2];  // per cluster rank (read in rank 0)
+    constexpr int D = ring_depth<NP>();
+    constexpr int TS = NP * 32;  // uint4 per packed tile
     const int ld = Kp + 16;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
     const int KT = Kp / 32, RT = (M + 15) / 16;
@@ -440,96 +457,98 @@ k_matvec_rows(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const
     // row tiles rt0, rt0 + stride, ... (one tile per cluster when S > 1)
     const int rt0 = blockIdx.x / S, stride = gridDim.x / S;
     const int ntiles = rt0 < RT ? (RT - 1 - rt0) / stride + 1 : 0;
-    const int wi = crank * 8 + warp, nwi = S * 8;
-    const int k0 = KT * wi / nwi, k1 = KT * (wi + 1) / nwi;
-    constexpr int TS = NP * 32;  // uint4 per packed tile
+    const int nwi = S * 8, nk = (KT + nwi - 1) / nwi;
+    const int k0 = (crank * 8 + warp) * nk, k1 = min(KT, k0 + nk);
+    const int total = ntiles * nk;  // unit steps, the same for every warp of the cluster
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // every CTA of the cluster must be running before rank 0's shared memory is
     // written: arrive now, wait just before the write
     if (S > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-    const uint4 *pl = planes + lane;
-    uint4 cur[NP];
-    if (ntiles > 0 && k0 < k1) {
-        const uint4 *tp0 = pl + ((size_t)rt0 * KT + k0) * TS;
+    // prefetch cursor: step pj of the tile whose column tile k0 starts at pbase
+    // (unit step q is tile q / nk, column tile k0 + q % nk; empty past k1)
+    int pj = 0;
+    const uint4 *pbase = planes + lane + ((size_t)rt0 * KT + k0) * TS;
+    const size_t tile_step = (size_t)stride * KT * TS;
+    auto prefetch = [&](uint4 (&dst)[NP]) {
+        if (k0 + pj < k1) load_tile<NP>(dst, pbase + (size_t)pj * TS);
+        if (++pj == nk) { pj = 0; pbase += tile_step; }
+    };
+    uint4 buf[D][NP];
 #pragma unroll
-        for (int p = 0; p < NP; p++) cur[p] = ld_stream_u4(tp0 + p * 32);
-    }
+    for (int s = 0; s < D - 1; s++)
+        if (s < total) prefetch(buf[s]);
     // x and (with add) out are produced by the previous kernel
     asm volatile("griddepcontrol.wait;" ::: "memory");
     stage_digits(xd, ld, xg, N, Kp, nrm_w);
     const unsigned char *xb = xd + g * ld + 4 * t;
-    for (int i = 0; i < ntiles; i++) {
-        const int rt = rt0 + i * stride;
-        int c[NP][4];
+    int c[NP][4];
 #pragma unroll
-        for (int p = 0; p < NP; p++)
+    for (int p = 0; p < NP; p++)
 #pragma unroll
-            for (int q = 0; q < 4; q++) c[p][q] = 0;
-        i128 r0 = 0, r1 = 0;
-        int since_fold = 0;
-        for (int kt = k0; kt < k1; kt++) {
-            // the next unit: this tile's next column tile, else the next tile's first
-            uint4 nxt[NP];
-            const bool more = kt + 1 < k1 || i + 1 < ntiles;
-            if (more) {
-                const size_t un = kt + 1 < k1 ? (size_t)rt * KT + kt + 1 : (size_t)(rt + stride) * KT + k0;
-                const uint4 *tn = pl + un * TS;
+        for (int q = 0; q < 4; q++) c[p][q] = 0;
+    int j = 0, rt = rt0;  // current step within the tile, current tile
+    for (int qb = 0; qb < total; qb += D) {
 #pragma unroll
-                for (int p = 0; p < NP; p++) nxt[p] = ld_stream_u4(tn + p * 32);
+        for (int s = 0; s < D; s++) {
+            const int q = qb + s;
+            if (q >= total) break;
+            if (q + D - 1 < total) prefetch(buf[(s + D - 1) % D]);
+            const int kt = k0 + j;
+            if (kt < k1) {
+                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(xb + kt * 32);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t *>(xb + kt * 32 + 16);
+                mma_tile<NP>(c, buf[s], b0, b1);
             }
-            const uint32_t b0 = *reinterpret_cast<const uint32_t *>(xb + kt * 32);
-            const uint32_t b1 = *reinterpret_cast<const uint32_t *>(xb + kt * 32 + 16);
+            if (++j < nk) continue;
+            // ---- end of this warp's part of tile rt: reduce and write
+            j = 0;
+            i128 r0 = 0, r1 = 0;
+            fold_planes(c, t, r0, r1);
 #pragma unroll
-            for (int p = 0; p < NP - 1; p++) mma_i8<false>(c[p], cur[p], b0, b1);
-            mma_i8<true>(c[NP - 1], cur[NP - 1], b0, b1);  // top plane: signed
-            if (++since_fold >= 1024) { fold_planes(c, t, r0, r1); since_fold = 0; }
-#pragma unroll
-            for (int p = 0; p < NP; p++) cur[p] = nxt[p];
-        }
-        fold_planes(c, t, r0, r1);
-#pragma unroll
-        for (int m = 1; m <= 2; m <<= 1) {  // the 4 lanes of a row group hold the 8 digits
-            r0 += shfl_xor_i128(r0, m);
-            r1 += shfl_xor_i128(r1, m);
-        }
-        if (t == 0) {
-            wpart[warp][g][0] = (uint64_t)r0; wpart[warp][g][1] = (uint64_t)((u128)r0 >> 64);
-            wpart[warp][g + 8][0] = (uint64_t)r1; wpart[warp][g + 8][1] = (uint64_t)((u128)r1 >> 64);
-        }
-        __syncthreads();
-        i128 v = 0;
-        if (threadIdx.x < 16) {
-#pragma unroll
-            for (int w = 0; w < 8; w++)
-                v += (i128)(((u128)wpart[w][threadIdx.x][1] << 64) | wpart[w][threadIdx.x][0]);
-        }
-        if (S > 1) {
-            asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+            for (int m = 1; m <= 2; m <<= 1) {  // the 4 lanes of a row group hold the 8 digits
+                r0 += shfl_xor_i128(r0, m);
+                r1 += shfl_xor_i128(r1, m);
+            }
+            if (t == 0) {
+                wpart[warp][g][0] = (uint64_t)r0; wpart[warp][g][1] = (uint64_t)((u128)r0 >> 64);
+                wpart[warp][g + 8][0] = (uint64_t)r1; wpart[warp][g + 8][1] = (uint64_t)((u128)r1 >> 64);
+            }
+            __syncthreads();
+            i128 v = 0;
             if (threadIdx.x < 16) {
-                uint32_t remote;
-                asm volatile("mapa.shared::cluster.u32 %0, %1, 0;"
-                             : "=r"(remote)
-                             : "r"((uint32_t)__cvta_generic_to_shared(&cpart[crank][threadIdx.x][0])));
-                asm volatile("st.shared::cluster.v2.u64 [%0], {%1, %2};"
-                             :: "r"(remote), "l"((uint64_t)v), "l"((uint64_t)((u128)v >> 64)) : "memory");
+#pragma unroll
+                for (int w = 0; w < 8; w++)
+                    v += (i128)(((u128)wpart[w][threadIdx.x][1] << 64) | wpart[w][threadIdx.x][0]);
             }
-            asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-            asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-            if (crank != 0) return;  // one tile per cluster
-            if (threadIdx.x < 16) {
-                v = 0;
-                for (uint32_t r = 0; r < S; r++)
-                    v += (i128)(((u128)cpart[r][threadIdx.x][1] << 64) | cpart[r][threadIdx.x][0]);
+            if (S > 1) {
+                asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+                if (threadIdx.x < 16) {
+                    uint32_t remote;
+                    asm volatile("mapa.shared::cluster.u32 %0, %1, 0;"
+                                 : "=r"(remote)
+                                 : "r"((uint32_t)__cvta_generic_to_shared(&cpart[crank][threadIdx.x][0])));
+                    asm volatile("st.shared::cluster.v2.u64 [%0], {%1, %2};"
+                                 :: "r"(remote), "l"((uint64_t)v), "l"((uint64_t)((u128)v >> 64)) : "memory");
+                }
+                asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+                asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+                if (crank != 0) return;  // one tile per cluster
+                if (threadIdx.x < 16) {
+                    v = 0;
+                    for (uint32_t r = 0; r < S; r++)
+                        v += (i128)(((u128)cpart[r][threadIdx.x][1] << 64) | cpart[r][threadIdx.x][0]);
+                }
             }
+            const int row = rt * 16 + (int)threadIdx.x;
+            if (threadIdx.x < 16 && row < M) {
+                const int64_t val = finish_row(v, row, R, xd, ld, xg);
+                out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)val) : val;
+            }
+            __syncthreads();  // wpart is rewritten by the next tile
+            rt += stride;
         }
-        const int row = rt * 16 + (int)threadIdx.x;
-        if (threadIdx.x < 16 && row < M) {
-            const int64_t val = finish_row(v, row, R, xd, ld, xg);
-            out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)val) : val;
-        }
-        __syncthreads();  // wpart is rewritten by the next tile
     }
-    if (S > 1 && ntiles == 0) {  // keep the cluster barrier phases matched
+    if (S > 1 && total == 0) {  // keep the cluster barrier phases matched
         asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
         asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
         asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");

@@ -36,6 +36,7 @@ SIGNATURES = {
     "iq_gemm_dev": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "iq_pack_weights_dev": (_I, [_P, _I, _I, _P, _P]),
     "iq_packed_free": (_I, [_P]),
+    "iq_packed_info": (_I, [_P, _P, _P, _P]),
     "iq_matvec_packed_dev": (_I, [_P, _P, _P, _P]),
     "iq_matvec_packed_noalloc_dev": (_I, [_P, _P, _P, _P]),
     "iq_pack_weights_tc_dev": (_I, [_P, _I, _I, _P, _P]),
@@ -180,6 +181,12 @@ class Packed:
         self.h = ctypes.c_void_p()
         self.M, self.N = M, N
         _call("iq_pack_weights_dev", _dp(d_w), M, N, _sp(stream), ctypes.byref(self.h))
+
+    def info(self):
+        """(np, p0, residual_entries): stored planes p0 .. p0+np-1 and the sparse residual size."""
+        a, b, c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        _call("iq_packed_info", self.h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c))
+        return a.value, b.value, c.value
 
     def free(self):
         if self.h:

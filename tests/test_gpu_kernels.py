@@ -289,3 +289,42 @@ def test_plane_count_matvec_and_gemm(n):
     iq.gemm_tc_dev(dg, pt, dev(X), rows)
     assert (host(dg) == orc.matmul_rows(w, X)).all()
     pk.free(); pt.free()
+
+
+def test_plane_window_config_weights():
+    """bf16-derived config weights keep planes 3..5 (3 bytes per weight) and put
+    the few weights with nonzero low bytes into the sparse residual."""
+    import torch
+    w = orc.synth_weights(1, "w:window", (2048, 2048))
+    pk = iq.Packed(dev(w), 2048, 2048)
+    np_, p0, nnz = pk.info()
+    low = (w.view(np.uint64) & np.uint64((1 << 8 * p0) - 1)) != 0
+    assert (np_, p0) == (3, 3) and nnz == int(low.sum()) and 0 < nnz < 2048 * 2048 // 1024
+    x = orc.synth_acts(1, "x:window", (2048,))
+    do = torch.zeros(2048, dtype=torch.int64, device="cuda")
+    iq.matvec_packed_dev(do, pk, dev(x))
+    assert (host(do) == orc.matmul_vec(w, x)).all()
+    pk.free()
+
+
+@pytest.mark.parametrize("M,N", [(300, 2048), (9600, 64)])
+def test_plane_window_residual_edges(M, N):
+    """Weights whose high bytes fit planes 3..5 with planted low-byte entries:
+    a row holding many of them, first and last rows and columns, negative
+    weights and full-range activations (row-owned and stream-K kernels)."""
+    import torch
+    rng = np.random.default_rng(M + N)
+    w = rng.integers(-(1 << 23), 1 << 23, (M, N), dtype=np.int64) << 24   # bytes 3..5 only
+    planted = [(7, k) for k in range(0, N, max(1, N // 40))] + [(0, 0), (M - 1, N - 1), (M // 2, 1)]
+    for r, k in planted:
+        w[r, k] += int(rng.integers(1, 1 << 24))
+    w[3, 5] = -int(rng.integers(1, 1 << 24))    # a negative weight with low bytes
+    x = rand_full(rng, (N,))
+    pk = iq.Packed(dev(w), M, N)
+    np_, p0, nnz = pk.info()
+    assert p0 == 3 and np_ == 3 and nnz == int(((w.view(np.uint64) & np.uint64(0xFFFFFF)) != 0).sum())
+    for _ in range(2):
+        do = torch.zeros(M, dtype=torch.int64, device="cuda")
+        iq.matvec_packed_dev(do, pk, dev(x))
+        assert (host(do) == orc.matmul_vec(w, x)).all()
+    pk.free()
