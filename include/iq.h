@@ -124,6 +124,10 @@ IQ_API int iq_matvec_packed_noalloc_dev(int64_t *d_out, const iq_packed *w, cons
 typedef struct iq_packed_tc iq_packed_tc;
 IQ_API int iq_pack_weights_tc_dev(const int64_t *d_w, int M, int N, void *stream, iq_packed_tc **out);
 IQ_API int iq_packed_tc_free(iq_packed_tc *p);
+/* The GEMM form's stored window and residual size, as iq_packed_info (the
+ * GEMM keeps a residual only when it is nearly empty: its epilogue pays more
+ * per entry than the matvec's). */
+IQ_API int iq_packed_tc_info(const iq_packed_tc *p, int *np, int *p0, int *residual_entries);
 IQ_API int iq_gemm_tc_dev(int64_t *d_out, const iq_packed_tc *w, const int64_t *d_X, int rows, void *stream);
 
 /* Synchronises the current device and returns (and clears) the status that

@@ -160,23 +160,47 @@ static int count_planes(const int64_t *d_w, int64_t n, cudaStream_t s, int *np) 
 // Lowest stored plane: the p0 that saves the most bytes, counting each
 // residual entry (4-byte column + 8-byte value + its share of row offsets)
 // as 16 bytes against Mp*Kp bytes per dropped plane, among the p0 whose
-// residual stays at most one entry per 1024 weights (one thread adds a row's
-// entries serially when the row is written, so density costs latency).
+// residual stays at most one entry per 2^density_log2 weights (the entries are
+// added serially by the row's writer, so density costs latency: the matvec
+// allows 1/1024; the GEMM's epilogue pays 32 strided loads per entry and holds
+// its CTA meanwhile, so it allows 1/2^20).
 // IQ_PLANE_P0 (0..7) in the environment caps it (0 = keep every plane).
-static int choose_p0(int top, const unsigned long long low[8], int64_t plane_bytes) {
+static int choose_p0(int top, const unsigned long long low[8], int64_t plane_bytes, int density_log2) {
     static const int cap = getenv("IQ_PLANE_P0") ? atoi(getenv("IQ_PLANE_P0")) : 8;
     int best = 0;
     long double best_gain = 0, below = 0;
     for (int p0 = 1; p0 < top && p0 <= cap; p0++) {
         below += (long double)low[p0 - 1];
         const long double gain = (long double)p0 * plane_bytes - 16.0L * below;
-        if (below * 1024.0L > (long double)plane_bytes) break;
+        if (below * (long double)(1ull << density_log2) > (long double)plane_bytes) break;
         if (gain > best_gain) { best_gain = gain; best = p0; }
     }
     return best;
 }
 
 static void free_packed(Packed *P);
+
+// Sparse residual of the plane window (see iq_planes.cuh): CSR over rows_pad
+// rows of the weights' bits in `mask` (the bytes below p0); nnz entries, in
+// column order per row. Synchronises s.
+static int build_residual(const int64_t *d_w, int M, int N, int rows_pad, int nnz, uint64_t mask,
+                          cudaStream_t s, int *res_ptr, int *res_col, int64_t *res_val) {
+    std::vector<int> cnt(rows_pad + 1, 0);
+    IQ_CUDA(cudaMemsetAsync(res_ptr, 0, (size_t)(rows_pad + 1) * sizeof(int), s));
+    const int g = std::min((M + 7) / 8, dev_info().sms * 16);
+    k_res_count<<<g, 256, 0, s>>>(res_ptr, d_w, M, N, mask);
+    IQ_CHECK_LAUNCH();
+    IQ_CUDA(cudaMemcpyAsync(cnt.data(), res_ptr, (size_t)rows_pad * sizeof(int), cudaMemcpyDeviceToHost, s));
+    IQ_CUDA(cudaStreamSynchronize(s));
+    int run = 0;  // exclusive scan on the host
+    for (int r = 0; r <= rows_pad; r++) { int c = r < rows_pad ? cnt[r] : 0; cnt[r] = run; run += c; }
+    if (run != nnz) return IQ_ERR_STATE;
+    IQ_CUDA(cudaMemcpyAsync(res_ptr, cnt.data(), (size_t)(rows_pad + 1) * sizeof(int), cudaMemcpyHostToDevice, s));
+    k_res_fill<<<g, 256, 0, s>>>(res_col, res_val, res_ptr, d_w, M, N, mask);
+    IQ_CHECK_LAUNCH();
+    IQ_CUDA(cudaStreamSynchronize(s));  // cnt is a host buffer that goes out of scope
+    return IQ_OK;
+}
 
 static int pack_weights(const int64_t *d_w, int M, int N, cudaStream_t s, Packed *P) {
     P->M = M; P->N = N;
@@ -186,7 +210,7 @@ static int pack_weights(const int64_t *d_w, int M, int N, cudaStream_t s, Packed
     unsigned long long low[8];
     int rc = plane_stats(d_w, (int64_t)M * N, s, &top, low);
     if (rc) return rc;
-    P->p0 = choose_p0(top, low, (int64_t)P->Mp * P->Kp);
+    P->p0 = choose_p0(top, low, (int64_t)P->Mp * P->Kp, 10);
     P->np = top - P->p0;
     P->nnz = 0;
     for (int b = 0; b < P->p0; b++) P->nnz += (int)low[b];
@@ -208,22 +232,9 @@ static int pack_weights(const int64_t *d_w, int M, int N, cudaStream_t s, Packed
     IQ_CHECK_LAUNCH();
     k_row_sums<<<std::min(P->Mp / 8 + 1, dev_info().sms * 16), 256, 0, s>>>(P->rowsum, d_w, M, N, P->Mp, mask);
     IQ_CHECK_LAUNCH();
-    if (P->nnz > 0) {
-        // CSR offsets: per-row counts on the device, exclusive scan on the host
-        std::vector<int> cnt(P->Mp + 1, 0);
-        IQ_CUDA(cudaMemsetAsync(P->res_ptr, 0, (size_t)(P->Mp + 1) * sizeof(int), s));
-        const int g = std::min((M + 7) / 8, dev_info().sms * 16);
-        k_res_count<<<g, 256, 0, s>>>(P->res_ptr, d_w, M, N, mask);
-        IQ_CHECK_LAUNCH();
-        IQ_CUDA(cudaMemcpyAsync(cnt.data(), P->res_ptr, (size_t)P->Mp * sizeof(int), cudaMemcpyDeviceToHost, s));
-        IQ_CUDA(cudaStreamSynchronize(s));
-        int run = 0;
-        for (int r = 0; r <= P->Mp; r++) { int c = r < P->Mp ? cnt[r] : 0; cnt[r] = run; run += c; }
-        if (run != P->nnz) { free_packed(P); return IQ_ERR_STATE; }
-        IQ_CUDA(cudaMemcpyAsync(P->res_ptr, cnt.data(), (size_t)(P->Mp + 1) * sizeof(int), cudaMemcpyHostToDevice, s));
-        k_res_fill<<<g, 256, 0, s>>>(P->res_col, P->res_val, P->res_ptr, d_w, M, N, mask);
-        IQ_CHECK_LAUNCH();
-        IQ_CUDA(cudaStreamSynchronize(s));  // cnt is a host buffer that goes out of scope
+    if (P->nnz > 0 && (rc = build_residual(d_w, M, N, P->Mp, P->nnz, mask, s, P->res_ptr, P->res_col, P->res_val))) {
+        free_packed(P);
+        return rc;
     }
     return IQ_OK;
 }
@@ -442,17 +453,29 @@ static int encode_u8_map(CUtensorMap *map, const void *base, uint64_t rows, uint
 }
 
 struct PackedTC {
-    int M = 0, K = 0, Mpad = 0, Kpad = 0, np = 8;
-    uint8_t *planes = nullptr;   // [8][Mpad][Kpad]
-    int64_t *rowsum = nullptr;   // [Mpad][2]
+    int M = 0, K = 0, Mpad = 0, Kpad = 0, np = 8, p0 = 0, nnz = 0;
+    uint8_t *planes = nullptr;   // [np][Mpad][Kpad]: bytes p0 .. p0+np-1
+    int64_t *rowsum = nullptr;   // [Mpad][2] (128-bit sum of w_hi)
+    int *res_ptr = nullptr, *res_col = nullptr;  // sparse residual (CSR over Mpad rows)
+    int64_t *res_val = nullptr;
     CUtensorMap mapA;
 };
 
 static void free_packed_tc(PackedTC *P) {
     if (P->planes) cudaFree(P->planes);
     if (P->rowsum) cudaFree(P->rowsum);
+    if (P->res_ptr) cudaFree(P->res_ptr);
+    if (P->res_col) cudaFree(P->res_col);
+    if (P->res_val) cudaFree(P->res_val);
     P->planes = nullptr;
     P->rowsum = nullptr;
+    P->res_ptr = P->res_col = nullptr;
+    P->res_val = nullptr;
+    P->nnz = 0;
+}
+
+static PackedRes packed_res(const PackedTC &P) {
+    return PackedRes{P.p0, P.rowsum, P.res_ptr, P.res_col, P.res_val};
 }
 
 static int pack_weights_tc(const int64_t *d_w, int M, int K, cudaStream_t s, PackedTC *P) {
@@ -460,17 +483,35 @@ static int pack_weights_tc(const int64_t *d_w, int M, int K, cudaStream_t s, Pac
     P->M = M; P->K = K;
     P->Mpad = (M + TC_BM - 1) / TC_BM * TC_BM;
     P->Kpad = (K + TC_BK - 1) / TC_BK * TC_BK;
-    int rc = count_planes(d_w, (int64_t)M * K, s, &P->np);
+    int top = 8;
+    unsigned long long low[8];
+    int rc = plane_stats(d_w, (int64_t)M * K, s, &top, low);
     if (rc) return rc;
+    P->p0 = choose_p0(top, low, (int64_t)P->Mpad * P->Kpad, 20);
+    P->np = top - P->p0;
+    P->nnz = 0;
+    for (int b = 0; b < P->p0; b++) P->nnz += (int)low[b];
+    const uint64_t mask = P->p0 ? (~0ull >> (64 - 8 * P->p0)) : 0ull;
     size_t n = (size_t)P->Mpad * P->Kpad;
-    IQ_CUDA(cudaMalloc(&P->planes, (size_t)P->np * n));
-    cudaError_t e = cudaMalloc(&P->rowsum, (size_t)P->Mpad * 16);
+    cudaError_t e = cudaMalloc(&P->planes, (size_t)P->np * n);
+    if (e == cudaSuccess) e = cudaMalloc(&P->rowsum, (size_t)P->Mpad * 16);
+    if (e == cudaSuccess && P->nnz > 0) {
+        e = cudaMalloc(&P->res_ptr, (size_t)(P->Mpad + 1) * sizeof(int));
+        if (e == cudaSuccess) e = cudaMalloc(&P->res_col, (size_t)P->nnz * sizeof(int));
+        if (e == cudaSuccess) e = cudaMalloc(&P->res_val, (size_t)P->nnz * sizeof(int64_t));
+    }
     if (e != cudaSuccess) { free_packed_tc(P); return cuda_fail(e); }
     k_pack_rowplanes<<<(int)std::min<size_t>((n + 255) / 256, (size_t)dev_info().sms * 64), 256, 0, s>>>(
-        P->planes, d_w, M, K, P->Mpad, P->Kpad, P->np);
+        P->planes, d_w, M, K, P->Mpad, P->Kpad, P->np, P->p0);
     IQ_CHECK_LAUNCH();
-    k_row_sums<<<std::min(P->Mpad / 8 + 1, dev_info().sms * 16), 256, 0, s>>>(P->rowsum, d_w, M, K, P->Mpad);
+    k_row_sums<<<std::min(P->Mpad / 8 + 1, dev_info().sms * 16), 256, 0, s>>>(P->rowsum, d_w, M, K, P->Mpad,
+                                                                            mask);
     IQ_CHECK_LAUNCH();
+    if (P->nnz > 0 &&
+        (rc = build_residual(d_w, M, K, P->Mpad, P->nnz, mask, s, P->res_ptr, P->res_col, P->res_val))) {
+        free_packed_tc(P);
+        return rc;
+    }
     rc = encode_u8_map(&P->mapA, P->planes, (uint64_t)P->np * P->Mpad, (uint64_t)P->Kpad, TC_BM);
     if (rc) { free_packed_tc(P); return rc; }
     return IQ_OK;
@@ -531,13 +572,13 @@ int launch_gemm_tc(int64_t *out, const PackedTC &P, const int64_t *X, int R, cud
     IQ_CUDA(cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
     const int ks = part ? gemm_ksplit(P, R) : 1;
     dim3 grid(P.Mpad / TC_BM, Rpad / TC_BR, ks);
-    k_gemm_tc<<<grid, 192, TC_SMEM, s>>>(P.mapA, mapB, out, P.rowsum, P.M, R, P.Mpad, P.Kpad, add, part, Rpad,
-                                         P.np);
+    k_gemm_tc<<<grid, 192, TC_SMEM, s>>>(P.mapA, mapB, out, packed_res(P), X, P.K, P.M, R, P.Mpad, P.Kpad, add,
+                                         part, Rpad, P.np);
     IQ_CHECK_LAUNCH();
     if (ks > 1) {
         int64_t n = (int64_t)R * P.M;
         k_gemm_reduce<<<(int)std::min<int64_t>((n + 255) / 256, (int64_t)dev_info().sms * 16), 256, 0, s>>>(
-            out, part, P.rowsum, P.M, R, P.Mpad, Rpad, ks, add);
+            out, part, packed_res(P), X, P.K, P.M, R, P.Mpad, Rpad, ks, add);
         IQ_CHECK_LAUNCH();
     }
     return IQ_OK;
@@ -795,6 +836,14 @@ IQ_API int iq_pack_weights_tc_dev(const int64_t *d_w, int M, int N, void *stream
     p->dev = dev;
     if ((rc = pack_weights_tc(d_w, M, N, pick(stream), &p->P))) { delete p; return rc; }
     *out = p;
+    return IQ_OK;
+}
+
+IQ_API int iq_packed_tc_info(const iq_packed_tc *p, int *np, int *p0, int *residual_entries) {
+    if (!p || !np || !p0 || !residual_entries) return IQ_ERR_ARG;
+    *np = p->P.np;
+    *p0 = p->P.p0;
+    *residual_entries = p->P.nnz;
     return IQ_OK;
 }
 

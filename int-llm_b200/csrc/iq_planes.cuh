@@ -233,6 +233,14 @@ __device__ __forceinline__ void fold_planes(int (&c)[NP][4], int t, i128 &r0, i1
     }
 }
 
+// Exact signed 64 x 64 -> 128-bit product from the two hardware halves (a
+// plain (i128)a * b may be compiled as a full 128 x 128 multiply).
+__device__ __forceinline__ i128 mul_wide(int64_t a, int64_t b) {
+    const uint64_t lo = (uint64_t)a * (uint64_t)b;
+    const int64_t hi = __mul64hi(a, b);
+    return (i128)(((u128)(uint64_t)hi << 64) | lo);
+}
+
 // The row's result from its 128-bit plane sum `acc` (stored planes, before the
 // 2^(8 p0) scale): scale, subtract 2^63 sum w_hi, add the sparse residual
 // sum x_k w_lo,k (x from the staged digits when xd != nullptr, else from xg),
@@ -253,7 +261,7 @@ __device__ __forceinline__ int64_t finish_row(i128 acc, int row, const PackedRes
             } else {
                 xk = xg[k];
             }
-            v += (u128)((i128)xk * R.val[e]);
+            v += (u128)mul_wide(xk, R.val[e]);
         }
     }
     return (int64_t)((i128)v >> 48);

@@ -6,8 +6,10 @@
 // and the unsigned digits D_j of x_u = x + 2^63,
 //   out[r][i] = low64( (sum_{p,j} 2^{8(p+j)} P_pj[r][i] - 2^63 sum_k W[i][k]) >> 48 )
 //   P_pj[r][i] = sum_k B_p(W[i][k]) * D_j(x_u[r][k])       (exact int32)
-// Only the np planes the weights need are stored (see bytes_needed in
-// iq_planes.cuh; the top stored plane is the signed one).
+// Only the window of planes p0 .. p0+np-1 is stored (see iq_planes.cuh: the
+// top stored plane is the signed one, and the low bytes below p0 that few
+// weights use are an exact sparse per-row residual sum_k x[r][k] w_lo[i][k]
+// added by the epilogue before the shift).
 // For plane p the products for all digits are one GEMM: A = plane p of W
 // ([Mpad][Kpad] bytes, K-major) times B = the digit matrix
 // ([(row, digit)][Kpad] bytes, K-major, row = 8*r + j), so the MMA's N
@@ -37,14 +39,14 @@ constexpr int TC_B_BYTES = TC_BR * 8 * TC_BK;        // 32 KB
 constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
 constexpr size_t TC_SMEM = 1024 + (size_t)TC_STAGES * TC_STAGE_BYTES + 256;
 
-// W [M][K] int64 -> planes [np][Mpad][Kpad] bytes (zero padded; top plane signed)
+// W [M][K] int64 -> planes [np][Mpad][Kpad] bytes p0 .. p0+np-1 (zero padded; top plane signed)
 __global__ void k_pack_rowplanes(uint8_t *__restrict__ out, const int64_t *__restrict__ W, int M, int K,
-                                 int Mpad, int Kpad, int np) {
+                                 int Mpad, int Kpad, int np, int p0) {
     const int64_t n = (int64_t)Mpad * Kpad;
     for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
         int m = (int)(e / Kpad), k = (int)(e % Kpad);
         uint64_t w = (m < M && k < K) ? (uint64_t)W[(size_t)m * K + k] : 0ull;
-        for (int p = 0; p < np; p++) out[(size_t)p * n + e] = (uint8_t)(w >> (8 * p));
+        for (int p = 0; p < np; p++) out[(size_t)p * n + e] = (uint8_t)(w >> (8 * (p0 + p)));
     }
 }
 
@@ -62,8 +64,9 @@ __global__ void k_x_digits(uint8_t *__restrict__ out, const int64_t *__restrict_
 
 __global__ void __launch_bounds__(192, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-          int64_t *__restrict__ out, const int64_t *__restrict__ rowsum, int M, int R, int Mpad, int Kpad,
-          int add, int64_t *__restrict__ part, int Rpad, int np) {
+          int64_t *__restrict__ out, const PackedRes res, const int64_t *__restrict__ X, int K, int M, int R,
+          int Mpad, int Kpad, int add, int64_t *__restrict__ part, int Rpad, int np) {
+    const int64_t *__restrict__ rowsum = res.rowsum;
     extern __shared__ unsigned char smraw[];
     unsigned char *sm = smraw + ((1024 - (smem_u32(smraw) & 1023)) & 1023);  // 1024-aligned stages
     unsigned char *stage = sm;
@@ -150,7 +153,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUte
                 for (int rr = 0; rr < 4; rr++)
 #pragma unroll
                     for (int j = 0; j < 8; j++)
-                        acc[4 * c + rr] += (i128)(int32_t)v[rr * 8 + j] << (8 * (p + j));
+                        acc[4 * c + rr] += (i128)(int32_t)v[rr * 8 + j] << (8 * (res.p0 + p + j));
             }
             tc_fence_before();
             __syncwarp();
@@ -165,6 +168,16 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUte
                 pp[1] = (int64_t)(uint64_t)((u128)acc[r] >> 64);
             }
         } else if (ok && row < M) {
+            if (res.ptr) {  // sparse residual: sum_k x[r][k] * w_lo[row][k]
+#pragma unroll 1
+                for (int e = res.ptr[row], e1 = res.ptr[row + 1]; e < e1; e++) {
+                    const int k = res.col[e];
+                    const int64_t wl = res.val[e];
+#pragma unroll
+                    for (int r = 0; r < TC_BR; r++)
+                        if (r0 + r < R) acc[r] += mul_wide(X[(size_t)(r0 + r) * K + k], wl);
+                }
+            }
             const i128 ws = (i128)(((u128)(uint64_t)rowsum[2 * row + 1] << 64) | (uint64_t)rowsum[2 * row]);
             const u128 bias = (u128)ws << 63;
 #pragma unroll
@@ -186,9 +199,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUte
 }
 
 // split-K finish: out[r][m] (+)= low64((sum_ks part[ks][r][m] - 2^63 rowsum[m]) >> 48)
-__global__ void k_gemm_reduce(int64_t *__restrict__ out, const int64_t *__restrict__ part,
-                              const int64_t *__restrict__ rowsum, int M, int R, int Mpad, int Rpad, int KS,
+__global__ void k_gemm_reduce(int64_t *__restrict__ out, const int64_t *__restrict__ part, const PackedRes res,
+                              const int64_t *__restrict__ X, int K, int M, int R, int Mpad, int Rpad, int KS,
                               int add) {
+    const int64_t *__restrict__ rowsum = res.rowsum;
     const int64_t n = (int64_t)R * M;
     for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
         const int r = (int)(e / M), m = (int)(e % M);
@@ -197,6 +211,9 @@ __global__ void k_gemm_reduce(int64_t *__restrict__ out, const int64_t *__restri
             const int64_t *pp = part + (((size_t)ks * Rpad + r) * Mpad + m) * 2;
             acc += ((u128)(uint64_t)pp[1] << 64) | (uint64_t)pp[0];
         }
+        if (res.ptr)  // sparse residual: sum_k x[r][k] * w_lo[m][k]
+            for (int q = res.ptr[m], q1 = res.ptr[m + 1]; q < q1; q++)
+                acc += (u128)mul_wide(X[(size_t)r * K + res.col[q]], res.val[q]);
         const u128 ws = ((u128)(uint64_t)rowsum[2 * m + 1] << 64) | (uint64_t)rowsum[2 * m];
         int64_t v = (int64_t)((i128)(acc - (ws << 63)) >> 48);
         int64_t *o = out + (size_t)r * M + m;

@@ -41,6 +41,7 @@ SIGNATURES = {
     "iq_matvec_packed_noalloc_dev": (_I, [_P, _P, _P, _P]),
     "iq_pack_weights_tc_dev": (_I, [_P, _I, _I, _P, _P]),
     "iq_packed_tc_free": (_I, [_P]),
+    "iq_packed_tc_info": (_I, [_P, _P, _P, _P]),
     "iq_gemm_tc_dev": (_I, [_P, _P, _P, _I, _P]),
     "iq_device_status": (_I, []),
     "iq_fp_dev": (_I, [_I, _P, _P, _P, _I64, _P]),
@@ -114,6 +115,9 @@ def _dp(t):
     return ctypes.c_void_p(t.data_ptr())
 
 
+_CUDA_STREAM_LEGACY = 0x1
+
+
 def _sp(stream):
     """Stream argument: an explicit stream, else torch's current stream when torch
     has initialised CUDA (so device calls order with the tensors' producers),
@@ -122,7 +126,10 @@ def _sp(stream):
         import sys
         t = sys.modules.get("torch")
         if t is not None and t.cuda.is_initialized():
-            return ctypes.c_void_p(t.cuda.current_stream().cuda_stream)
+            h = t.cuda.current_stream().cuda_stream
+            # torch's default stream has handle 0, which the library would read as
+            # "its own stream": name the legacy default stream (cudaStreamLegacy) instead
+            return ctypes.c_void_p(h if h else _CUDA_STREAM_LEGACY)
         return None
     return ctypes.c_void_p(getattr(stream, "cuda_stream", stream))
 
@@ -210,6 +217,12 @@ class PackedTC:
     def __init__(self, d_w, M, N, stream=None):
         self.h = ctypes.c_void_p()
         _call("iq_pack_weights_tc_dev", _dp(d_w), M, N, _sp(stream), ctypes.byref(self.h))
+
+    def info(self):
+        """(np, p0, residual_entries) of the GEMM form."""
+        a, b, c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        _call("iq_packed_tc_info", self.h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c))
+        return a.value, b.value, c.value
 
     def free(self):
         if self.h:

@@ -328,3 +328,35 @@ def test_plane_window_residual_edges(M, N):
         iq.matvec_packed_dev(do, pk, dev(x))
         assert (host(do) == orc.matmul_vec(w, x)).all()
     pk.free()
+
+
+def test_gemm_plane_window_and_residual():
+    """tcgen05 GEMM on weights whose high bytes fit planes 3..5, with three
+    planted low-byte entries (few enough for the GEMM's residual): window
+    (3, 3, 3); config weights keep bytes 2..5; exact with split-K (5 rows)
+    and in one pass (300 rows)."""
+    import torch
+    rng = np.random.default_rng(77)
+    M = N = 2048
+    w = rng.integers(-(1 << 23), 1 << 23, (M, N), dtype=np.int64) << 24
+    w[0, 0] += 12345
+    w[7, 1000] -= 777
+    w[M - 1, N - 1] += (1 << 24) - 1
+    pt = iq.PackedTC(dev(w), M, N)
+    assert pt.info() == (3, 3, 3)
+    for rows in (5, 300):
+        X = rand_full(rng, (rows, N))
+        dg = torch.zeros((rows, M), dtype=torch.int64, device="cuda")
+        iq.gemm_tc_dev(dg, pt, dev(X), rows)
+        assert iq.device_status() == 0
+        assert (host(dg) == orc.matmul_rows(w, X)).all(), rows
+    pt.free()
+    wc = orc.synth_weights(2, "w:tcwindow", (2560, 2048))
+    pc = iq.PackedTC(dev(wc), 2560, 2048)
+    np_, p0, nnz = pc.info()
+    assert (np_, p0) == (4, 2) and nnz == int(((wc.view(np.uint64) & np.uint64(0xFFFF)) != 0).sum())
+    X = orc.synth_acts(2, "X:tcwindow", (64, 2048))
+    dg = torch.zeros((64, 2560), dtype=torch.int64, device="cuda")
+    iq.gemm_tc_dev(dg, pc, dev(X), 64)
+    assert (host(dg) == orc.matmul_rows(wc, X)).all()
+    pc.free()
