@@ -245,26 +245,44 @@ __device__ __forceinline__ i128 mul_wide(int64_t a, int64_t b) {
 // 2^(8 p0) scale): scale, subtract 2^63 sum w_hi, add the sparse residual
 // sum x_k w_lo,k (x from the staged digits when xd != nullptr, else from xg),
 // then low64(>> 48) (llama_int.c:1044).
-__device__ __forceinline__ int64_t finish_row(i128 acc, int row, const PackedRes &R,
-                                              const unsigned char *xd, int ld, const int64_t *__restrict__ xg) {
-    i128 ws = (i128)(((u128)(uint64_t)R.rowsum[2 * row + 1] << 64) | (uint64_t)R.rowsum[2 * row]);
-    u128 v = ((u128)acc << (8 * R.p0)) - ((u128)ws << 63);
+// The static per-row inputs of finish_row (row sum, residual range and its
+// first entry), loadable before the kernel waits for its predecessor.
+struct RowPre {
+    i128 ws;
+    int e0, e1, col0;
+    int64_t val0;
+};
+__device__ __forceinline__ RowPre row_pre(int row, const PackedRes &R) {
+    RowPre p;
+    p.ws = (i128)(((u128)(uint64_t)R.rowsum[2 * row + 1] << 64) | (uint64_t)R.rowsum[2 * row]);
+    p.e0 = p.e1 = p.col0 = 0;
+    p.val0 = 0;
     if (R.ptr) {
-        for (int e = R.ptr[row], e1 = R.ptr[row + 1]; e < e1; e++) {
-            const int k = R.col[e];
-            int64_t xk;
-            if (xd) {
-                uint64_t xu = 0;
+        p.e0 = R.ptr[row];
+        p.e1 = R.ptr[row + 1];
+        if (p.e0 < p.e1) { p.col0 = R.col[p.e0]; p.val0 = R.val[p.e0]; }
+    }
+    return p;
+}
+__device__ __forceinline__ int64_t x_from_digits(const unsigned char *xd, int ld, int k) {
+    uint64_t xu = 0;
 #pragma unroll
-                for (int j = 0; j < 8; j++) xu |= (uint64_t)xd[j * ld + k] << (8 * j);
-                xk = (int64_t)(xu ^ 0x8000000000000000ull);
-            } else {
-                xk = xg[k];
-            }
-            v += (u128)mul_wide(xk, R.val[e]);
-        }
+    for (int j = 0; j < 8; j++) xu |= (uint64_t)xd[j * ld + k] << (8 * j);
+    return (int64_t)(xu ^ 0x8000000000000000ull);
+}
+__device__ __forceinline__ int64_t finish_row(i128 acc, const RowPre &p, const PackedRes &R,
+                                              const unsigned char *xd, int ld, const int64_t *__restrict__ xg) {
+    u128 v = ((u128)acc << (8 * R.p0)) - ((u128)p.ws << 63);
+    for (int e = p.e0; e < p.e1; e++) {
+        const int k = e == p.e0 ? p.col0 : R.col[e];
+        const int64_t wl = e == p.e0 ? p.val0 : R.val[e];
+        v += (u128)mul_wide(xd ? x_from_digits(xd, ld, k) : xg[k], wl);
     }
     return (int64_t)((i128)v >> 48);
+}
+__device__ __forceinline__ int64_t finish_row(i128 acc, int row, const PackedRes &R,
+                                              const unsigned char *xd, int ld, const int64_t *__restrict__ xg) {
+    return finish_row(acc, row_pre(row, R), R, xd, ld, xg);
 }
 
 // 4 digits j of x_u[k..k+3] packed into one word (byte i = element k+i)
@@ -485,6 +503,9 @@ k_matvec_rows(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const
 #pragma unroll
     for (int s = 0; s < D - 1; s++)
         if (s < total) prefetch(buf[s]);
+    // the writers' static row data for the first tile (row sums, residual)
+    RowPre pre = {};
+    if (threadIdx.x < 16 && ntiles > 0 && rt0 * 16 + (int)threadIdx.x < M) pre = row_pre(rt0 * 16 + threadIdx.x, R);
     // x and (with add) out are produced by the previous kernel
     asm volatile("griddepcontrol.wait;" ::: "memory");
     stage_digits(xd, ld, xg, N, Kp, nrm_w);
@@ -549,7 +570,8 @@ k_matvec_rows(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const
             }
             const int row = rt * 16 + (int)threadIdx.x;
             if (threadIdx.x < 16 && row < M) {
-                const int64_t val = finish_row(v, row, R, xd, ld, xg);
+                if (rt != rt0) pre = row_pre(row, R);
+                const int64_t val = finish_row(v, pre, R, xd, ld, xg);
                 out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)val) : val;
             }
             __syncthreads();  // wpart is rewritten by the next tile
