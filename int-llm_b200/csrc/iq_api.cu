@@ -322,7 +322,8 @@ int launch_matvec_rows(int64_t *out, const Packed &P, const int64_t *x, cudaStre
     const int RT = P.Mp / 16, KT = P.Kp / 32;
     // beyond two waves the stream-K kernel's even split wins (measured: 1.2 waves
     // row-owned +2%, 6.8 waves -4%)
-    if (RT > slots && (mode < 2 || RT > 2 * slots)) return IQ_ERR_UNSUPPORTED;
+    static const int waves = getenv("IQ_MV_ROWS_WAVES") ? atoi(getenv("IQ_MV_ROWS_WAVES")) : 2;
+    if (RT > slots && (mode < 2 || RT > (int64_t)waves * slots)) return IQ_ERR_UNSUPPORTED;
     int S = 1;
     while (S < 8 && (int64_t)RT * S * 2 <= slots && KT >= 2 * 8 * S * 2) S *= 2;
     const int64_t grid = RT > slots ? slots : (int64_t)RT * S;
