@@ -149,11 +149,20 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUte
                 uint32_t v[32];
                 tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * 256 + c * 32), v);
                 tmem_ld_wait();
+                // digits 0..3 and 4..7 of one x-row each sum exactly in 64 bits
+                // (|v| < 2^31, shifts <= 24: < 2^57), then one 128-bit
+                // shift-add per x-row: sum_j v_j 2^(8(p0+p+j))
+                const int sh = 8 * (res.p0 + p);
 #pragma unroll
-                for (int rr = 0; rr < 4; rr++)
+                for (int rr = 0; rr < 4; rr++) {
+                    int64_t lo = 0, hi = 0;
 #pragma unroll
-                    for (int j = 0; j < 8; j++)
-                        acc[4 * c + rr] += (i128)(int32_t)v[rr * 8 + j] << (8 * (res.p0 + p + j));
+                    for (int j = 0; j < 4; j++) {
+                        lo += (int64_t)(int32_t)v[rr * 8 + j] * (1ll << (8 * j));
+                        hi += (int64_t)(int32_t)v[rr * 8 + 4 + j] * (1ll << (8 * j));
+                    }
+                    acc[4 * c + rr] += (i128)((u128)((i128)lo + (i128)((u128)(i128)hi << 32)) << sh);
+                }
             }
             tc_fence_before();
             __syncwarp();
