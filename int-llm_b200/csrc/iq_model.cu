@@ -297,6 +297,25 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
         IQ_CHECK_LAUNCH();
         return proj(out, P, T, m->normed, rows, 0);
     };
+    // rmsnorm -> gate|up -> SwiGLU into act. One row: the matvec over the
+    // pair-interleaved gate|up rows forms SwiGLU in its epilogue (no gu
+    // round trip, one launch); several rows: GEMM into m->gu, then k_swiglu.
+    auto norm_gu_swiglu = [&](int64_t *act, int l, const int64_t *x, const int64_t *nw, int rows) -> int {
+        if (rows == 1 && S.it_l % 8 == 0) {
+            if ((size_t)8 * (m->pgu[l].Kp + 16) <= 100 * 1024)
+                return launch_matvec_planes(act, m->pgu[l], x, s, IQ_EPI_SWIGLU, m->racc, nw);
+            k_rmsnorm<<<1, 256, 0, s>>>(m->normed, x, nw, d);
+            IQ_CHECK_LAUNCH();
+            return launch_matvec_planes(act, m->pgu[l], m->normed, s, IQ_EPI_SWIGLU, m->racc);
+        }
+        k_rmsnorm<<<rows, 256, 0, s>>>(m->normed, x, nw, d);
+        IQ_CHECK_LAUNCH();
+        int rc = proj(m->gu, m->pgu[l], m->tgu[l], m->normed, rows, 0);
+        if (rc) return rc;
+        k_swiglu<<<(rows * S.it_l + 255) / 256, 256, 0, s>>>(act, m->gu, S.it_l, rows);
+        IQ_CHECK_LAUNCH();
+        return IQ_OK;
+    };
     k_embed<<<dim3((d + 255) / 256, R), 256, 0, s>>>(m->hidden, m->embed, tok, d);
     IQ_CHECK_LAUNCH();
     const int pairs = (S.nh_l + S.nkv_l) * (hd / 2) + m->kvd_l;
@@ -341,9 +360,7 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
         } else if ((rc = proj(m->hidden, m->po[l], m->to[l], m->att, R, 1))) {
             return rc;
         }
-        if ((rc = norm_proj(m->gu, m->pgu[l], m->tgu[l], m->hidden, m->norm2[l], R))) return rc;
-        k_swiglu<<<(R * S.it_l + 255) / 256, 256, 0, s>>>(act_out, m->gu, S.it_l, R);
-        IQ_CHECK_LAUNCH();
+        if ((rc = norm_gu_swiglu(act_out, l, m->hidden, m->norm2[l], R))) return rc;
         if (tp) {
             if ((rc = gather_rows(m, m->act_l, m->act, R, S.it_l))) return rc;
             if ((rc = proj(m->proj_l, m->pdown[l], m->tdown[l], m->act, R, 0))) return rc;
@@ -431,7 +448,21 @@ static int repack_layer(iq_model *m, int l) {
     int rc, d = c.hidden_dim, it = c.intermediate_dim;
     if ((rc = repack(m, &m->pqkv[l], m->wqkv[l], m->qkv_rows, d))) return rc;
     if ((rc = repack(m, &m->po[l], m->wo[l], S.d_l, d))) return rc;
-    if ((rc = repack(m, &m->pgu[l], m->wgu[l], 2 * S.it_l, d))) return rc;
+    if (S.it_l % 8) {  // no pair interleave: SwiGLU stays a separate kernel
+        if ((rc = repack(m, &m->pgu[l], m->wgu[l], 2 * S.it_l, d))) return rc;
+    } else {
+        // the matvec form of gate|up is packed pair-interleaved (see k_interleave_pairs)
+        int64_t *tmp = nullptr;
+        const int64_t n = (int64_t)2 * S.it_l * d;
+        IQ_CUDA(cudaMalloc(&tmp, (size_t)n * 8));
+        k_interleave_pairs<<<(int)std::min<int64_t>((n + 255) / 256, 65535), 256, 0, m->s>>>(tmp, m->wgu[l], S.it_l,
+                                                                                            d);
+        cudaError_t e = cudaGetLastError();
+        rc = e == cudaSuccess ? repack(m, &m->pgu[l], tmp, 2 * S.it_l, d) : cuda_fail(e);
+        cudaStreamSynchronize(m->s);
+        cudaFree(tmp);
+        if (rc) return rc;
+    }
     if ((rc = repack(m, &m->pdown[l], m->wdown[l], S.d_l, it))) return rc;
     if ((rc = repack_tc(m, &m->tqkv[l], m->wqkv[l], m->qkv_rows, d))) return rc;
     if ((rc = repack_tc(m, &m->to[l], m->wo[l], S.d_l, d))) return rc;

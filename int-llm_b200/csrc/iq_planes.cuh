@@ -195,6 +195,27 @@ __global__ void k_row_sums(int64_t *__restrict__ rs, const int64_t *__restrict__
     }
 }
 
+// Fused gate|up rows [gate (half rows); up (half rows)] reordered so that each
+// 16-row tile holds gate rows i..i+7 at tile rows 0..7 and the matching up
+// rows at 8..15 (i = 8 * tile): a matvec epilogue that writes tile rows g and
+// g + 8 together can then form SwiGLU directly (add mode IQ_EPI_SWIGLU).
+// half must be a multiple of 8.
+__global__ void k_interleave_pairs(int64_t *__restrict__ out, const int64_t *__restrict__ W, int half, int N) {
+    const int64_t n = (int64_t)2 * half * N;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        const int r = (int)(e / N), k = (int)(e % N);
+        const int tile = r >> 4, g = r & 15;
+        const int src = g < 8 ? tile * 8 + g : half + tile * 8 + (g - 8);
+        out[e] = W[(size_t)src * N + k];
+    }
+}
+
+// Epilogue modes of the matvec kernels (their `add` argument).
+#define IQ_EPI_STORE 0   // out[row] = result
+#define IQ_EPI_ADD 1     // out[row] += result (residual, int64 wrap)
+#define IQ_EPI_SWIGLU 2  // pair-interleaved gate|up rows: out[8 * tile + g] =
+                         // fp_mul(fp_silu(gate), up) (llama_int.c:1549-1552)
+
 // ----------------------------------------------------------------- kernel
 
 __device__ __forceinline__ uint4 ld_stream_u4(const uint4 *p) {
@@ -416,7 +437,32 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
                     r0 += shfl_xor_i128(r0, m);
                     r1 += shfl_xor_i128(r1, m);
                 }
-                if (t == 0) {
+                if (t == 0 && add == IQ_EPI_SWIGLU) {
+                    // rows g (gate) and g + 8 (up) complete together: one counter
+                    const int row = rt * 16 + g;
+                    i128 f0 = r0, f1 = r1;
+                    bool write = k0 == 0 && k1 == KT;
+                    if (!write) {
+                        RowAcc *ra = racc + row, *rb = racc + row + 8;
+                        atomic_add_i128(ra, r0);
+                        atomic_add_i128(rb, r1);
+                        cuda::atomic_ref<unsigned int, cuda::thread_scope_device> done(ra->done);
+                        unsigned int prev = done.fetch_add((unsigned int)(k1 - k0), cuda::memory_order_acq_rel);
+                        if (prev + (unsigned int)(k1 - k0) == (unsigned int)KT) {
+                            unsigned long long alo = atomicExch(&ra->lo, 0ull), ahi = atomicExch(&ra->hi, 0ull);
+                            unsigned long long blo = atomicExch(&rb->lo, 0ull), bhi = atomicExch(&rb->hi, 0ull);
+                            atomicExch(&ra->done, 0u);
+                            f0 = (i128)(((u128)ahi << 64) | alo);
+                            f1 = (i128)(((u128)bhi << 64) | blo);
+                            write = true;
+                        }
+                    }
+                    if (write) {
+                        const int64_t gate = finish_row(f0, row, R, XSMEM ? xd : nullptr, ld, xg);
+                        const int64_t up = finish_row(f1, row + 8, R, XSMEM ? xd : nullptr, ld, xg);
+                        out[rt * 8 + g] = d_mul(d_silu(gate), up);
+                    }
+                } else if (t == 0) {
 #pragma unroll
                     for (int h = 0; h < 2; h++) {
                         const int row = rt * 16 + g + 8 * h;
@@ -569,10 +615,15 @@ k_matvec_rows(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const
                 }
             }
             const int row = rt * 16 + (int)threadIdx.x;
+            int64_t val = 0;
             if (threadIdx.x < 16 && row < M) {
                 if (rt != rt0) pre = row_pre(row, R);
-                const int64_t val = finish_row(v, pre, R, xd, ld, xg);
-                out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)val) : val;
+                val = finish_row(v, pre, R, xd, ld, xg);
+                if (add != IQ_EPI_SWIGLU) out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)val) : val;
+            }
+            if (add == IQ_EPI_SWIGLU && warp == 0) {  // tile rows g (gate) and g + 8 (up)
+                const int64_t up = __shfl_down_sync(0xffffffffu, val, 8);
+                if (lane < 8 && rt * 16 + lane < M) out[rt * 8 + lane] = d_mul(d_silu(val), up);
             }
             __syncthreads();  // wpart is rewritten by the next tile
             rt += stride;
