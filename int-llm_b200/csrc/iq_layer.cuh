@@ -251,22 +251,56 @@ k_attn_scores(int64_t *__restrict__ sc, int64_t *__restrict__ mx, const int64_t 
     if (t0 >= T) return;
     const int nt = min(ATT_TILE, T - t0);
     const int grp = nh / nkv, dim = nh * hd, kvd = nkv * hd, kld = hd + 1;
-    int64_t *qs = smem;               // [grp][hd]
-    int64_t *kt = qs + grp * hd;      // [ATT_TILE][hd + 1]
+    // Exact int128 dots in 32-bit limbs (six mad.wide.s32 per MAC instead of a
+    // 64 x 64 -> 128 product): q = a0 + a1 2^22 + a2 2^44 (a0, a1 unsigned
+    // 22-bit, a2 signed), k = kh 2^32 + ks + 2^31 (kh = k >> 32, ks = low word
+    // - 2^31, both signed 32-bit), so
+    //   sum q k = sum_i 2^(22 i) (2^32 H_i + L_i) + 2^31 sum q   (mod 2^128)
+    // with H_i = sum a_i kh, L_i = sum a_i ks; every term is < 2^53, so the
+    // int64 sums are exact for hd <= 256.
+    i128 *qsum = reinterpret_cast<i128 *>(smem);                        // [grp]
+    int32_t *qa = reinterpret_cast<int32_t *>(qsum + grp);               // [3][grp * hd]
+    int2 *kt = reinterpret_cast<int2 *>(smem + 2 * grp + (3 * grp * hd + 1) / 2);  // [ATT_TILE][hd + 1]
     const int64_t *q = qkv + (size_t)b * (dim + 2 * kvd) + (size_t)g * grp * hd;
-    for (int e = threadIdx.x; e < grp * hd; e += blockDim.x) qs[e] = q[e];
+    for (int e = threadIdx.x; e < grp * hd; e += blockDim.x) {
+        const int64_t v = q[e];
+        qa[e] = (int32_t)(v & 0x3FFFFF);
+        qa[grp * hd + e] = (int32_t)((v >> 22) & 0x3FFFFF);
+        qa[2 * grp * hd + e] = (int32_t)(v >> 44);
+    }
+    {   // sum q per head: one warp per head
+        const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+        for (int hh = w; hh < grp; hh += blockDim.x >> 5) {
+            i128 t = 0;
+            for (int d = l; d < hd; d += 32) t += (i128)q[hh * hd + d];
+            t = warp_sum_i128(t);
+            if (l == 0) qsum[hh] = t;
+        }
+    }
     const int64_t *kb = kc + ((size_t)seq_arr[b] * max_seq + t0) * kvd + g * hd;
-    for (int e = threadIdx.x; e < nt * hd; e += blockDim.x) kt[(e / hd) * kld + e % hd] = kb[(size_t)(e / hd) * kvd + e % hd];
+    for (int e = threadIdx.x; e < nt * hd; e += blockDim.x) {
+        const int64_t v = kb[(size_t)(e / hd) * kvd + e % hd];
+        kt[(e / hd) * kld + e % hd] = make_int2((int32_t)(v >> 32), (int32_t)((uint32_t)v ^ 0x80000000u));
+    }
     __syncthreads();
     for (int e = threadIdx.x; e < grp * ATT_TILE; e += blockDim.x) {
         const int hh = e / ATT_TILE, tt = e % ATT_TILE;
         int64_t v = INT64_MIN;
         if (tt < nt) {
-            const int64_t *qh = qs + hh * hd, *kr = kt + tt * kld;
-            i128 dot = 0;
-#pragma unroll 8
-            for (int dd = 0; dd < hd; dd++) dot += d_mul128(qh[dd], kr[dd]);
-            v = d_mul((int64_t)(dot >> 48), scale);
+            const int32_t *a0 = qa + hh * hd, *a1 = a0 + grp * hd, *a2 = a1 + grp * hd;
+            const int2 *kr = kt + tt * kld;
+            int64_t h0 = 0, h1 = 0, h2 = 0, l0 = 0, l1 = 0, l2 = 0;
+#pragma unroll 4
+            for (int dd = 0; dd < hd; dd++) {
+                const int2 kv = kr[dd];
+                const int32_t x0 = a0[dd], x1 = a1[dd], x2 = a2[dd];
+                madw(h0, x0, kv.x); madw(h1, x1, kv.x); madw(h2, x2, kv.x);
+                madw(l0, x0, kv.y); madw(l1, x1, kv.y); madw(l2, x2, kv.y);
+            }
+            const u128 dot = ((u128)(i128)h0 << 32) + ((u128)(i128)h1 << 54) + ((u128)(i128)h2 << 76) +
+                             (u128)(i128)l0 + ((u128)(i128)l1 << 22) + ((u128)(i128)l2 << 44) +
+                             ((u128)qsum[hh] << 31);
+            v = d_mul((int64_t)((i128)dot >> 48), scale);
             sc[((size_t)b * nh + g * grp + hh) * Tcap + t0 + tt] = v;
         }
         // tile max per head: the 64 tt of one head are two consecutive warps
@@ -274,6 +308,11 @@ k_attn_scores(int64_t *__restrict__ sc, int64_t *__restrict__ mx, const int64_t 
         if ((threadIdx.x & 31) == 0 && v != INT64_MIN)
             atomicMax((long long *)&mx[(size_t)b * nh + g * grp + hh], (long long)v);
     }
+}
+
+// shared memory of k_attn_scores: q sums, q limbs, key tile of int2 (int64 units)
+__host__ __device__ constexpr size_t att_scores_smem(int grp, int hd) {
+    return ((size_t)2 * grp + (3 * (size_t)grp * hd + 1) / 2 + (size_t)ATT_TILE * (hd + 1)) * 8;
 }
 
 // phase 2: e_t = fp_safe_exp(s_t - max) in place, S = wrapping int64 sum

@@ -591,9 +591,10 @@ IQ_API int iq_model_create_tp(const iq_config *cfg, int max_batch, int device, i
     {
         static int att_env = getenv("IQ_ATT") ? atoi(getenv("IQ_ATT")) : 1;
         const size_t grp = (size_t)sh.nh_l / sh.nkv_l, hd = c.head_dim;
-        m->att_s1 = (grp * hd + (size_t)ATT_TILE * (hd + 1)) * 8;
+        m->att_s1 = att_scores_smem((int)grp, (int)hd);
         m->att_s3 = (grp * ATT_TILE + (size_t)ATT_TILE * hd) * 8;
-        m->att_phased = att_env == 1 && m->att_s1 <= 200 * 1024 && m->att_s3 <= 200 * 1024;
+        // the phased scores use 32-bit limb dots, exact for head_dim <= 256
+        m->att_phased = att_env == 1 && hd <= 256 && m->att_s1 <= 200 * 1024 && m->att_s3 <= 200 * 1024;
         if (m->att_phased) {
             size_t n = (size_t)m->rmax * sh.nh_l;
             if ((rc = dalloc((void **)&m->asc, n * c.max_seq_len * 8)) || (rc = dalloc((void **)&m->amx, n * 8)) ||
