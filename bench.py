@@ -9,7 +9,10 @@ working set exceeds the 126 MB L2, so each shape is read cold from HBM).
 
 N > 1 runs under torchrun: every rank runs the whole workload on its own GPU
 (independent matvecs, no data-path collective: weak scaling); time is the max
-over ranks. `--impl reference` times the reference's own CPU matmul_vec
+over ranks. The same line carries two extra workloads: `cfg0_decode`
+(TinyLlama greedy decode, output-row tensor parallel over the N ranks with
+NCCL all-gathers) and, at N = 1, `cfg2_gemm` (the M=512 prefill GEMM), each
+with its own roofline and CPU baseline. `--impl reference` times the reference's own CPU matmul_vec
 (oracle/_ref, llama_int.c:1014) on the host cores, rows split across threads.
 """
 import argparse
@@ -48,11 +51,20 @@ def workload_config():
             "parallelism": "independent replicas per GPU (weak scaling)"}
 
 
-def synth_inputs():
-    """Seeded config-1 inputs from the library's own generator (iq_synth_*)."""
-    import iq
-    return [(iq.synth_weights(1, configs.matvec_names(K, N)[0], (N, K)),
-             iq.synth_acts(1, configs.matvec_names(K, N)[1], (K,))) for K, N in SHAPES]
+def synth_inputs(gen=None):
+    """Seeded config-1 inputs. Our arm uses the library's own generator
+    (iq_synth_*); the reference arm passes the oracle's C generator, which makes
+    identical values (tests/test_abi.py) without loading libiq.so."""
+    if gen is None:
+        import iq as gen
+    return [(gen.synth_weights(1, configs.matvec_names(K, N)[0], (N, K)),
+             gen.synth_acts(1, configs.matvec_names(K, N)[1], (K,))) for K, N in SHAPES]
+
+
+def _oracle():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    return orc
 
 
 class Clocks:
@@ -105,10 +117,11 @@ def measured_peak():
 
 
 def load_traffic():
-    """dram bytes per launch of the dominant kernel from the committed ncu summary."""
+    """ncu dram bytes (read + write) of one LM-head launch, from the committed
+    summary of the profiled bench command (profiles/traffic.json)."""
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            return json.load(f).get("k_matvec_planes_per_step_bytes")
+            return json.load(f).get("lm_head_launch_bytes")
     except Exception:
         return None
 
@@ -118,8 +131,7 @@ def load_traffic():
 def cpu_reference_lib():
     """The reference's own matmul_vec compiled from source (oracle/_ref), else
     the oracle's C restatement. Returns (callable(out,w,x,M,N,threads), kind)."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as orc
+    orc = _oracle()
     R = orc.ref()
     if R is not None:
         return (lambda o, w, x, M, N, t: R.ref_matmul_vec_mt(orc.p(o), orc.p(w), orc.p(x), M, N, t)), "reference"
@@ -150,7 +162,7 @@ def run_reference(args):
     rank = env_int("RANK", 0)
     if rank != 0:
         return
-    ins = synth_inputs()
+    ins = synth_inputs(_oracle())
     fn, kind = cpu_reference_lib()
     threads = os.cpu_count() or 1
     outs = [np.empty(N, np.int64) for K, N in SHAPES]
@@ -167,7 +179,7 @@ def run_reference(args):
     v = MACS_PER_STEP * done / dt / 1e9
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": done, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "steps": done, "warmup": args.warmup, "ms_per_step": dt / done * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int64",
         "data": "synthetic", "config": workload_config(),
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": kind,
@@ -177,16 +189,16 @@ def run_reference(args):
 
 # ------------------------------------------------------------------ GPU leg
 
-def run_ours(args):
+def _events(n):
+    import torch
+    return [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+
+
+def cfg1_leg(args, rank, world, local, dist):
+    """Config 1 headline: one step = the five config-1 matvecs (one CUDA-graph
+    replay), packed weights resident in HBM, every rank its own replica."""
     import torch
     import iq
-    rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
-    torch.cuda.set_device(local)
-    iq.set_device(local)
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     ins = synth_inputs()
     dev = [(torch.from_numpy(w).cuda(), torch.from_numpy(x).cuda()) for w, x in ins]
     outs = [torch.empty(N, dtype=torch.int64, device="cuda") for K, N in SHAPES]
@@ -201,42 +213,46 @@ def run_ours(args):
     torch.cuda.synchronize()
     ptrs = [(ctypes.c_void_p(o.data_ptr()), ctypes.c_void_p(w.data_ptr()), ctypes.c_void_p(x.data_ptr()), pk.h)
             for o, (w, x), pk in zip(outs, dev, packed)]
+    # bytes one launch of each shape reads: the stored form, x and out
+    shape_bytes = [(8 * K * N if raw else pk.nbytes()) + 8 * (K + N) for pk, (K, N) in zip(packed, SHAPES)]
+    step_bytes = sum(shape_bytes)
 
-    def step(evs=None):
-        for i, ((po, pw, px, pk), (K, N)) in enumerate(zip(ptrs, SHAPES)):
-            if evs is not None:
-                evs[i][0].record(s)
-            rc = L.iq_matvec_dev(po, pw, px, N, K, sp) if raw else L.iq_matvec_packed_dev(po, pk, px, sp)
-            if rc:
-                raise iq.IQError("iq_matvec_dev", rc, L)
-            if evs is not None:
-                evs[i][1].record(s)
+    def launch(i):
+        po, pw, px, pk = ptrs[i]
+        K, N = SHAPES[i]
+        rc = L.iq_matvec_dev(po, pw, px, N, K, sp) if raw else L.iq_matvec_packed_dev(po, pk, px, sp)
+        if rc:
+            raise iq.IQError("iq_matvec_dev", rc, L)
 
-    # warm-up (the device results are compared with the drop-in path's below)
+    def step():
+        for i in range(len(SHAPES)):
+            launch(i)
+
     with torch.cuda.stream(s):
         for _ in range(max(3, args.warmup)):
             step()
     torch.cuda.synchronize()
 
     # one step = one CUDA-graph replay of the 5 launches, so host launch overhead
-    # never leaves the GPU idle inside the timed region; a second graph carries
-    # CUDA events between the launches for the per-kernel durations
+    # never leaves the GPU idle inside the timed region
     g_step = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_step, stream=s, capture_error_mode="thread_local"):
         step()
+    # per-shape graphs of R back-to-back launches: average launch duration of
+    # each kernel with no per-replay gap (the LM head's 199 MB exceeds L2, so
+    # each launch reads HBM; the small shapes are L2-resident in this form and
+    # are reported for information only)
+    R = 20
     g_shape = []
     for i in range(len(SHAPES)):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
-            po, pw, px, pk = ptrs[i]
-            K, N = SHAPES[i]
-            rc = L.iq_matvec_dev(po, pw, px, N, K, sp) if raw else L.iq_matvec_packed_dev(po, pk, px, sp)
-            assert rc == 0
+            for _ in range(R):
+                launch(i)
         g_shape.append(g)
     torch.cuda.synchronize()
 
-    nev = args.steps * len(SHAPES)
-    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_start, t_end = _events(2)
     clk = Clocks(local)
     if dist:
         dist.barrier()
@@ -255,29 +271,20 @@ def run_ours(args):
     if dist:
         dist.barrier()
     ms_total = t_start.elapsed_time(t_end)
-    # per-shape durations: events around single-launch graph replays, shapes in
-    # rotation (so each matrix is read cold from HBM, as in the step)
-    per_shape_ms = [0.0] * len(SHAPES)
-    nsamp = min(args.steps, 300)
-    sev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-            for _ in SHAPES] for _ in range(nsamp)]
+    reps = 5
+    per_launch_ms = []
     with torch.cuda.stream(s):
-        for k in range(nsamp):
-            for i in range(len(SHAPES)):
-                sev[k][i][0].record(s)
-                g_shape[i].replay()
-                sev[k][i][1].record(s)
-    torch.cuda.synchronize()
-    for k in range(nsamp):
         for i in range(len(SHAPES)):
-            per_shape_ms[i] += sev[k][i][0].elapsed_time(sev[k][i][1]) * args.steps / nsamp
-    # the step graph holds only k_matvec_planes launches: its device time is the
-    # kernel's time (plus ~1 us graph-internal launch gaps)
-    kern_ms = ms_total
-    if dist:
-        t = torch.tensor([ms_total, kern_ms], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_total, kern_ms = t.tolist()
+            g_shape[i].replay()
+            e0, e1 = _events(2)
+            e0.record(s)
+            for _ in range(reps):
+                g_shape[i].replay()
+            e1.record(s)
+            torch.cuda.synchronize()
+            per_launch_ms.append(e0.elapsed_time(e1) / (reps * R))
+    ms_total = _max_over_ranks(dist, ms_total)
+    per_launch_ms = [_max_over_ranks(dist, t) for t in per_launch_ms]
 
     # e2e: the public host-pointer drop-in iq_matmul_vec, pinned host buffers,
     # H2D of x and D2H of out inside the timed region every call
@@ -297,51 +304,222 @@ def run_ours(args):
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
         e2e_step()
-    e2e_s = time.perf_counter() - t0
-    if dist:
-        t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = t.item()
+    e2e_s = _max_over_ranks(dist, time.perf_counter() - t0)
     # the drop-in result must equal the device path's (same inputs)
     for o, hoo in zip(outs, ho):
         assert (o.cpu().numpy() == hoo).all(), "drop-in and device path disagree"
+    iq.weight_cache_clear()
 
-    if rank != 0:
-        if dist:
-            dist.destroy_process_group()
-        return
     peak, peak_kind = measured_peak()
-    achieved = BYTES_PER_STEP * args.steps / (kern_ms / 1e3) / 1e9
-    traffic = load_traffic()
+    dom = len(SHAPES) - 1   # the 2048x32000 LM head: 69% of the step's bytes
+    K, N = SHAPES[dom]
+    ach = shape_bytes[dom] / (per_launch_ms[dom] / 1e3) / 1e9
+    step_gbs = step_bytes * args.steps / (ms_total / 1e3) / 1e9
     line = {
         "metric": METRIC, "value": MACS_PER_STEP * args.steps * world / (ms_total / 1e3) / 1e9,
         "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_total / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int64", "data": "synthetic", "config": workload_config(),
-        "gb_per_s_per_gpu": BYTES_PER_STEP * args.steps / (ms_total / 1e3) / 1e9,
-        "per_shape_gbs": {f"{K}x{N}": 8 * (K * N + K + N) * args.steps / (t / 1e3) / 1e9
-                          for (K, N), t in zip(SHAPES, per_shape_ms)},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "peak_source": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)",
-                     "kernel": "k_matvec" if raw else "k_matvec_planes", "traffic": traffic,
-                     "note": "achieved = algorithmic int64 bytes 8*(K*N+K+N) per step / step time; the packed "
-                             "format stores a window of byte planes (planes_stored: count, lowest, sparse "
-                             "residual entries per shape) so DRAM traffic per step is below the algorithmic "
-                             "bytes by design, not by skipped work; dram_gbs is the measured traffic's rate",
-                     "planes_stored": None if raw else {f"{K}x{N}": list(pk.info())
-                                                        for pk, (K, N) in zip(packed, SHAPES)},
-                     "dram_gbs": (traffic / (ms_total / args.steps / 1e3) / 1e9) if traffic else None},
+        "roofline": {
+            "bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+            "peak_source": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)",
+            "kernel": ("k_matvec" if raw else "k_matvec_planes") + f" {K}x{N} (LM head)",
+            "bytes_per_launch": shape_bytes[dom], "launch_ms": per_launch_ms[dom],
+            "traffic": load_traffic(),
+            "note": "achieved = bytes of the stored form one launch reads (iq_packed_bytes: byte-plane "
+                    "window + row sums + sparse residual, plus x and out) / average launch duration "
+                    "(CUDA events around 100 back-to-back launches); traffic = ncu dram bytes of one "
+                    "launch (profiles/); the int64 form the reference streams is 8 B/weight "
+                    "(int64_equiv_gbs)"},
+        "step_roofline": {"bytes_per_step": step_bytes, "gbs": step_gbs, "frac": step_gbs / peak,
+                          "int64_equiv_gbs": BYTES_PER_STEP * args.steps / (ms_total / 1e3) / 1e9},
+        "per_launch_us": {f"{K}x{N}": t * 1e3 for (K, N), t in zip(SHAPES, per_launch_ms)},
+        "planes_stored": None if raw else {f"{K}x{N}": list(pk.info()) for pk, (K, N) in zip(packed, SHAPES)},
         "e2e": {"value": MACS_PER_STEP * e2e_steps * world / e2e_s / 1e9, "unit": UNIT,
                 "h2d_bytes_per_step": sum(8 * K for K, N in SHAPES),
                 "d2h_bytes_per_step": sum(8 * N for K, N in SHAPES),
                 "api": "iq_matmul_vec (host pointers, weights registered)"},
-        "gpu_launches": nev,
+        "gpu_launches": args.steps * len(SHAPES),
         "clocks": clocks,
     }
-    if world == 1 and not args.no_cpu:
+    for pk in packed:
+        pk.free()
+    del dev, outs
+    torch.cuda.empty_cache()
+    if world == 1 and rank == 0 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(ins)
-    print(json.dumps(line))
+    return line
+
+
+def cpu_baseline_cfg0(budget_s=8.0):
+    """The reference's own llama_forward (oracle/_ref) on 1 core at TinyLlama
+    shape. Bounded sample: the 22 layers share layer 0's seeded weights (same
+    work per token as 22 distinct layers; 0.38 GB instead of 8.3 GB of host
+    weights to generate), forwards at positions 0, 1, 2, ... for ~budget_s."""
+    orc = _oracle()
+    R = orc.ref()
+    if R is None:
+        return None
+    c = configs.TINYLLAMA
+    d, V = c["dim"], c["vocab"]
+    one = np.full(d, 1 << 48, dtype=np.int64)
+    lay = [one if len(sh) == 1 else orc.synth_weights(0, configs.layer_name(0, t), sh)
+           for t, sh in zip(configs.LAYER_TENSORS, configs.layer_shapes(c))]
+    emb = orc.synth_weights(0, "model.embed_tokens.weight", (V, d))
+    lm = orc.synth_weights(0, "lm_head.weight", (V, d))
+    fn = np.full(d, 1 << 48, dtype=np.int64)
+    ptrs = (ctypes.c_void_p * (9 * c["n_layers"]))(*([a.ctypes.data for a in lay] * c["n_layers"]))
+    cfg9 = (ctypes.c_int * 9)(*configs.cfg9(c))
+    h = R.ref_model_create(cfg9, orc.p(emb), orc.p(fn), orc.p(lm), ptrs)
+    toks = orc.synth_tokens(0, "prompt:0", 64, V)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s and n < 64:
+        R.ref_model_forward(h, int(toks[n]), n, None)
+        n += 1
+    dt = time.perf_counter() - t0
+    R.ref_model_free(h)
+    return {"value": n / dt, "unit": "tokens/s", "cores": 1, "kind": "reference",
+            "sample": f"{n} reference llama_forward calls (positions 0..{n - 1}) at TinyLlama shape, "
+                      f"22 layers sharing layer 0's weights, single thread, {dt:.1f} s"}
+
+
+def cfg0_leg(args, rank, world, local, dist, nid):
+    """Config 0: TinyLlama greedy decode at batch 1, output-row tensor
+    parallelism over the ranks (NCCL all-gathers) when world > 1."""
+    import iq
+    c = configs.TINYLLAMA
+    t0 = time.perf_counter()
+    m = iq.Model(c, device=local, tp_rank=rank, tp_size=world, nccl_id=nid)
+    m.synth(0, threads=max(1, (os.cpu_count() or 1) // world))
+    t_load = time.perf_counter() - t0
+    prompt = iq.synth_tokens(0, "prompt:0", 8, c["vocab"])
+    m.generate(prompt, 32)   # first use (graphs, NCCL connections); fills the cache to pos 38
     if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    toks, _ = m.generate(prompt, 32)
+    e2e_s = _max_over_ranks(dist, time.perf_counter() - t0)
+    pos0, dec = 39, 64
+    m.decode_steps_timed(pos0, 3)
+    ms = _max_over_ranks(dist, m.decode_steps_timed(pos0, dec))
+    wb, _ = m.weight_bytes()
+    sh = iq.tp_shard_info(c, world, rank)
+    kv_bytes = 8 * 2 * c["n_layers"] * sh["nkv"] * c["head_dim"] * (pos0 + 1 + dec / 2)
+    step_s = ms / 1e3 / dec
+    peak, peak_kind = measured_peak()
+    ach = (wb + kv_bytes) / step_s / 1e9
+    m.close()
+    out = {"metric": "TinyLlama greedy decode tokens/s (B=1), bit-exact", "value": dec / (ms / 1e3),
+           "unit": "tokens/s", "ms_per_token": ms / dec, "n_gpus": world,
+           "parallelism": f"tp{world}", "decode_positions": f"{pos0}..{pos0 + dec - 1}", "load_s": t_load,
+           "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                        "peak_source": peak_kind, "kernel": "whole decode step (per GPU)",
+                        "bytes_per_token_per_gpu": wb + kv_bytes,
+                        "note": "stored-form weight bytes of every matvec + LM head "
+                                "(iq_model_weight_bytes) + KV reads, per token per GPU"},
+           "e2e": {"value": (len(toks) - len(prompt)) / e2e_s, "unit": "tokens/s",
+                   "h2d_bytes_per_step": 4 * len(prompt), "d2h_bytes_per_step": 4 * len(toks),
+                   "api": "iq_generate (8-token prompt + 32 greedy tokens per call, prefill included)"}}
+    if world == 1 and rank == 0 and not args.no_cpu:
+        out["cpu_baseline"] = cpu_baseline_cfg0()
+    return out
+
+
+def cpu_baseline_cfg2(budget_s=6.0):
+    """Config 2 on the CPU: rows of the reference's own matmul_vec, 1 core."""
+    orc = _oracle()
+    fn, kind = cpu_reference_lib()
+    rows = configs.CFG2_ROWS
+    mac, tt, desc = 0, 0.0, []
+    for tag, K, N in configs.CFG2_SHAPES:
+        wn, xn = configs.gemm_names(tag, K, N, rows)
+        w = orc.synth_weights(2, wn, (N, K))
+        X = orc.synth_acts(2, xn, (8, K))
+        o = np.empty(N, np.int64)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s / 4 and n < 8:
+            fn(o, w, X[n], N, K, 1)
+            n += 1
+        tt += time.perf_counter() - t0
+        mac += n * K * N
+        desc.append(f"{tag}:{n}")
+    return {"value": mac / tt / 1e9, "unit": "GMAC/s", "cores": 1, "kind": kind,
+            "sample": "rows of X through matmul_vec, single thread (" + ", ".join(desc) + f"), {tt:.1f} s"}
+
+
+def int8_peak():
+    try:
+        with open(os.path.join(ROOT, "profiles", "i8_peak.json")) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+def cfg2_leg(args):
+    """Config 2: M=512 prefill GEMM on the fused TinyLlama projections
+    (tcgen05 kind::i8 byte planes), one GPU."""
+    import torch
+    import iq
+    rows = configs.CFG2_ROWS
+    s = torch.cuda.Stream()
+    per, tot_mac, tot_ms, i8_ops = {}, 0, 0.0, 0
+    for tag, K, N in configs.CFG2_SHAPES:
+        wn, xn = configs.gemm_names(tag, K, N, rows)
+        w = torch.from_numpy(iq.synth_weights(2, wn, (N, K))).cuda()
+        X = torch.from_numpy(iq.synth_acts(2, xn, (rows, K))).cuda()
+        pk = iq.PackedTC(w, N, K)
+        npl = pk.info()[0]
+        out = torch.empty((rows, N), dtype=torch.int64, device="cuda")
+        reps = 20
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                iq.gemm_tc_dev(out, pk, X, rows, stream=s)
+            e0, e1 = _events(2)
+            e0.record(s)
+            for _ in range(reps):
+                iq.gemm_tc_dev(out, pk, X, rows, stream=s)
+            e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        macs = rows * K * N
+        # int8 tensor work: every Q16.48 MAC is npl weight planes x 8 activation digits
+        ops = 2 * macs * npl * 8
+        per[tag] = {"K": K, "N": N, "ms": ms, "gmacs": macs / ms / 1e6, "planes": npl,
+                    "int8_tops": ops / ms / 1e9}
+        tot_mac += macs
+        tot_ms += ms
+        i8_ops += ops
+        pk.free()
+        del w, X, out
+    torch.cuda.empty_cache()
+    pk8 = int8_peak()
+    tops = i8_ops / tot_ms / 1e9
+    out = {"metric": "Q16.48 prefill GEMM GMAC/s, config 2 (M=512, 4 fused TinyLlama projections), bit-exact",
+           "value": tot_mac / tot_ms / 1e6, "unit": "GMAC/s", "n_gpus": 1, "per_shape": per,
+           "roofline": {"bound": "tensor", "achieved": tops, "unit": "int8 TOP/s",
+                        "peak": pk8["tops"] if pk8 else None,
+                        "frac": tops / pk8["tops"] if pk8 else None,
+                        "peak_source": ("measured tcgen05 kind::i8 peak, " + pk8["source"]) if pk8 else
+                        "none measured", "kernel": "k_gemm_tc (all four shapes)"}}
+    if not args.no_cpu:
+        out["cpu_baseline"] = cpu_baseline_cfg2()
+    return out
+
+
+def run_ours(args):
+    import torch
+    import iq
+    rank, world, local, dist, nid = _tp_setup()
+    line = cfg1_leg(args, rank, world, local, dist)
+    if not args.headline_only:
+        line["cfg0_decode"] = cfg0_leg(args, rank, world, local, dist, nid)
+        torch.cuda.empty_cache()
+        if world == 1:
+            line["cfg2_gemm"] = cfg2_leg(args)
+    if rank == 0:
+        print(json.dumps(line))
+    if dist:
+        dist.barrier()
         dist.destroy_process_group()
 
 
@@ -497,7 +675,9 @@ def main():
     ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="config 1 only (no config-0 decode / config-2 GEMM extras)")
     ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg0", "cfg2", "cfg3", "cfg4"],
                     help="cfg1 (default, the headline): M=1 matvec microbench")
     args = ap.parse_args()

@@ -65,11 +65,14 @@ IQ_API int iq_set_device(int device);
 /* Replaces `static void matmul_vec(fixed_t *out, const int64_t *weight,
  * const fixed_t *in, int M, int N)` (llama_int.c:1014-1015) with the same
  * argument order and meaning on HOST pointers: out[M] is written in full,
- * weight [M][N] and in[N] are read. Weights are uploaded to HBM on first use
- * and cached, keyed by (weight, M, N); like the reference's loaded weights
- * (llama_int.c:2464) they must not change afterwards -- call
- * iq_weight_unregister first if they do. Returns IQ_OK or an iq_status
- * (the reference returns void and has no error path). */
+ * weight [M][N] and in[N] are read. Returns IQ_OK or an iq_status (the
+ * reference returns void and has no error path).
+ * Weights are uploaded to HBM on first use, packed and cached. A cached copy is
+ * used only while the host matrix still holds what was uploaded (see
+ * iq_weight_check_mode): the reference's streaming path frees each layer after
+ * use and the next malloc can return the same address with other weights
+ * (llama_int.c:2840-2872). Calls are not thread-safe against each other
+ * (the reference is single-threaded); serialise them. */
 IQ_API int iq_matmul_vec(int64_t *out, const int64_t *weight, const int64_t *in, int M, int N);
 
 /* Explicit residency control for iq_matmul_vec's cache (no reference
@@ -77,6 +80,23 @@ IQ_API int iq_matmul_vec(int64_t *out, const int64_t *weight, const int64_t *in,
 IQ_API int iq_weight_register(const int64_t *weight, int M, int N);
 IQ_API int iq_weight_unregister(const int64_t *weight);
 IQ_API int iq_weight_cache_clear(void);
+
+/* How iq_matmul_vec decides that a cached copy still matches the host matrix:
+ *   IQ_WCHECK_NONE    - by address and shape only (weights that never change:
+ *                       mmap'd .mgw, --cache-layers);
+ *   IQ_WCHECK_SAMPLED - (default) plus a 64-bit fingerprint of 1,152 fixed
+ *                       positions, recomputed every call (microseconds); a
+ *                       matrix that differs from the cached one in none of
+ *                       those positions is not detected;
+ *   IQ_WCHECK_FULL    - plus a hash of every value, every call (host memory
+ *                       bandwidth); copies are also found by content, so the
+ *                       streaming path's re-read layers hit the cache. */
+enum { IQ_WCHECK_NONE = 0, IQ_WCHECK_SAMPLED = 1, IQ_WCHECK_FULL = 2 };
+IQ_API int iq_weight_check_mode(int mode);
+/* Device bytes the cache may hold (default 64 GiB); least recently used
+ * entries are freed beyond it. */
+IQ_API int iq_weight_cache_limit(int64_t bytes);
+IQ_API int iq_weight_cache_stats(int *entries, int64_t *device_bytes);
 
 /* ------------------------------------------------------- device kernels */
 
@@ -100,6 +120,9 @@ IQ_API int iq_packed_free(iq_packed *p);
  * the number of residual entries (weights with nonzero bytes below p0). */
 IQ_API int iq_packed_info(const iq_packed *p, int *np, int *p0, int *residual_entries);
 IQ_API int iq_matvec_packed_dev(int64_t *d_out, const iq_packed *w, const int64_t *d_in, void *stream);
+/* Bytes of the stored form one iq_matvec_packed_dev launch reads (planes, row
+ * sums, residual; not x or out): the numerator of its HBM roofline. */
+IQ_API int iq_packed_bytes(const iq_packed *p, int64_t *bytes);
 
 /* Same result as iq_matvec_packed_dev, but allocates no device memory: for
  * callers that cannot call cudaMalloc when they run (a process whose device
@@ -133,6 +156,11 @@ IQ_API int iq_gemm_tc_dev(int64_t *d_out, const iq_packed_tc *w, const int64_t *
 /* Synchronises the current device and returns (and clears) the status that
  * kernels with bounded waits record: IQ_OK or IQ_ERR_TIMEOUT. */
 IQ_API int iq_device_status(void);
+/* Self-test of that mechanism (no reference counterpart): launches one thread
+ * that waits on an mbarrier nothing arrives at, giving up after limit_ns
+ * (<= 100 ms). Returns IQ_OK when the wait gave up as designed; the status it
+ * recorded (IQ_ERR_TIMEOUT) is then read and cleared by iq_device_status. */
+IQ_API int iq_wait_selftest(int64_t limit_ns);
 
 /* Batched rows: d_out[r][i] = matmul_vec(d_w, d_X[r])[i] for r < rows, i.e.
  * exactly `rows` independent calls of llama_int.c:1014 (the reference has no
@@ -197,6 +225,18 @@ IQ_API int iq_model_load_globals(iq_model *m, const int64_t *embed, const int64_
 /* One layer's 9 tensors in layer_weights_t order (llama_int.c:1250-1260):
  * input_layernorm, q, k, v, o, post_attention_layernorm, gate, up, down. */
 IQ_API int iq_model_load_layer(iq_model *m, int layer, const int64_t *const w[9]);
+/* The configuration a model was created with. */
+IQ_API int iq_model_config(const iq_model *m, iq_config *cfg);
+
+/* int-llm's native .mgw container (llama_int.c:386-454). iq_mgw_read_config
+ * reads its config block (so the caller can create a matching model, with or
+ * without tensor parallelism); iq_model_load_mgw maps the file and loads every
+ * tensor into the model as mgw_load does (llama_int.c:2344-2560: same header,
+ * bounds and completeness checks; lm_head_tied uses the embedding), each rank
+ * taking its own rows. IQ_ERR_ARG for a malformed file or one whose config
+ * differs from the model's. */
+IQ_API int iq_mgw_read_config(const char *path, iq_config *cfg, int *lm_head_tied);
+IQ_API int iq_model_load_mgw(iq_model *m, const char *path);
 /* Fills every weight with the seeded synthetic generator (below) for the
  * given config index, generating on `threads` host threads. */
 IQ_API int iq_model_synth(iq_model *m, int config_index, int threads);
@@ -221,9 +261,12 @@ IQ_API int iq_generate(iq_model *m, const int *prompt, int prompt_len, int max_n
 /* Batched greedy decode of B = max_batch independent sequences in lockstep
  * (the reference runs each sequence alone; rows are independent, so results
  * equal B separate generate() calls). prompts [B][prompt_len], out_tokens
- * [B][prompt_len + max_new], n_out[B]. */
+ * [B][prompt_len + max_new], n_out[B]. logit_hashes (may be NULL) receives per
+ * sequence the FNV-1a-64 over every logit of every forward that sequence's
+ * generate() would run, as iq_generate's logit_hash (costs a logits copy per
+ * step). */
 IQ_API int iq_generate_batch(iq_model *m, const int *prompts, int prompt_len, int max_new,
-                             int *out_tokens, int *n_out);
+                             int *out_tokens, int *n_out, uint64_t *logit_hashes);
 
 /* Timing helper: runs `steps` greedy decode steps (graph replays) of all
  * max_batch sequences from position pos0 with no host synchronisation and no
@@ -237,6 +280,12 @@ IQ_API int iq_decode_steps_timed(iq_model *m, int pos0, int steps, float *ms);
  * (tiles of 64 positions). 0 = always phased. Returns IQ_ERR_UNSUPPORTED if
  * the single-kernel form does not fit shared memory at this max_seq_len. */
 IQ_API int iq_model_set_attention(iq_model *m, int short_max);
+
+/* Bytes of stored weights this rank's decode step reads per token at batch 1
+ * (every projection's matvec form plus the LM head; not the KV cache), and the
+ * bytes of the GEMM forms (prefill / batched decode). The numerators of the
+ * decode roofline; no reference counterpart. */
+IQ_API int iq_model_weight_bytes(iq_model *m, int64_t *decode_bytes, int64_t *gemm_bytes);
 
 /* ------------------------------------------------ synthetic inputs (host) */
 

@@ -17,6 +17,16 @@ LLAMA7B = dict(dim=4096, n_heads=32, n_kv_heads=32, head_dim=128, n_layers=32, i
 TINY_TEST = dict(dim=256, n_heads=8, n_kv_heads=2, head_dim=32, n_layers=2, inter=704,
                  vocab=512, max_seq=128, rope_theta=10000)
 
+# Llama-2-7B geometry at reduced width for parity tests: head_dim 128, MHA
+# (n_kv_heads = n_heads), FFN / dim = 11008 / 4096; positions beyond 384 reach
+# the phased attention kernels
+GEOM7B_TEST = dict(dim=512, n_heads=4, n_kv_heads=4, head_dim=128, n_layers=2, inter=1376,
+                   vocab=1024, max_seq=448, rope_theta=10000)
+# config-3 geometry (full TinyLlama width, GQA 8:1, head_dim 64) with 2 layers and a
+# smaller vocabulary, decoding at context ~2100 with max_seq 2176
+CFG3_TEST = dict(dim=2048, n_heads=32, n_kv_heads=4, head_dim=64, n_layers=2, inter=5632,
+                 vocab=4096, max_seq=2176, rope_theta=10000)
+
 # config 1: matvec shapes as (K, N) = (input length, output rows)
 CFG1_SHAPES = [(2048, 2048), (2048, 256), (2048, 5632), (5632, 2048), (2048, 32000)]
 # config 2: prefill GEMM M=512 on fused TinyLlama projections (K, N)

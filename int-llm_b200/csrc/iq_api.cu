@@ -597,38 +597,175 @@ int take_dev_error() {
 }
 
 // ------------------------------------------------------- weight cache
+//
+// The drop-in iq_matmul_vec receives host matrices. Each is uploaded, packed
+// and cached on first use. The reference's weights never change after load
+// when they are mmap'd or cached (llama_int.c:2464, --cache-layers), but its
+// default streaming path reads every layer into fresh malloc'd buffers and
+// frees them after the layer (llama_int.c:2840-2872, mgw_stream_load_layer /
+// free_layer_weights): a later call can pass a different matrix at the same
+// address. So an entry is trusted only while the matrix's content still
+// matches what was uploaded:
+//   IQ_WCHECK_SAMPLED (default): a 64-bit fingerprint of 1,152 fixed
+//     positions (the first and last 64 values and 1,024 spread over the
+//     matrix) is recomputed on every call (microseconds); a mismatch uploads
+//     the new content;
+//   IQ_WCHECK_FULL: a hash of every value is recomputed on every call (host
+//     memory bandwidth), and entries are also found by content, so a layer
+//     re-read into a new buffer reuses its packed copy without an upload;
+//   IQ_WCHECK_NONE: the address alone (weights known to be immutable).
+// Entries are evicted least recently used beyond a byte limit of device memory.
 
-struct WEntry { Packed P; int M = 0, N = 0; int dev = 0; };
+struct WEntry {
+    Packed P;
+    int M = 0, N = 0, dev = 0;
+    uint64_t fp_sampled = 0, fp_full = 0;
+    bool has_full = false;
+    uint64_t last_use = 0;
+    int64_t bytes = 0;
+};
 static std::mutex g_wmu;
-static std::unordered_map<const void *, WEntry> g_wcache;
+static std::unordered_map<uint64_t, WEntry> g_wents;              // id -> entry
+static std::unordered_map<const void *, uint64_t> g_wptr;          // host pointer -> id
+static std::unordered_map<uint64_t, uint64_t> g_wcontent;          // content key -> id (FULL mode)
+static uint64_t g_wnext = 1, g_wclock = 0;
+static int g_wcheck = 1;                                           // IQ_WCHECK_SAMPLED
+static int64_t g_wlimit = (int64_t)64 << 30, g_wbytes = 0;
 
-// Drop-in weight cache: the host matrix is uploaded once and kept only in the
-// packed byte-plane form (same 8 bytes per weight).
-static int weight_lookup(const int64_t *w, int M, int N, int dev, bool create, Packed **pp) {
-    std::lock_guard<std::mutex> lk(g_wmu);
-    auto it = g_wcache.find(w);
-    if (it != g_wcache.end()) {
-        if (it->second.M == M && it->second.N == N && it->second.dev == dev) {
-            *pp = &it->second.P;
-            return IQ_OK;
-        }
-        free_packed(&it->second.P);
-        g_wcache.erase(it);
+static inline uint64_t mix64(uint64_t h, uint64_t v) {
+    h ^= v + 0x9E3779B97F4A7C15ull + (h << 6) + (h >> 2);
+    h *= 0xBF58476D1CE4E5B9ull;
+    return h ^ (h >> 31);
+}
+
+static uint64_t fingerprint_sampled(const int64_t *w, int M, int N) {
+    const uint64_t n = (uint64_t)M * (uint64_t)N;
+    uint64_t h = mix64(0x6A09E667F3BCC909ull, n);
+    const uint64_t edge = n < 64 ? n : 64;
+    for (uint64_t i = 0; i < edge; i++) h = mix64(h, (uint64_t)w[i]);
+    for (uint64_t i = 0; i < edge; i++) h = mix64(h, (uint64_t)w[n - 1 - i]);
+    uint64_t r = 0x243F6A8885A308D3ull;
+    for (int k = 0; k < 1024; k++) {
+        r = r * 6364136223846793005ull + 1442695040888963407ull;
+        const uint64_t i = (uint64_t)(((unsigned __int128)(r >> 11) * n) >> 53);
+        h = mix64(h, (uint64_t)w[i]);
     }
-    if (!create) { *pp = nullptr; return IQ_OK; }
+    return h;
+}
+
+// Every value, four independent lanes (multiply-xor, then a final mix).
+static uint64_t fingerprint_full(const int64_t *w, int M, int N) {
+    const uint64_t n = (uint64_t)M * (uint64_t)N;
+    uint64_t h0 = 0x9E3779B97F4A7C15ull, h1 = 0xC2B2AE3D27D4EB4Full, h2 = 0x165667B19E3779F9ull,
+             h3 = 0xD6E8FEB86659FD93ull;
+    const uint64_t K0 = 0xFF51AFD7ED558CCDull;
+    uint64_t i = 0;
+    for (; i + 4 <= n; i += 4) {
+        h0 = (h0 ^ (uint64_t)w[i]) * K0;
+        h1 = (h1 ^ (uint64_t)w[i + 1]) * K0;
+        h2 = (h2 ^ (uint64_t)w[i + 2]) * K0;
+        h3 = (h3 ^ (uint64_t)w[i + 3]) * K0;
+        h0 ^= h0 >> 29; h1 ^= h1 >> 29; h2 ^= h2 >> 29; h3 ^= h3 >> 29;
+    }
+    for (; i < n; i++) h0 = mix64(h0, (uint64_t)w[i]);
+    return mix64(mix64(mix64(mix64(n, h0), h1), h2), h3);
+}
+
+static uint64_t content_key(uint64_t full, int M, int N, int dev) {
+    return mix64(mix64(mix64(full, (uint64_t)M), (uint64_t)N), (uint64_t)dev);
+}
+
+static void wcache_drop(uint64_t id) {
+    auto it = g_wents.find(id);
+    if (it == g_wents.end()) return;
+    if (it->second.has_full) {
+        auto c = g_wcontent.find(content_key(it->second.fp_full, it->second.M, it->second.N, it->second.dev));
+        if (c != g_wcontent.end() && c->second == id) g_wcontent.erase(c);
+    }
+    g_wbytes -= it->second.bytes;
+    free_packed(&it->second.P);
+    g_wents.erase(it);
+    for (auto p = g_wptr.begin(); p != g_wptr.end();)
+        p = p->second == id ? g_wptr.erase(p) : std::next(p);
+}
+
+// Least recently used entries out until `extra` more bytes fit the limit.
+static void wcache_make_room(int64_t extra) {
+    while (!g_wents.empty() && g_wbytes + extra > g_wlimit) {
+        uint64_t oldest = 0, t = UINT64_MAX;
+        for (auto &kv : g_wents)
+            if (kv.second.last_use < t) { t = kv.second.last_use; oldest = kv.first; }
+        wcache_drop(oldest);
+    }
+}
+
+static int weight_upload(const int64_t *w, int M, int N, int dev, WEntry *en) {
     size_t bytes = (size_t)M * N * sizeof(int64_t);
     int64_t *d = nullptr;
     IQ_CUDA(cudaMalloc(&d, bytes));
     cudaError_t e = cudaMemcpy(d, w, bytes, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) { cudaFree(d); return cuda_fail(e); }
-    WEntry en; en.M = M; en.N = N; en.dev = dev;
-    int rc = pack_weights(d, M, N, 0, &en.P);
+    en->M = M; en->N = N; en->dev = dev;
+    int rc = pack_weights(d, M, N, 0, &en->P);
     e = cudaDeviceSynchronize();
     cudaFree(d);
     if (rc) return rc;
-    if (e != cudaSuccess) { free_packed(&en.P); return cuda_fail(e); }
-    g_wcache[w] = en;
-    *pp = &g_wcache[w].P;
+    if (e != cudaSuccess) { free_packed(&en->P); return cuda_fail(e); }
+    en->bytes = packed_bytes(en->P);
+    return IQ_OK;
+}
+
+// Finds (or uploads) the packed copy of host matrix w [M][N] on dev.
+static int weight_lookup(const int64_t *w, int M, int N, int dev, Packed **pp) {
+    std::lock_guard<std::mutex> lk(g_wmu);
+    const int mode = g_wcheck;
+    const uint64_t fs = mode == 1 ? fingerprint_sampled(w, M, N) : 0;
+    const uint64_t ff = mode == 2 ? fingerprint_full(w, M, N) : 0;
+    auto pit = g_wptr.find(w);
+    if (pit != g_wptr.end()) {
+        auto eit = g_wents.find(pit->second);
+        if (eit != g_wents.end()) {
+            WEntry &e = eit->second;
+            const bool same = e.M == M && e.N == N && e.dev == dev &&
+                              (mode == 0 || (mode == 1 && e.fp_sampled == fs) ||
+                               (mode == 2 && e.has_full && e.fp_full == ff));
+            if (same) {
+                e.last_use = ++g_wclock;
+                *pp = &e.P;
+                return IQ_OK;
+            }
+            // the address now holds another matrix: forget the old entry
+            // (its packed copy stays findable by content in FULL mode)
+            if (!e.has_full) wcache_drop(pit->second);
+            else g_wptr.erase(pit);
+        } else {
+            g_wptr.erase(pit);
+        }
+    }
+    if (mode == 2) {  // the same content under another address
+        auto c = g_wcontent.find(content_key(ff, M, N, dev));
+        if (c != g_wcontent.end() && g_wents.count(c->second)) {
+            WEntry &e = g_wents[c->second];
+            e.last_use = ++g_wclock;
+            g_wptr[w] = c->second;
+            *pp = &e.P;
+            return IQ_OK;
+        }
+    }
+    WEntry en;
+    int rc = weight_upload(w, M, N, dev, &en);
+    if (rc) return rc;
+    wcache_make_room(en.bytes);
+    en.fp_sampled = fingerprint_sampled(w, M, N);
+    en.fp_full = mode == 2 ? ff : 0;
+    en.has_full = mode == 2;
+    en.last_use = ++g_wclock;
+    const uint64_t id = g_wnext++;
+    g_wbytes += en.bytes;
+    g_wents[id] = en;
+    g_wptr[w] = id;
+    if (en.has_full) g_wcontent[content_key(ff, M, N, dev)] = id;
+    *pp = &g_wents[id].P;
     return IQ_OK;
 }
 
@@ -673,22 +810,47 @@ IQ_API int iq_weight_register(const int64_t *weight, int M, int N) {
     int rc = ensure_device(g_host_device);
     if (rc) return rc;
     Packed *d;
-    return weight_lookup(weight, M, N, g_host_device, true, &d);
+    return weight_lookup(weight, M, N, g_host_device, &d);
 }
 
 IQ_API int iq_weight_unregister(const int64_t *weight) {
     std::lock_guard<std::mutex> lk(g_wmu);
-    auto it = g_wcache.find(weight);
-    if (it == g_wcache.end()) return IQ_ERR_STATE;
-    free_packed(&it->second.P);
-    g_wcache.erase(it);
+    auto it = g_wptr.find(weight);
+    if (it == g_wptr.end()) return IQ_ERR_STATE;
+    wcache_drop(it->second);
     return IQ_OK;
 }
 
 IQ_API int iq_weight_cache_clear(void) {
     std::lock_guard<std::mutex> lk(g_wmu);
-    for (auto &kv : g_wcache) free_packed(&kv.second.P);
-    g_wcache.clear();
+    for (auto &kv : g_wents) free_packed(&kv.second.P);
+    g_wents.clear();
+    g_wptr.clear();
+    g_wcontent.clear();
+    g_wbytes = 0;
+    return IQ_OK;
+}
+
+IQ_API int iq_weight_check_mode(int mode) {
+    if (mode < IQ_WCHECK_NONE || mode > IQ_WCHECK_FULL) return IQ_ERR_ARG;
+    std::lock_guard<std::mutex> lk(g_wmu);
+    g_wcheck = mode;
+    return IQ_OK;
+}
+
+IQ_API int iq_weight_cache_limit(int64_t bytes) {
+    if (bytes < 0) return IQ_ERR_ARG;
+    std::lock_guard<std::mutex> lk(g_wmu);
+    g_wlimit = bytes;
+    wcache_make_room(0);
+    return IQ_OK;
+}
+
+IQ_API int iq_weight_cache_stats(int *entries, int64_t *device_bytes) {
+    if (!entries || !device_bytes) return IQ_ERR_ARG;
+    std::lock_guard<std::mutex> lk(g_wmu);
+    *entries = (int)g_wents.size();
+    *device_bytes = g_wbytes;
     return IQ_OK;
 }
 
@@ -716,7 +878,7 @@ IQ_API int iq_matmul_vec(int64_t *out, const int64_t *weight, const int64_t *in,
     int rc = ensure_device(dev);
     if (rc) return rc;
     Packed *dw = nullptr;
-    rc = weight_lookup(weight, M, N, dev, true, &dw);
+    rc = weight_lookup(weight, M, N, dev, &dw);
     if (rc) return rc;
     std::lock_guard<std::mutex> lk(g_stage_mu);
     Staging &st = g_stage[dev];
@@ -815,6 +977,12 @@ IQ_API int iq_packed_info(const iq_packed *p, int *np, int *p0, int *residual_en
     return IQ_OK;
 }
 
+IQ_API int iq_packed_bytes(const iq_packed *p, int64_t *bytes) {
+    if (!p || !bytes) return IQ_ERR_ARG;
+    *bytes = packed_bytes(p->P);
+    return IQ_OK;
+}
+
 IQ_API int iq_matvec_packed_dev(int64_t *d_out, const iq_packed *w, const int64_t *d_in, void *stream) {
     if (!d_out || !w || !d_in || d_out == d_in) return IQ_ERR_ARG;
     int dev, rc;
@@ -876,6 +1044,21 @@ IQ_API int iq_device_status(void) {
     if ((rc = cur_device(&dev))) return rc;
     IQ_CUDA(cudaDeviceSynchronize());
     return take_dev_error();
+}
+
+IQ_API int iq_wait_selftest(int64_t limit_ns) {
+    if (limit_ns < 0 || limit_ns > 100000000) return IQ_ERR_ARG;
+    int dev, rc;
+    if ((rc = cur_device(&dev))) return rc;
+    int *d = nullptr, h = -1;
+    IQ_CUDA(cudaMalloc(&d, sizeof(int)));
+    k_wait_selftest<<<1, 32, 0, lib_stream()>>>((uint64_t)limit_ns, d);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&h, d, sizeof(int), cudaMemcpyDeviceToHost, lib_stream());
+    if (e == cudaSuccess) e = cudaStreamSynchronize(lib_stream());
+    cudaFree(d);
+    if (e != cudaSuccess) return cuda_fail(e);
+    return h == 0 ? IQ_OK : IQ_ERR_STATE;  // the wait must have given up
 }
 
 }  // extern "C"

@@ -4,3 +4,4 @@
 #include "iq_model.cu"
 #include "iq_synth.cu"
 #include "iq_noalloc.cu"
+#include "iq_mgw.cu"

@@ -626,6 +626,12 @@ IQ_API int iq_model_create_tp(const iq_config *cfg, int max_batch, int device, i
     return IQ_OK;
 }
 
+IQ_API int iq_model_config(const iq_model *m, iq_config *cfg) {
+    if (!m || !cfg) return IQ_ERR_ARG;
+    *cfg = m->c;
+    return IQ_OK;
+}
+
 IQ_API int iq_model_create(const iq_config *cfg, int max_batch, int device, iq_model **out) {
     return iq_model_create_tp(cfg, max_batch, device, 0, 1, nullptr, out);
 }
@@ -882,7 +888,8 @@ IQ_API int iq_generate(iq_model *m, const int *prompt, int plen, int max_new, in
     return take_dev_error();
 }
 
-IQ_API int iq_generate_batch(iq_model *m, const int *prompts, int plen, int max_new, int *out, int *n_out) {
+IQ_API int iq_generate_batch(iq_model *m, const int *prompts, int plen, int max_new, int *out, int *n_out,
+                             uint64_t *logit_hashes) {
     if (!m || !prompts || !out || !n_out || plen < 1 || max_new < 1) return IQ_ERR_ARG;
     if (!model_ready(m)) return IQ_ERR_STATE;
     const iq_config &c = m->c;
@@ -892,11 +899,34 @@ IQ_API int iq_generate_batch(iq_model *m, const int *prompts, int plen, int max_
     if (plen > c.max_seq_len) return IQ_ERR_RANGE;
     int rc;
     if ((rc = iq_model_reset(m))) return rc;
-    for (int b = 0; b < B; b++)  // each sequence's prompt as batched rows
-        if ((rc = enqueue_prefill(m, b, prompts + (size_t)b * plen, plen, nullptr))) return rc;
+    const bool hash = logit_hashes != nullptr;
+    const int V = c.vocab_size;
+    std::vector<int64_t> hv;
+    for (int b = 0; b < B; b++) {  // each sequence's prompt as batched rows
+        if ((rc = enqueue_prefill(m, b, prompts + (size_t)b * plen, plen, hash ? &hv : nullptr))) return rc;
+        if (hash) {
+            logit_hashes[b] = fnv_mix(1469598103934665603ULL, hv.data(), hv.size());
+            hv.clear();
+        }
+    }
     const int steps = std::min(max_new - 1, c.max_seq_len - plen);
-    for (int i = 1; i <= steps; i++)
+    std::vector<int64_t> lg;
+    std::vector<int> argm, live(B, 1);
+    if (hash) { lg.resize((size_t)B * V); argm.resize(B); }
+    for (int i = 1; i <= steps; i++) {
         if ((rc = run_step(m, B, plen + i))) return rc;
+        if (!hash) continue;
+        // every sequence's logits of this step enter its hash until (and
+        // including) the step that samples EOS, as the reference's loop forwards
+        IQ_CUDA(cudaMemcpyAsync(lg.data(), m->logits, lg.size() * 8, cudaMemcpyDeviceToHost, m->s));
+        IQ_CUDA(cudaMemcpyAsync(argm.data(), m->d_arg, (size_t)B * 4, cudaMemcpyDeviceToHost, m->s));
+        IQ_CUDA(cudaStreamSynchronize(m->s));
+        for (int b = 0; b < B; b++) {
+            if (!live[b]) continue;
+            logit_hashes[b] = fnv_mix(logit_hashes[b], lg.data() + (size_t)b * V, V);
+            if (argm[b] == 2) live[b] = 0;
+        }
+    }
     const int stride = c.max_seq_len + 1;
     std::vector<int> hist((size_t)B * stride);
     IQ_CUDA(cudaMemcpyAsync(hist.data(), m->d_hist, hist.size() * 4, cudaMemcpyDeviceToHost, m->s));
@@ -924,6 +954,20 @@ IQ_API int iq_model_set_attention(iq_model *m, int short_max) {
     IQ_CUDA(cudaStreamSynchronize(m->s));
     if (m->graph_s) { cudaGraphExecDestroy(m->graph_s); m->graph_s = nullptr; }
     m->att_short = short_max;
+    return IQ_OK;
+}
+
+IQ_API int iq_model_weight_bytes(iq_model *m, int64_t *decode_bytes, int64_t *gemm_bytes) {
+    if (!m || !decode_bytes || !gemm_bytes) return IQ_ERR_ARG;
+    if (!model_ready(m)) return IQ_ERR_STATE;
+    int64_t d = packed_bytes(m->plm), g = 0;
+    for (const std::vector<Packed> *v : {&m->pqkv, &m->po, &m->pgu, &m->pdown})
+        for (const Packed &P : *v) d += packed_bytes(P);
+    for (const std::vector<PackedTC> *v : {&m->tqkv, &m->to, &m->tgu, &m->tdown})
+        for (const PackedTC &P : *v) g += (int64_t)P.np * P.Mpad * P.Kpad + 16 * (int64_t)P.Mpad;
+    g += (int64_t)m->tlm.np * m->tlm.Mpad * m->tlm.Kpad + 16 * (int64_t)m->tlm.Mpad;
+    *decode_bytes = d;
+    *gemm_bytes = g;
     return IQ_OK;
 }
 

@@ -61,10 +61,10 @@ extern "C" IQ_API int iq_matvec_packed_noalloc_dev(int64_t *d_out, const iq_pack
     if (!d_out || !w || !d_in || d_out == d_in) return IQ_ERR_ARG;
     int wdev = -1;
     const Packed *P = iq_packed_inner(w, &wdev);
-    if (P->Mp > IQ_NOALLOC_MAX_ROWS) return IQ_ERR_RANGE;  // more rows than the fixed scratch holds
     int dev = 0;
     IQ_CUDA(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64 || dev != wdev) return IQ_ERR_ARG;
+    if (dev < 0 || dev >= 64 || dev != wdev) return IQ_ERR_ARG;  // checked first, as iq_matvec_packed_dev does
+    if (P->Mp > IQ_NOALLOC_MAX_ROWS) return IQ_ERR_RANGE;  // more rows than the fixed scratch holds
     int rc = ensure_device_pub(dev);  // device properties + library stream; no memory allocation
     if (rc) return rc;
     RowAcc *rows = nullptr;

@@ -55,6 +55,14 @@ struct Packed {
     int64_t *res_val = nullptr; // [nnz] w_lo
 };
 
+// Bytes of the stored form one matvec launch reads: planes, 128-bit row sums
+// and the residual CSR (x and out not counted).
+inline int64_t packed_bytes(const Packed &P) {
+    int64_t b = (int64_t)P.np * P.Mp * P.Kp + 16 * (int64_t)P.Mp;
+    if (P.nnz) b += 4 * ((int64_t)P.Mp + 1) + 12 * (int64_t)P.nnz;
+    return b;
+}
+
 // What a kernel needs of a Packed beyond the planes (passed by value).
 struct PackedRes {
     int p0;

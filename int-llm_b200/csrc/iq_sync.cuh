@@ -43,16 +43,27 @@ __device__ __forceinline__ uint64_t global_ns() {
 }
 // Gives up after IQ_WAIT_NS of wall time (healthy waits here last microseconds).
 #define IQ_WAIT_NS 2000000000ull
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64_t limit_ns = IQ_WAIT_NS) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     for (;;) {
         for (int i = 0; i < 64; i++)
             if (mbar_try_wait(bar, parity)) return true;
-        if (global_ns() - t0 > IQ_WAIT_NS) break;
+        if (global_ns() - t0 > limit_ns) break;
     }
     atomicExch(&g_iq_err, (int)IQ_ERR_TIMEOUT);
     return false;
+}
+
+// Self-test of the bounded wait: one thread waits on an mbarrier that nothing
+// arrives at, for limit_ns; *waited = 1 if the wait (wrongly) succeeded, else 0.
+__global__ void k_wait_selftest(uint64_t limit_ns, int *waited) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        *waited = mbar_wait(&bar, 0, limit_ns) ? 1 : 0;
+    }
 }
 
 // 2-D tiled TMA load (no multicast) into shared memory, completing on bar.

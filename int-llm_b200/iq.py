@@ -1,4 +1,8 @@
-"""Python host-side binding of libiq.so (the C ABI in include/iq.h).
+"""Python host-side binding of libiq.so (the C ABI in include/iq.h) -- TEST AND
+BENCH TOOLING, not the product: the product is the C ABI (include/iq.h,
+libiq.so), which C hosts such as llama_int.c call directly. This module is how
+the tests and bench.py reach that ABI from Python; torch appears here only to
+hand over device memory and streams.
 
 This is a thin ctypes mirror of the reference's operator surface: ``matmul_vec``
 (llama_int.c:1014) with its argument order ``(out, weight, in, M, N)``, where M
@@ -32,6 +36,9 @@ SIGNATURES = {
     "iq_weight_register": (_I, [_P, _I, _I]),
     "iq_weight_unregister": (_I, [_P]),
     "iq_weight_cache_clear": (_I, []),
+    "iq_weight_check_mode": (_I, [_I]),
+    "iq_weight_cache_limit": (_I, [_I64]),
+    "iq_weight_cache_stats": (_I, [_P, _P]),
     "iq_matvec_dev": (_I, [_P, _P, _P, _I, _I, _P]),
     "iq_gemm_dev": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "iq_pack_weights_dev": (_I, [_P, _I, _I, _P, _P]),
@@ -39,11 +46,13 @@ SIGNATURES = {
     "iq_packed_info": (_I, [_P, _P, _P, _P]),
     "iq_matvec_packed_dev": (_I, [_P, _P, _P, _P]),
     "iq_matvec_packed_noalloc_dev": (_I, [_P, _P, _P, _P]),
+    "iq_packed_bytes": (_I, [_P, _P]),
     "iq_pack_weights_tc_dev": (_I, [_P, _I, _I, _P, _P]),
     "iq_packed_tc_free": (_I, [_P]),
     "iq_packed_tc_info": (_I, [_P, _P, _P, _P]),
     "iq_gemm_tc_dev": (_I, [_P, _P, _P, _I, _P]),
     "iq_device_status": (_I, []),
+    "iq_wait_selftest": (_I, [_I64]),
     "iq_fp_dev": (_I, [_I, _P, _P, _P, _I64, _P]),
     "iq_rmsnorm_dev": (_I, [_P, _P, _P, _I, _I, _P]),
     "iq_softmax_dev": (_I, [_P, _I, _I, _P]),
@@ -55,12 +64,16 @@ SIGNATURES = {
     "iq_model_load_globals": (_I, [_P, _P, _P, _P]),
     "iq_model_load_layer": (_I, [_P, _I, _P]),
     "iq_model_synth": (_I, [_P, _I, _I]),
+    "iq_model_config": (_I, [_P, _P]),
+    "iq_mgw_read_config": (_I, [ctypes.c_char_p, _P, _P]),
+    "iq_model_load_mgw": (_I, [_P, ctypes.c_char_p]),
     "iq_model_reset": (_I, [_P]),
     "iq_forward": (_I, [_P, _I, _I, _P, _P]),
     "iq_generate": (_I, [_P, _P, _I, _I, _P, _P, _P]),
-    "iq_generate_batch": (_I, [_P, _P, _I, _I, _P, _P]),
+    "iq_generate_batch": (_I, [_P, _P, _I, _I, _P, _P, _P]),
     "iq_decode_steps_timed": (_I, [_P, _I, _I, _P]),
     "iq_model_set_attention": (_I, [_P, _I]),
+    "iq_model_weight_bytes": (_I, [_P, _P, _P]),
     "iq_tensor_seed": (ctypes.c_uint64, [_I, ctypes.c_char_p]),
     "iq_synth_weights": (_I, [ctypes.c_uint64, _P, _I64]),
     "iq_synth_acts": (_I, [ctypes.c_uint64, _P, _I64]),
@@ -155,6 +168,24 @@ def weight_cache_clear():
     _call("iq_weight_cache_clear")
 
 
+WCHECK = dict(none=0, sampled=1, full=2)
+
+
+def weight_check_mode(mode):
+    _call("iq_weight_check_mode", WCHECK[mode] if isinstance(mode, str) else mode)
+
+
+def weight_cache_limit(nbytes):
+    _call("iq_weight_cache_limit", nbytes)
+
+
+def weight_cache_stats():
+    """(entries, device bytes) of the drop-in's weight cache."""
+    e, b = ctypes.c_int(), ctypes.c_int64()
+    _call("iq_weight_cache_stats", ctypes.byref(e), ctypes.byref(b))
+    return e.value, b.value
+
+
 def nccl_unique_id():
     """128-byte NCCL id for iq_model_create_tp (made on one rank, shared with all)."""
     buf = ctypes.create_string_buffer(128)
@@ -169,6 +200,16 @@ def tp_shard_info(cfg, tp_size, tp_rank):
     _call("iq_tp_shard_info", ctypes.byref(c), tp_size, tp_rank, info)
     keys = ("q_lo", "nh", "kv_lo", "nkv", "d_lo", "d_n", "it_lo", "it_n")
     return dict(zip(keys, list(info)))
+
+
+def mgw_config(path):
+    """(config dict, lm_head_tied) of an int-llm .mgw file."""
+    c = Config()
+    tied = ctypes.c_int(0)
+    _call("iq_mgw_read_config", os.fsencode(path), ctypes.byref(c), ctypes.byref(tied))
+    return dict(dim=c.hidden_dim, n_heads=c.num_heads, n_kv_heads=c.num_kv_heads, head_dim=c.head_dim,
+                n_layers=c.num_layers, inter=c.intermediate_dim, vocab=c.vocab_size, max_seq=c.max_seq_len,
+                rope_theta=c.rope_theta), bool(tied.value)
 
 
 def set_device(d):
@@ -194,6 +235,12 @@ class Packed:
         a, b, c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
         _call("iq_packed_info", self.h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c))
         return a.value, b.value, c.value
+
+    def nbytes(self):
+        """Bytes of the stored form one matvec launch reads (iq_packed_bytes)."""
+        b = ctypes.c_int64()
+        _call("iq_packed_bytes", self.h, ctypes.byref(b))
+        return b.value
 
     def free(self):
         if self.h:
@@ -329,6 +376,10 @@ class Model:
             arr = (ctypes.c_void_p * 9)(*[a.ctypes.data for a in lay])
             _call("iq_model_load_layer", self.h, l, arr)
 
+    def load_mgw(self, path):
+        """Every tensor from an int-llm .mgw file (iq_model_load_mgw)."""
+        _call("iq_model_load_mgw", self.h, os.fsencode(path))
+
     def synth(self, config_index, threads=None):
         _call("iq_model_synth", self.h, config_index, threads or os.cpu_count() or 1)
 
@@ -350,18 +401,27 @@ class Model:
               ctypes.byref(h) if logit_hash else None)
         return out[:n.value].tolist(), (h.value if logit_hash else None)
 
-    def generate_batch(self, prompts, max_new):
+    def generate_batch(self, prompts, max_new, logit_hash=False):
+        """Tokens per sequence; with logit_hash=True also the per-sequence hashes."""
         pr = np.ascontiguousarray(prompts, dtype=np.int32)
         B, L = pr.shape
         assert B == self.max_batch
         out = np.zeros((B, L + max_new), dtype=np.int32)
         n = np.zeros(B, dtype=np.int32)
-        _call("iq_generate_batch", self.h, _hp(pr), L, max_new, _hp(out), _hp(n))
-        return [out[b, :n[b]].tolist() for b in range(B)]
+        hs = np.zeros(B, dtype=np.uint64)
+        _call("iq_generate_batch", self.h, _hp(pr), L, max_new, _hp(out), _hp(n), _hp(hs) if logit_hash else None)
+        toks = [out[b, :n[b]].tolist() for b in range(B)]
+        return (toks, [int(h) for h in hs]) if logit_hash else toks
 
     def set_attention(self, short_max):
         """Contexts up to short_max use the single-kernel attention (0 = phased only)."""
         _call("iq_model_set_attention", self.h, short_max)
+
+    def weight_bytes(self):
+        """(decode bytes per token, GEMM-form bytes) of this rank's stored weights."""
+        d, g = ctypes.c_int64(), ctypes.c_int64()
+        _call("iq_model_weight_bytes", self.h, ctypes.byref(d), ctypes.byref(g))
+        return d.value, g.value
 
     def decode_steps_timed(self, pos0, steps):
         ms = ctypes.c_float(0)

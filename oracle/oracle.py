@@ -5,7 +5,10 @@ this module. It exposes:
   * ``O``   -- libiqoracle.so, the C restatement of the reference path
                (iq_oracle.c), always available once built;
   * ``ref()`` -- oracle/_ref/libllamaref.so, the reference llama_int.c compiled
-               from source (ref_harness.c), or None where it was not built.
+               from source (ref_harness.c), or None where it was not built;
+  * ``ref(shim=True)`` -- oracle/_ref/libllamaref_iq.so, the same reference
+               with its matmul_vec replaced by the libiq.so drop-in
+               (include/iq_matvec_shim.h): the integration check of that shim.
 """
 import ctypes
 import os
@@ -16,6 +19,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "libiqoracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libllamaref.so")
+REF_IQ_SO = os.path.join(HERE, "_ref", "libllamaref_iq.so")
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -66,31 +70,43 @@ O = _load_oracle()
 _REF = None
 
 
-def ref():
-    """The reference compiled from source, or None when oracle/_ref was not built."""
-    global _REF
-    if _REF is None and os.path.exists(REF_SO):
-        L = ctypes.CDLL(REF_SO)
-        sig = {
-            "ref_matmul_vec": (None, [_P, _P, _P, _I, _I]),
-            "ref_matmul_vec_mt": (None, [_P, _P, _P, _I, _I, _I]),
-            "ref_rmsnorm": (None, [_P, _P, _P, _I]),
-            "ref_softmax": (None, [_P, _I]),
-            "ref_bf16_to_q1648": (_I64, [ctypes.c_uint16]),
-            "ref_fp": (_I64, [_I, _I64, _I64]),
-            "ref_rope_tables": (None, [_I, _I, _I, _P, _P]),
-            "ref_model_create": (_P, [_P, _P, _P, _P, _P]),
-            "ref_model_reset": (None, [_P]),
-            "ref_model_forward": (_I, [_P, _I, _I, _P]),
-            "ref_model_generate": (_I, [_P, _P, _I, _I, _P]),
-            "ref_model_free": (None, [_P]),
-        }
-        for k, (r, a) in sig.items():
+_REF_IQ = None
+_REF_SIG = {
+    "ref_matmul_vec": (None, [_P, _P, _P, _I, _I]),
+    "ref_matmul_vec_mt": (None, [_P, _P, _P, _I, _I, _I]),
+    "ref_rmsnorm": (None, [_P, _P, _P, _I]),
+    "ref_softmax": (None, [_P, _I]),
+    "ref_bf16_to_q1648": (_I64, [ctypes.c_uint16]),
+    "ref_fp": (_I64, [_I, _I64, _I64]),
+    "ref_rope_tables": (None, [_I, _I, _I, _P, _P]),
+    "ref_model_create": (_P, [_P, _P, _P, _P, _P]),
+    "ref_model_reset": (None, [_P]),
+    "ref_model_forward": (_I, [_P, _I, _I, _P]),
+    "ref_model_generate": (_I, [_P, _P, _I, _I, _P]),
+    "ref_model_free": (None, [_P]),
+    "ref_model_open_mgw": (_P, [ctypes.c_char_p, _I]),
+    "ref_model_close_mgw": (None, [_P]),
+}
+
+
+def ref(shim=False):
+    """The reference compiled from source (or, shim=True, its drop-in build
+    linked to libiq.so), or None when oracle/_ref does not hold it."""
+    global _REF, _REF_IQ
+    path = REF_IQ_SO if shim else REF_SO
+    cur = _REF_IQ if shim else _REF
+    if cur is None and os.path.exists(path):
+        L = ctypes.CDLL(path)
+        for k, (r, a) in _REF_SIG.items():
             f = getattr(L, k)
             f.restype = r
             f.argtypes = a
-        _REF = L
-    return _REF
+        cur = L
+        if shim:
+            _REF_IQ = L
+        else:
+            _REF = L
+    return cur
 
 
 def p(a):

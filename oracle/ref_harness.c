@@ -16,9 +16,20 @@
  *   ref_rope_tables    -> rope_init             llama_int.c:960-986
  *   ref_model_*        -> llama_forward / generate on caller-owned weights
  *                         llama_int.c:2807-2886, 3067-3135
+ *   ref_model_open_mgw -> mgw_load (mmap, layers cached) or mgw_load_streaming
+ *                         (layers pread into fresh buffers and freed after
+ *                         every layer), llama_int.c:2344-2803
+ *
+ * Built a second time against a copy of llama_int.c whose matmul_vec is
+ * renamed and replaced by the libiq.so drop-in (include/iq_matmul_vec_shim.h):
+ * oracle/_ref/libllamaref_iq.so, the integration test of that shim.
  */
 #define main llama_int_main
+#ifdef REF_SOURCE
+#include REF_SOURCE   /* a patched copy of llama_int.c (the drop-in shim build) */
+#else
 #include "llama_int.c"
+#endif
 #undef main
 
 #include <pthread.h>
@@ -155,5 +166,38 @@ REFAPI void ref_model_free(void *h) {
     kv_cache_free(&m->kv);
     free(m->scratch_buf);
     free(m->cached_layers);
+    free(m);
+}
+
+/* Opens a .mgw model the way main() does for --native / --native-stream
+ * (llama_int.c:4877-4910, 5048-5084). Returns NULL on any load error. */
+REFAPI void *ref_model_open_mgw(const char *path, int streaming) {
+    llama_model_t *m = (llama_model_t *)calloc(1, sizeof(llama_model_t));
+    if (!m) return NULL;
+    m->native_stream_fd = -1;
+    int rc = streaming ? mgw_load_streaming(m, path) : mgw_load(m, path);
+    if (rc != 0) { free(m); return NULL; }
+    rope_init(&m->rope, &m->cfg);
+    if (kv_cache_init(&m->kv, &m->cfg) != 0) return NULL;
+    llama_init_scratch(m);
+    return m;
+}
+
+REFAPI void ref_model_close_mgw(void *h) {
+    llama_model_t *m = (llama_model_t *)h;
+    if (!m) return;
+    rope_free(&m->rope);
+    kv_cache_free(&m->kv);
+    free(m->scratch_buf);
+    if (m->native_loaded) {
+        free(m->cached_layers);
+        munmap(m->native_mmap, m->native_mmap_size);
+    } else if (m->native_stream) {
+        if (!m->lm_head_tied) free(m->lm_head);
+        free(m->embed_tokens);
+        free(m->final_norm);
+        free(m->ns_index);
+        if (m->native_stream_fd >= 0) close(m->native_stream_fd);
+    }
     free(m);
 }

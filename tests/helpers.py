@@ -69,3 +69,41 @@ class OracleModel:
 
     def close(self):
         getattr(self.L, self.pre + "model_free")(self.h)
+
+
+# ------------------------------------------------------------ .mgw files
+
+MGW_NAMES = {"embed": "model.embed_tokens.weight", "final_norm": "model.norm.weight",
+             "lm_head": "lm_head.weight"}
+
+
+def write_mgw(path, c, w, tied=False):
+    """Writes a model in int-llm's native .mgw container (llama_int.c:386-454):
+    64-byte header ("MGW\\0", version 1, endian tag 0x01020304, tensor count,
+    index and data offsets), 64-byte config block (llama_config_t fields +
+    lm_head_tied), 96-byte index entries (name[64], elements, offset, ndims,
+    shape[2]), then 8-byte aligned little-endian int64 data."""
+    import struct
+    tensors = [(MGW_NAMES["embed"], w["embed"]), (MGW_NAMES["final_norm"], w["final_norm"])]
+    if not tied:
+        tensors.append((MGW_NAMES["lm_head"], w["lm_head"]))
+    for l, lay in enumerate(w["layers"]):
+        for t, a in zip(configs.LAYER_TENSORS, lay):
+            tensors.append((configs.layer_name(l, t), a))
+    n = len(tensors)
+    index_off = 128
+    data_off = index_off + 96 * n
+    data_off = (data_off + 7) // 8 * 8
+    hdr = struct.pack("<4sIIIQQ32s", b"MGW\0", 1, 0x01020304, n, index_off, data_off, b"\0" * 32)
+    cfg = struct.pack("<10i24s", c["dim"], c["n_heads"], c["n_kv_heads"], c["head_dim"], c["n_layers"],
+                      c["inter"], c["vocab"], c["max_seq"], c["rope_theta"], 1 if tied else 0, b"\0" * 24)
+    idx, off = [], data_off
+    for name, a in tensors:
+        shp = list(a.shape) + [0] * (2 - a.ndim)
+        idx.append(struct.pack("<64sQQIIII", name.encode(), a.size, off, a.ndim, shp[0], shp[1], 0))
+        off += a.size * 8
+    with open(path, "wb") as f:
+        f.write(hdr + cfg + b"".join(idx))
+        f.write(b"\0" * (data_off - f.tell()))
+        for name, a in tensors:
+            f.write(np.ascontiguousarray(a, dtype="<i8").tobytes())

@@ -360,3 +360,99 @@ def test_gemm_plane_window_and_residual():
     iq.gemm_tc_dev(dg, pc, dev(X), 64)
     assert (host(dg) == orc.matmul_rows(wc, X)).all()
     pc.free()
+
+
+# ---------------------------------------------------- config-2 reference golden
+
+def test_gemm_tc_cfg2_shapes_match_reference_golden():
+    """Config 2 at its own shapes (512 rows of QKV 2048->2560, O 2048->2048,
+    gate+up 2048->11264, down 5632->2048): the tcgen05 GEMM's outputs hash to
+    the values the reference's own matmul_vec produced row by row
+    (tests/golden/gemm_cfg2.json, made by make_golden.py --cfg2)."""
+    import torch
+    for g in json.load(open(os.path.join(GOLD, "gemm_cfg2.json"))):
+        K, N, rows = g["K"], g["N"], g["rows"]
+        w = iq.synth_weights(2, g["weight"], (N, K))
+        X = iq.synth_acts(2, g["act"], (rows, K))
+        pk = iq.PackedTC(dev(w), N, K)
+        do = torch.zeros((rows, N), dtype=torch.int64, device="cuda")
+        iq.gemm_tc_dev(do, pk, dev(X), rows)
+        got = host(do)
+        assert iq.device_status() == 0
+        assert [orc.fnv_hash(got[r]) for r in range(0, rows, 64)] == g["row_hashes"], g["tag"]
+        assert orc.fnv_hash(got) == g["out_hash"], g["tag"]
+        pk.free()
+
+
+# ---------------------------------------------------------- bounded waits
+
+def test_bounded_wait_gives_up_and_reports_timeout():
+    """A wait on an mbarrier that nothing arrives at gives up after its limit
+    (1 ms here), records IQ_ERR_TIMEOUT, and the host reads it once: the next
+    read is IQ_OK again, and the context stays usable."""
+    assert iq.device_status() == 0
+    assert iq.lib().iq_wait_selftest(1000000) == 0
+    assert iq.device_status() == -5   # IQ_ERR_TIMEOUT
+    assert iq.device_status() == 0
+    test_matvec_dev_edges(3, 17, "full")   # a later launch still runs correctly
+
+
+# ------------------------------------------- drop-in cache: changed host weights
+
+def test_dropin_detects_new_matrix_at_the_same_address():
+    """The reference's streaming path frees each layer after use and the next
+    layer can land at the same address (llama_int.c:2840-2872). Overwriting the
+    host matrix in place must never return the previous matrix's results: the
+    default sampled fingerprint and the full hash both catch it."""
+    rng = np.random.default_rng(21)
+    M, N = 300, 2048
+    buf = np.empty((M, N), np.int64)
+    x = orc.synth_acts(1, "x:stale", (N,))
+    try:
+        for mode in ("sampled", "full", "none"):
+            iq.weight_check_mode(mode)
+            iq.weight_cache_clear()
+            for layer in range(3):
+                buf[:] = orc.synth_weights(1, f"w:stale{layer}", (M, N))
+                out = np.empty(M, np.int64)
+                iq.matmul_vec(out, buf, x, M, N)
+                if mode != "none" or layer == 0:
+                    assert (out == orc.matmul_vec(buf, x)).all(), (mode, layer)
+            # one changed value in a sampled position (the first) is seen too
+            if mode != "none":
+                buf[0, 0] += 1 << 40
+                out = np.empty(M, np.int64)
+                iq.matmul_vec(out, buf, x, M, N)
+                assert (out == orc.matmul_vec(buf, x)).all(), mode
+    finally:
+        iq.weight_check_mode("sampled")
+        iq.weight_cache_clear()
+
+
+def test_dropin_full_mode_finds_reloaded_layers_by_content():
+    """Full-hash mode: a layer re-read into a fresh buffer (another address)
+    reuses its packed copy; results stay exact; the LRU byte limit evicts."""
+    M, N = 256, 1024
+    x = orc.synth_acts(1, "x:reload", (N,))
+    mats = [orc.synth_weights(1, f"w:reload{i}", (M, N)) for i in range(3)]
+    try:
+        iq.weight_check_mode("full")
+        iq.weight_cache_clear()
+        for token in range(3):
+            for i, w in enumerate(mats):
+                fresh = w.copy()           # new buffer each time, like the streaming loader
+                out = np.empty(M, np.int64)
+                iq.matmul_vec(out, fresh, x, M, N)
+                assert (out == orc.matmul_vec(w, x)).all(), (token, i)
+                del fresh
+        entries, nbytes = iq.weight_cache_stats()
+        assert entries == 3 and nbytes > 0
+        iq.weight_cache_limit(nbytes // 3 + 1)   # room for one entry
+        assert iq.weight_cache_stats()[0] == 1
+        out = np.empty(M, np.int64)
+        iq.matmul_vec(out, mats[0].copy(), x, M, N)
+        assert (out == orc.matmul_vec(mats[0], x)).all()
+    finally:
+        iq.weight_cache_limit(64 << 30)
+        iq.weight_check_mode("sampled")
+        iq.weight_cache_clear()

@@ -140,3 +140,78 @@ def test_long_prompt_chunked_prefill_matches_sequential_oracle():
     t3, _ = m.generate(pr, 12)
     assert t1 == t2 == t3 and h1 == h2
     m.close(); o.close()
+
+
+def _load_model(g, max_batch=1):
+    c = g["config"]
+    w = helpers.model_weights(g["cfg_index"], c)
+    m = iq.Model(c, max_batch=max_batch)
+    m.load(w)
+    return c, w, m
+
+
+def test_geom7b_hd128_mha_matches_reference_golden():
+    """Llama-2-7B geometry at reduced width (head_dim 128, n_kv = n_heads, FFN
+    ratio 11008/4096): a 370-token prompt and 29 decode steps that cross from the
+    single-kernel attention (context <= 384) to the phased kernels. Tokens and
+    the hash of every logit of all 399 forwards equal the reference's."""
+    g = gold("geom7b_model.json")
+    c, w, m = _load_model(g)
+    prompt = orc.synth_tokens(g["cfg_index"], g["prompt_name"], g["prompt_len"], c["vocab"])
+    for short_max in (384, 0):   # default switch-over, then phased attention only
+        m.set_attention(short_max)
+        toks, lh = m.generate(prompt, g["max_new"], logit_hash=True)
+        assert toks[g["prompt_len"]:] == g["tokens"], short_max
+        assert lh == g["logit_hash"], short_max
+        toks2, _ = m.generate(prompt, g["max_new"])   # graph path, no per-step sync
+        assert toks2[g["prompt_len"]:] == g["tokens"], short_max
+    m.close()
+
+
+def test_eos_stops_generation_like_the_reference():
+    """A model whose LM-head row 2 ties the row of a token greedy decoding emits
+    mid-generation: the first-max rule then samples EOS (2) and generate() stops
+    (llama_int.c:3110). Tokens, the returned length and the logit hash (which
+    covers the forward that sampled EOS) equal the reference's; the batched path
+    stops each sequence the same way."""
+    g = gold("eos_model.json")
+    c = g["config"]
+    w = helpers.model_weights(g["cfg_index"], c)
+    w["lm_head"][2] = w["lm_head"][g["lm_head_row2_from"]]
+    m = iq.Model(c)
+    m.load(w)
+    toks, lh = m.generate(np.array(g["prompt"]), g["max_new"], logit_hash=True)
+    assert toks == g["tokens"] and len(toks) == g["n_out"] < len(g["prompt"]) + g["max_new"]
+    assert lh == g["logit_hash"]
+    toks2, _ = m.generate(np.array(g["prompt"]), g["max_new"])
+    assert toks2 == g["tokens"]
+    m.close()
+    mb = iq.Model(c, max_batch=3)
+    mb.load(w)
+    other = orc.synth_tokens(g["cfg_index"], "prompt:other", 8, c["vocab"])
+    prompts = np.stack([np.array(g["prompt"]), other, np.array(g["prompt"])])
+    got, hs = mb.generate_batch(prompts, g["max_new"], logit_hash=True)
+    assert got[0] == got[2] == g["tokens"] and hs[0] == hs[2] == g["logit_hash"]
+    o = helpers.OracleModel(c, w)
+    want1, lh1 = o.generate(other, g["max_new"])
+    assert got[1] == want1 and hs[1] == lh1
+    o.close()
+    mb.close()
+
+
+def test_cfg3_geometry_batched_decode_matches_reference_golden():
+    """Config-3 geometry (TinyLlama width, GQA 8:1, 2 layers, max_seq 2176):
+    8 sequences with 2080-token prompts prefilled, then 23 batched decode steps
+    at context 2081..2103. Every sequence's tokens and every-logit hash equal
+    the reference's generate() run on that sequence alone."""
+    g = gold("cfg3_model.json")
+    c, w, m = _load_model(g, max_batch=g["batch"])
+    prompts = np.stack([orc.synth_tokens(g["cfg_index"], n, g["prompt_len"], c["vocab"])
+                        for n in g["prompt_names"]])
+    got, hs = m.generate_batch(prompts, g["max_new"], logit_hash=True)
+    for b in range(g["batch"]):
+        assert got[b][g["prompt_len"]:] == g["tokens"][b], b
+        assert hs[b] == g["logit_hashes"][b], b
+    got2 = m.generate_batch(prompts, g["max_new"])
+    assert [t[g["prompt_len"]:] for t in got2] == g["tokens"]
+    m.close()

@@ -18,14 +18,19 @@ pytestmark = pytest.mark.gpu
 
 
 def _run(name, out, pk, x):
-    import torch
+    # iq._sp(None) names torch's current stream (cudaStreamLegacy for torch's
+    # default stream, whose handle 0 the library would read as its own stream),
+    # so both calls are ordered after the torch fills of `out` below
     L = iq.lib()
-    rc = getattr(L, name)(ctypes.c_void_p(out.data_ptr()), pk.h, ctypes.c_void_p(x.data_ptr()),
-                          ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    rc = getattr(L, name)(ctypes.c_void_p(out.data_ptr()), pk.h, ctypes.c_void_p(x.data_ptr()), iq._sp(None))
     assert rc == 0, (name, rc)
 
 
-@pytest.mark.parametrize("M,N", [(2048, 2048), (33, 5000), (32000, 2048)])
+# (2048, 2048) and (33, 5000) run the row-owned kernel, which needs no scratch;
+# (32000, 2048) runs the stream-K kernel with staged x digits and (4096, 16384)
+# the stream-K kernel without them (K beyond the staging limit), both of which
+# split rows between warps through the fixed array.
+@pytest.mark.parametrize("M,N", [(2048, 2048), (33, 5000), (32000, 2048), (4096, 16384)])
 def test_noalloc_matches_regular_entry_point_twice(M, N):
     """Two calls in a row through the C ABI: each equals iq_matvec_packed_dev's
     output exactly (the tests' tolerance for integer work is zero)."""
@@ -55,6 +60,6 @@ def test_noalloc_rejects_more_rows_than_its_fixed_scratch():
     out = torch.zeros(M, dtype=torch.int64, device="cuda")
     L = iq.lib()
     rc = L.iq_matvec_packed_noalloc_dev(ctypes.c_void_p(out.data_ptr()), pk.h,
-                                        ctypes.c_void_p(x.data_ptr()), None)
+                                        ctypes.c_void_p(x.data_ptr()), iq._sp(None))
     assert rc == -6  # IQ_ERR_RANGE
     pk.free()
