@@ -161,6 +161,11 @@ IQ_API int iq_device_status(void);
  * (<= 100 ms). Returns IQ_OK when the wait gave up as designed; the status it
  * recorded (IQ_ERR_TIMEOUT) is then read and cleared by iq_device_status. */
 IQ_API int iq_wait_selftest(int64_t limit_ns);
+/* Measured ceiling for the GEMM roofline (no reference counterpart): one CTA
+ * per SM issues iters x 4 tcgen05.mma.kind::i8 (M=128, N=256, K=32) on
+ * shared-memory operands only; *tops = int8 tera-ops/s (2 per MAC), *ms the
+ * kernel's CUDA-event time. */
+IQ_API int iq_bench_i8_peak(int iters, double *tops, float *ms);
 
 /* Batched rows: d_out[r][i] = matmul_vec(d_w, d_X[r])[i] for r < rows, i.e.
  * exactly `rows` independent calls of llama_int.c:1014 (the reference has no

@@ -13,6 +13,7 @@
 #include "iq_planes.cuh"
 #include "iq_tc_gemm.cuh"
 #include "iq_elem.cuh"
+#include "iq_peak.cuh"
 
 namespace iq {
 
@@ -1044,6 +1045,39 @@ IQ_API int iq_device_status(void) {
     if ((rc = cur_device(&dev))) return rc;
     IQ_CUDA(cudaDeviceSynchronize());
     return take_dev_error();
+}
+
+IQ_API int iq_bench_i8_peak(int iters, double *tops, float *ms) {
+    if (iters < 4 || iters > (1 << 24) || !tops || !ms) return IQ_ERR_ARG;
+    int dev, rc;
+    if ((rc = cur_device(&dev))) return rc;
+    const int smem = 49152 + 1024 + 64;
+    IQ_CUDA(cudaFuncSetAttribute(k_i8_peak, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    int *d = nullptr, h = 0;
+    IQ_CUDA(cudaMalloc(&d, sizeof(int)));
+    cudaStream_t s = lib_stream();
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    const int grid = dev_info().sms;
+    cudaMemsetAsync(d, 0, sizeof(int), s);
+    k_i8_peak<<<grid, 128, smem, s>>>(iters / 4, d);   // warm-up
+    cudaEventRecord(e0, s);
+    k_i8_peak<<<grid, 128, smem, s>>>(iters, d);
+    cudaEventRecord(e1, s);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&h, d, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    float t = 0;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&t, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaFree(d);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (h != 2 * grid) return take_dev_error() ? IQ_ERR_TIMEOUT : IQ_ERR_STATE;
+    *ms = t;
+    *tops = 2.0 * 128 * 256 * 32 * 4.0 * iters * grid / (t * 1e-3) / 1e12;
+    return IQ_OK;
 }
 
 IQ_API int iq_wait_selftest(int64_t limit_ns) {

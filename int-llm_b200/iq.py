@@ -53,6 +53,7 @@ SIGNATURES = {
     "iq_gemm_tc_dev": (_I, [_P, _P, _P, _I, _P]),
     "iq_device_status": (_I, []),
     "iq_wait_selftest": (_I, [_I64]),
+    "iq_bench_i8_peak": (_I, [_I, _P, _P]),
     "iq_fp_dev": (_I, [_I, _P, _P, _P, _I64, _P]),
     "iq_rmsnorm_dev": (_I, [_P, _P, _P, _I, _I, _P]),
     "iq_softmax_dev": (_I, [_P, _I, _I, _P]),
@@ -290,6 +291,13 @@ def gemm_tc_dev(out, packed, X, rows, stream=None):
 def device_status():
     """IQ_OK, or the timeout status a kernel's bounded wait recorded (then cleared)."""
     return lib().iq_device_status()
+
+
+def bench_i8_peak(iters=20000):
+    """(int8 TOP/s, ms) of the tcgen05 kind::i8 peak kernel on the current device."""
+    t, ms = ctypes.c_double(), ctypes.c_float()
+    _call("iq_bench_i8_peak", iters, ctypes.byref(t), ctypes.byref(ms))
+    return t.value, ms.value
 
 
 def gemm_dev(out, w, X, rows, M, N, stream=None):
