@@ -3,6 +3,14 @@ import sys
 
 import pytest
 
+# torch first: libiq.so links libnccl.so.2, and whichever NCCL is loaded first is
+# the one the process keeps; torch's CUDA library needs the NCCL it ships with,
+# so it must load before anything pulls in libiq.so (e.g. the drop-in shim build)
+try:
+    import torch  # noqa: F401
+except Exception:
+    pass
+
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 for sub in ("oracle", "int-llm_b200", "tests"):
     p = os.path.join(ROOT, sub)

@@ -447,8 +447,8 @@ def test_dropin_full_mode_finds_reloaded_layers_by_content():
                 del fresh
         entries, nbytes = iq.weight_cache_stats()
         assert entries == 3 and nbytes > 0
-        iq.weight_cache_limit(nbytes // 3 + 1)   # room for one entry
-        assert iq.weight_cache_stats()[0] == 1
+        iq.weight_cache_limit(nbytes - 1)   # one byte short: the least recently used goes
+        assert iq.weight_cache_stats()[0] == 2
         out = np.empty(M, np.int64)
         iq.matmul_vec(out, mats[0].copy(), x, M, N)
         assert (out == orc.matmul_vec(mats[0], x)).all()

@@ -14,7 +14,8 @@ import helpers
 import iq
 import oracle as orc
 
-needs_ref = pytest.mark.skipif(orc.ref() is None, reason="oracle/_ref not built")
+needs_ref = pytest.mark.skipif(not os.path.exists(orc.REF_SO), reason="oracle/_ref not built")
+needs_shim = pytest.mark.skipif(not os.path.exists(orc.REF_IQ_SO), reason="oracle/_ref/libllamaref_iq.so not built")
 
 
 def _ref_generate(L, path, streaming, prompt, max_new):
@@ -103,7 +104,7 @@ def test_model_load_mgw_matches_reference(tiny_mgw):
 
 
 @pytest.mark.gpu
-@pytest.mark.skipif(orc.ref(shim=True) is None, reason="oracle/_ref/libllamaref_iq.so not built")
+@needs_shim
 def test_dropin_shim_in_reference_generate_cached_and_streaming(tiny_mgw):
     """The reference's own generate() with every matmul_vec call served by
     iq_matmul_vec: the mmap'd (layers cached) path and the streaming path, which
