@@ -120,6 +120,20 @@ IQ_API int iq_packed_free(iq_packed *p);
  * the number of residual entries (weights with nonzero bytes below p0). */
 IQ_API int iq_packed_info(const iq_packed *p, int *np, int *p0, int *residual_entries);
 IQ_API int iq_matvec_packed_dev(int64_t *d_out, const iq_packed *w, const int64_t *d_in, void *stream);
+/* Which stored form packing chose: IQ_FMT_PLANES (the byte-plane window
+ * above) or IQ_FMT_BF16, two bytes per weight for matrices whose weights are
+ * bf16 values (bfloat16_to_q1648, safetensors.h:115-152) of magnitude below
+ * 0.25: each weight is kept as the bf16 number w / 2^48 and converted to its
+ * byte planes inside the kernel, weights outside that form (at most 1 in
+ * 1024) going whole to the exact sparse residual; chosen when it is smaller
+ * and N <= 12768. Results are bit-identical either way. IQ_MV_FORMAT=planes
+ * in the environment disables it. */
+enum { IQ_FMT_PLANES = 0, IQ_FMT_BF16 = 1 };
+IQ_API int iq_packed_format(const iq_packed *p, int *fmt);
+/* iq_pack_weights_dev with the form given: -1 = chosen as above,
+ * IQ_FMT_PLANES, or IQ_FMT_BF16 for any weights (those it cannot hold all go
+ * to the residual; IQ_ERR_UNSUPPORTED when N > 12768). */
+IQ_API int iq_pack_weights_fmt_dev(const int64_t *d_w, int M, int N, int fmt, void *stream, iq_packed **out);
 /* Bytes of the stored form one iq_matvec_packed_dev launch reads (planes, row
  * sums, residual; not x or out): the numerator of its HBM roofline. */
 IQ_API int iq_packed_bytes(const iq_packed *p, int64_t *bytes);

@@ -203,7 +203,30 @@ static int build_residual(const int64_t *d_w, int M, int N, int rows_pad, int nn
     return IQ_OK;
 }
 
-static int pack_weights(const int64_t *d_w, int M, int N, cudaStream_t s, Packed *P) {
+// Weights the bf16 form cannot hold (its residual entries). Synchronises s.
+static int bf_residual_count(const int64_t *d_w, int64_t n, cudaStream_t s, unsigned long long *cnt) {
+    unsigned long long *d = nullptr;
+    IQ_CUDA(cudaMalloc(&d, sizeof(unsigned long long)));
+    cudaError_t e = cudaMemsetAsync(d, 0, sizeof(unsigned long long), s);
+    if (e == cudaSuccess) {
+        k_bf_count<<<(int)std::min<int64_t>((n + 255) / 256, (int64_t)dev_info().sms * 16), 256, 0, s>>>(d, d_w, n);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(cnt, d, sizeof(unsigned long long), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    cudaFree(d);
+    if (e != cudaSuccess) return cuda_fail(e);
+    return IQ_OK;
+}
+
+// The matvec form: the bf16 form (2 bytes per weight) when it holds all but
+// at most one weight in 1024 exactly, the activations can be staged
+// (Kp <= 12784) and it is smaller than the plane window; else the window.
+// IQ_MV_FORMAT=planes|bf16 forces one (bf16 only where it applies).
+// want: -1 = choose, IQ_FMT_PLANES or IQ_FMT_BF16 = that form (bf16: any
+// weights, however many residual entries; IQ_ERR_UNSUPPORTED when N is too
+// long to stage the activations).
+static int pack_weights(const int64_t *d_w, int M, int N, cudaStream_t s, Packed *P, int want = -1) {
     P->M = M; P->N = N;
     P->Mp = (M + 15) / 16 * 16;
     P->Kp = (N + 31) / 32 * 32;
@@ -215,6 +238,48 @@ static int pack_weights(const int64_t *d_w, int M, int N, cudaStream_t s, Packed
     P->np = top - P->p0;
     P->nnz = 0;
     for (int b = 0; b < P->p0; b++) P->nnz += (int)low[b];
+    P->fmt = IQ_FMT_PLANES;
+    static const char *force_env = getenv("IQ_MV_FORMAT");
+    const char *force = want == IQ_FMT_PLANES ? "planes" : want == IQ_FMT_BF16 ? "bf16" : force_env;
+    const bool allow_bf = !(force && !strcmp(force, "planes"));
+    const bool fits = 8 * ((int64_t)P->Kp + 16) <= 100 * 1024;
+    if (want == IQ_FMT_BF16 && !fits) return IQ_ERR_UNSUPPORTED;
+    if (allow_bf && fits) {
+        unsigned long long nbf = 0;
+        if ((rc = bf_residual_count(d_w, (int64_t)M * N, s, &nbf))) return rc;
+        const int64_t cells = (int64_t)P->Mp * P->Kp;
+        const bool sparse = (long double)nbf * 1024.0L <= (long double)cells;
+        const long double bytes_bf = 2.0L * cells + 16.0L * nbf, bytes_pl = (long double)P->np * cells + 16.0L * P->nnz;
+        if (want == IQ_FMT_BF16 || (sparse && (bytes_bf < bytes_pl || (force && !strcmp(force, "bf16"))))) {
+            P->fmt = IQ_FMT_BF16;
+            P->np = 3;
+            P->p0 = 3;
+            P->nnz = (int)nbf;
+        }
+    }
+    if (P->fmt == IQ_FMT_BF16) {
+        cudaError_t e = cudaMalloc(&P->planes, (size_t)P->Mp * P->Kp * 2);
+        if (e == cudaSuccess) e = cudaMalloc(&P->rowsum, (size_t)P->Mp * 16);
+        if (e == cudaSuccess && P->nnz > 0) {
+            e = cudaMalloc(&P->res_ptr, (size_t)(P->Mp + 1) * sizeof(int));
+            if (e == cudaSuccess) e = cudaMalloc(&P->res_col, (size_t)P->nnz * sizeof(int));
+            if (e == cudaSuccess) e = cudaMalloc(&P->res_val, (size_t)P->nnz * sizeof(int64_t));
+        }
+        if (e != cudaSuccess) { free_packed(P); return cuda_fail(e); }
+        const int KT = P->Kp / 32;
+        const int64_t total = (int64_t)(P->Mp / 16) * KT * 32;
+        k_pack_bf<<<(int)std::min<int64_t>((total + 255) / 256, (int64_t)dev_info().sms * 32), 256, 0, s>>>(
+            P->planes, d_w, M, N, KT, total);
+        IQ_CHECK_LAUNCH();
+        k_bf_row_sums<<<std::min(P->Mp / 8 + 1, dev_info().sms * 16), 256, 0, s>>>(P->rowsum, d_w, M, N, P->Mp);
+        IQ_CHECK_LAUNCH();
+        if (P->nnz > 0 && (rc = build_residual(d_w, M, N, P->Mp, P->nnz, 0ull, s, P->res_ptr, P->res_col,
+                                                P->res_val))) {
+            free_packed(P);
+            return rc;
+        }
+        return IQ_OK;
+    }
     const uint64_t mask = P->p0 ? (~0ull >> (64 - 8 * P->p0)) : 0ull;
     size_t nbytes = (size_t)P->Mp * P->Kp * P->np;
     cudaError_t e = cudaMalloc(&P->planes, nbytes);
@@ -241,7 +306,7 @@ static int pack_weights(const int64_t *d_w, int M, int N, cudaStream_t s, Packed
 }
 
 static PackedRes packed_res(const Packed &P) {
-    return PackedRes{P.p0, P.rowsum, P.res_ptr, P.res_col, P.res_val};
+    return PackedRes{P.p0, P.fmt == IQ_FMT_BF16 ? 1 : 0, P.rowsum, P.res_ptr, P.res_col, P.res_val};
 }
 
 static void free_packed(Packed *P) {
@@ -280,12 +345,12 @@ typedef void (*RowsKernel)(int64_t *, const uint4 *, const PackedRes, const int6
 // Once per device and plane count: allow the largest staged-digit buffer
 // (the 48 KB default covers static + dynamic shared memory together) and
 // record the occupancy at that size.
-template <int NP>
+template <int NP, bool BF = false>
 static int rows_setup(RowsKernel *k, int *occ) {
     static int occs[64] = {0};
     int dev = 0;
     IQ_CUDA(cudaGetDevice(&dev));
-    *k = k_matvec_rows<NP>;
+    *k = k_matvec_rows<NP, BF>;
     if (dev >= 0 && dev < 64 && occs[dev]) { *occ = occs[dev]; return IQ_OK; }
     const int smax = 100 * 1024;
     IQ_CUDA(cudaFuncSetAttribute(*k, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
@@ -308,7 +373,8 @@ int launch_matvec_rows(int64_t *out, const Packed &P, const int64_t *x, cudaStre
     if (mode == 0) return IQ_ERR_UNSUPPORTED;
     RowsKernel kern = nullptr;
     int occ = 0, rc = IQ_OK;
-    switch (P.np) {
+    switch (P.fmt == IQ_FMT_BF16 ? 0 : P.np) {
+    case 0: rc = rows_setup<3, true>(&kern, &occ); break;
     case 1: rc = rows_setup<1>(&kern, &occ); break;
     case 2: rc = rows_setup<2>(&kern, &occ); break;
     case 3: rc = rows_setup<3>(&kern, &occ); break;
@@ -359,7 +425,9 @@ int launch_matvec_planes(int64_t *out, const Packed &P, const int64_t *x, cudaSt
         int rc = launch_matvec_rows(out, P, x, s, add, nrm_w, smem);
         if (rc != IQ_ERR_UNSUPPORTED) return rc;
     }
-    PlanesKernel kern = xs ? planes_kernel<true>(P.np) : planes_kernel<false>(P.np);
+    if (P.fmt == IQ_FMT_BF16 && !xs) return IQ_ERR_STATE;  // packing guarantees staged activations
+    PlanesKernel kern = P.fmt == IQ_FMT_BF16 ? k_matvec_planes<3, true, true>
+                        : xs ? planes_kernel<true>(P.np) : planes_kernel<false>(P.np);
     if (!xs) smem = 0;
     // static shared memory counts against the 48 KB default too
     if (smem > 40 * 1024) IQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -477,7 +545,7 @@ static void free_packed_tc(PackedTC *P) {
 }
 
 static PackedRes packed_res(const PackedTC &P) {
-    return PackedRes{P.p0, P.rowsum, P.res_ptr, P.res_col, P.res_val};
+    return PackedRes{P.p0, 0, P.rowsum, P.res_ptr, P.res_col, P.res_val};
 }
 
 static int pack_weights_tc(const int64_t *d_w, int M, int K, cudaStream_t s, PackedTC *P) {
@@ -950,16 +1018,20 @@ const Packed *iq_packed_inner(const iq_packed *w, int *dev) {
     return &w->P;
 }
 
-IQ_API int iq_pack_weights_dev(const int64_t *d_w, int M, int N, void *stream, iq_packed **out) {
-    if (!d_w || !out || M <= 0 || N <= 0) return IQ_ERR_ARG;
+IQ_API int iq_pack_weights_fmt_dev(const int64_t *d_w, int M, int N, int fmt, void *stream, iq_packed **out) {
+    if (!d_w || !out || M <= 0 || N <= 0 || fmt < -1 || fmt > IQ_FMT_BF16) return IQ_ERR_ARG;
     *out = nullptr;
     int dev, rc;
     if ((rc = cur_device(&dev))) return rc;
     iq_packed *p = new iq_packed();
     p->dev = dev;
-    if ((rc = pack_weights(d_w, M, N, pick(stream), &p->P))) { delete p; return rc; }
+    if ((rc = pack_weights(d_w, M, N, pick(stream), &p->P, fmt))) { delete p; return rc; }
     *out = p;
     return IQ_OK;
+}
+
+IQ_API int iq_pack_weights_dev(const int64_t *d_w, int M, int N, void *stream, iq_packed **out) {
+    return iq_pack_weights_fmt_dev(d_w, M, N, -1, stream, out);
 }
 
 IQ_API int iq_packed_free(iq_packed *p) {
@@ -975,6 +1047,12 @@ IQ_API int iq_packed_info(const iq_packed *p, int *np, int *p0, int *residual_en
     *np = p->P.np;
     *p0 = p->P.p0;
     *residual_entries = p->P.nnz;
+    return IQ_OK;
+}
+
+IQ_API int iq_packed_format(const iq_packed *p, int *fmt) {
+    if (!p || !fmt) return IQ_ERR_ARG;
+    *fmt = p->P.fmt;
     return IQ_OK;
 }
 

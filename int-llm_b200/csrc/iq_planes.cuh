@@ -31,6 +31,24 @@
 // 4(l%4)..+3 and 16+4(l%4)..+3), so one 16-byte load per plane per lane
 // streams the tile. Rows are padded to 16 and columns to 32 with zeros.
 //
+// bf16 form (fmt IQ_FMT_BF16, 2 bytes per weight). Weights that came from
+// bf16 (bfloat16_to_q1648, safetensors.h:115-152) are +-m 2^e with an 8-bit
+// m; when w is a multiple of 2^24 and v = w / 2^24 lies in [-2^22, 2^22) with
+// at most 8 significant bits, the bf16 number v 2^-24 holds w exactly and is
+// stored as is (the config weights: all but ~0.03%). The kernel recovers
+//   u = v + 2^22 = low 23 bits of fma.rm(f, 2^24, 1.5 * 2^23)
+// exactly (f = the bf16 value as fp32; the sum lies in [2^23, 2^24), where fp32
+// steps by 1, and rounding toward -inf of an exact integer changes nothing),
+// splits u into three unsigned byte planes in registers and runs the same
+// MMAs. Then, with U = sum_k u_k (a per-row constant) and X = sum_k x_k (per
+// launch, from the staged activations),
+//   sum_k x_k w_k = 2^24 (sum_{i,j} 2^{8(i+j)} P_ij - 2^63 U - 2^22 X) + residual
+// where every other weight (not of that form) is stored as 0 (v = 0) and its
+// whole value goes to the sparse residual, and padding columns are stored as
+// -0.25 (u = 0), so they add nothing. Layout: per 16x32 tile, 32 lanes x 2 x
+// 16 bytes: lane l's 16 weights (its A fragment, register r = 4 consecutive k)
+// as bf16 pairs, words [r0 k0k1, r0 k2k3, r1 k0k1, r1 k2k3] then r2, r3.
+//
 // The x digits D_j form the MMA's B operand (N = 8 = one column per digit),
 // staged once per CTA in shared memory as 8 byte-rows of Kp (+16 pad).
 // Work split: stream-K over (row tile, column tile) units, equal slices per
@@ -42,14 +60,17 @@
 
 namespace iq {
 
+// Stored forms (iq.h): IQ_FMT_PLANES = byte-plane window (np planes from p0),
+// IQ_FMT_BF16 = bf16 words converted in the kernel (3 planes, p0 = 3).
 struct Packed {
+    int fmt = IQ_FMT_PLANES;
     int M = 0, N = 0;       // logical shape: M rows of N columns
     int Mp = 0, Kp = 0;     // padded to 16 rows / 32 columns
     int np = 8;             // byte planes stored (top plane signed)
     int p0 = 0;             // lowest stored plane
     int nnz = 0;            // weights with nonzero bytes below p0 (residual entries)
     uint4 *planes = nullptr;
-    int64_t *rowsum = nullptr;  // [Mp][2] = 128-bit sum_k w_hi[row][k] (lo, hi)
+    int64_t *rowsum = nullptr;  // [Mp][2] = 128-bit sum_k w_hi[row][k] (lo, hi); bf16 form: sum_k u
     int *res_ptr = nullptr;     // [Mp + 1] CSR row offsets (nullptr when nnz == 0)
     int *res_col = nullptr;     // [nnz] column
     int64_t *res_val = nullptr; // [nnz] w_lo
@@ -58,7 +79,7 @@ struct Packed {
 // Bytes of the stored form one matvec launch reads: planes, 128-bit row sums
 // and the residual CSR (x and out not counted).
 inline int64_t packed_bytes(const Packed &P) {
-    int64_t b = (int64_t)P.np * P.Mp * P.Kp + 16 * (int64_t)P.Mp;
+    int64_t b = (int64_t)(P.fmt == IQ_FMT_BF16 ? 2 : P.np) * P.Mp * P.Kp + 16 * (int64_t)P.Mp;
     if (P.nnz) b += 4 * ((int64_t)P.Mp + 1) + 12 * (int64_t)P.nnz;
     return b;
 }
@@ -66,6 +87,7 @@ inline int64_t packed_bytes(const Packed &P) {
 // What a kernel needs of a Packed beyond the planes (passed by value).
 struct PackedRes {
     int p0;
+    int bf;  // bf16 form: subtract 2^22 sum_k x_k too
     const int64_t *rowsum;
     const int *ptr, *col;
     const int64_t *val;
@@ -117,12 +139,33 @@ __global__ void k_plane_count(unsigned long long *__restrict__ st, const int64_t
 }
 
 // Residual entries per row (weights with nonzero bytes below p0), one warp per row.
+// The bf16 bits that hold w exactly in the bf16 form (w = v 2^24, v in
+// [-2^22, 2^22) with at most 8 significant bits; v = 0 -> +0.0), else -1.
+__host__ __device__ __forceinline__ int bf_encode(int64_t w) {
+    if (w & 0xFFFFFF) return -1;
+    const int64_t v = w >> 24;
+    if (v < -(1 << 22) || v >= (1 << 22)) return -1;
+    if (v == 0) return 0;
+    const uint32_t a = (uint32_t)(v < 0 ? -v : v);
+    int e2 = 31, tz = 0;
+    while (!((a >> e2) & 1u)) e2--;
+    while (!((a >> tz) & 1u)) tz++;
+    if (e2 - tz >= 8) return -1;
+    return (v < 0 ? 0x8000 : 0) | ((e2 + 103) << 7) | (int)(((a << 7) >> e2) & 0x7F);
+}
+// v of the bf16 form (0 where the weight is left to the residual)
+__host__ __device__ __forceinline__ int64_t bf_v(int64_t w) { return bf_encode(w) < 0 ? 0 : (w >> 24); }
+// Residual value of a weight: its bits in `mask` (plane window), or, with
+// mask == 0 (bf16 form), the whole weight where the bf16 form cannot hold it.
+__device__ __forceinline__ uint64_t res_value(int64_t w, uint64_t mask) {
+    return mask ? ((uint64_t)w & mask) : (bf_encode(w) < 0 ? (uint64_t)w : 0ull);
+}
 __global__ void k_res_count(int *__restrict__ cnt, const int64_t *__restrict__ W, int M, int N, uint64_t mask) {
     const int lane = threadIdx.x & 31;
     for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < M;
          row += gridDim.x * (blockDim.x >> 5)) {
         int c = 0;
-        for (int k = lane; k < N; k += 32) c += ((uint64_t)W[(size_t)row * N + k] & mask) != 0;
+        for (int k = lane; k < N; k += 32) c += res_value(W[(size_t)row * N + k], mask) != 0;
         for (int m = 16; m >= 1; m >>= 1) c += __shfl_xor_sync(0xffffffffu, c, m);
         if (lane == 0) cnt[row] = c;
     }
@@ -136,7 +179,7 @@ __global__ void k_res_fill(int *__restrict__ col, int64_t *__restrict__ val, con
         int o = ptr[row];
         for (int k0 = 0; k0 < N; k0 += 32) {
             const int k = k0 + lane;
-            const uint64_t lo = k < N ? (uint64_t)W[(size_t)row * N + k] & mask : 0;
+            const uint64_t lo = k < N ? res_value(W[(size_t)row * N + k], mask) : 0;
             const unsigned b = __ballot_sync(0xffffffffu, lo != 0);
             if (lo) {
                 const int at = o + __popc(b & ((1u << lane) - 1));
@@ -184,6 +227,87 @@ __global__ void k_pack_planes(uint4 *__restrict__ planes, const int64_t *__restr
             dst[p * 32] = make_uint4(v[0], v[1], v[2], v[3]);
         }
     }
+}
+
+// ------------------------------------------------------------- bf16 form
+
+#define IQ_BF_PAD 0xBE80u  // -0.25: u = 0
+
+// Weights the bf16 form cannot hold exactly (its residual entries).
+__global__ void k_bf_count(unsigned long long *__restrict__ cnt, const int64_t *__restrict__ W, int64_t n) {
+    unsigned long long c = 0;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x)
+        c += bf_encode(W[e]) < 0;
+    for (int m = 16; m >= 1; m >>= 1) c += __shfl_xor_sync(0xffffffffu, c, m);
+    if ((threadIdx.x & 31) == 0 && c) atomicAdd(cnt, c);
+}
+
+// One thread per (row tile, column tile, lane): the lane's 16 weights as bf16.
+__global__ void k_pack_bf(uint4 *__restrict__ words, const int64_t *__restrict__ W, int M, int N, int KT,
+                          int64_t total) {
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int lane = (int)(e & 31);
+        const int64_t tile = e >> 5;
+        const int rt = (int)(tile / KT), kt = (int)(tile % KT);
+        const int g = lane >> 2, t = lane & 3;
+        uint32_t v[8];
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            const int row = rt * 16 + g + ((r & 1) ? 8 : 0);
+            const int col0 = kt * 32 + 4 * t + ((r & 2) ? 16 : 0);
+            uint32_t b[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int col = col0 + j;
+                if (row < M && col < N) {
+                    const int enc = bf_encode(W[(size_t)row * N + col]);
+                    b[j] = enc < 0 ? 0u : (uint32_t)enc;
+                } else {
+                    b[j] = IQ_BF_PAD;
+                }
+            }
+            v[2 * r] = b[0] | (b[1] << 16);
+            v[2 * r + 1] = b[2] | (b[3] << 16);
+        }
+        uint4 *dst = words + (size_t)tile * 64 + lane;
+        dst[0] = make_uint4(v[0], v[1], v[2], v[3]);
+        dst[32] = make_uint4(v[4], v[5], v[6], v[7]);
+    }
+}
+
+// 128-bit sum_k u_k = sum_k (v_k + 2^22) over the real columns (one warp per row).
+__global__ void k_bf_row_sums(int64_t *__restrict__ rs, const int64_t *__restrict__ W, int M, int N, int Mp) {
+    const int lane = threadIdx.x & 31;
+    for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < Mp;
+         row += gridDim.x * (blockDim.x >> 5)) {
+        i128 s = 0;
+        if (row < M)
+            for (int k = lane; k < N; k += 32) s += (i128)(bf_v(W[(size_t)row * N + k]) + (1 << 22));
+        s = warp_sum_i128(s);
+        if (lane == 0) {
+            rs[2 * row] = (int64_t)(uint64_t)s;
+            rs[2 * row + 1] = (int64_t)(uint64_t)((u128)s >> 64);
+        }
+    }
+}
+
+// u of one bf16 weight held in the high half of f_bits: fp32 fma rounding
+// toward -inf, exact (see the bf16 form above); the low 3 bytes are u's.
+__device__ __forceinline__ uint32_t bf_u(uint32_t f_bits) {
+    float r;
+    asm("fma.rm.f32 %0, %1, 0f4B800000, 0f4B400000;" : "=f"(r) : "f"(__uint_as_float(f_bits)));
+    return __float_as_uint(r);
+}
+// Four weights (bf16 pairs w01, w23; byte i = column k + i) -> their u bytes,
+// one register per plane.
+__device__ __forceinline__ void bf_quad(uint32_t w01, uint32_t w23, uint32_t &p0, uint32_t &p1, uint32_t &p2) {
+    const uint32_t r0 = bf_u(w01 << 16), r1 = bf_u(w01 & 0xFFFF0000u);
+    const uint32_t r2 = bf_u(w23 << 16), r3 = bf_u(w23 & 0xFFFF0000u);
+    const uint32_t t01 = __byte_perm(r0, r1, 0x5140), t23 = __byte_perm(r2, r3, 0x5140);
+    p0 = __byte_perm(t01, t23, 0x5410);
+    p1 = __byte_perm(t01, t23, 0x7632);
+    p2 = __byte_perm(__byte_perm(r0, r1, 0x0062), __byte_perm(r2, r3, 0x0062), 0x5410);
 }
 
 // 128-bit row sums of W with the bits in lo_mask cleared (one warp per row).
@@ -300,8 +424,12 @@ __device__ __forceinline__ int64_t x_from_digits(const unsigned char *xd, int ld
     return (int64_t)(xu ^ 0x8000000000000000ull);
 }
 __device__ __forceinline__ int64_t finish_row(i128 acc, const RowPre &p, const PackedRes &R,
-                                              const unsigned char *xd, int ld, const int64_t *__restrict__ xg) {
-    u128 v = ((u128)acc << (8 * R.p0)) - ((u128)p.ws << 63);
+                                              const unsigned char *xd, int ld, const int64_t *__restrict__ xg,
+                                              i128 xs = 0) {
+    // plane window: ws = sum w_hi (unscaled); bf16 form: ws = sum u, in units of
+    // 2^24 like acc, and u = v + 2^22 also subtracts 2^22 sum x
+    u128 v = R.bf ? ((u128)acc - ((u128)p.ws << 63) - ((u128)xs << 22)) << (8 * R.p0)
+                  : ((u128)acc << (8 * R.p0)) - ((u128)p.ws << 63);
     for (int e = p.e0; e < p.e1; e++) {
         const int k = e == p.e0 ? p.col0 : R.col[e];
         const int64_t wl = e == p.e0 ? p.val0 : R.val[e];
@@ -310,8 +438,9 @@ __device__ __forceinline__ int64_t finish_row(i128 acc, const RowPre &p, const P
     return (int64_t)((i128)v >> 48);
 }
 __device__ __forceinline__ int64_t finish_row(i128 acc, int row, const PackedRes &R,
-                                              const unsigned char *xd, int ld, const int64_t *__restrict__ xg) {
-    return finish_row(acc, row_pre(row, R), R, xd, ld, xg);
+                                              const unsigned char *xd, int ld, const int64_t *__restrict__ xg,
+                                              i128 xs = 0) {
+    return finish_row(acc, row_pre(row, R), R, xd, ld, xg, xs);
 }
 
 // 4 digits j of x_u[k..k+3] packed into one word (byte i = element k+i)
@@ -330,10 +459,13 @@ __device__ __forceinline__ uint32_t digit_word(const int64_t *__restrict__ xg, i
 // Fused rmsnorm (llama_int.c:1048-1058) when nrm_w is given: the CTA computes
 // the inverse rms of x itself and stages the digits of
 // fp_mul(fp_mul(x, inv), w) instead of x.
+// With xsum (bf16 form), every thread also receives sum_k x_k of the staged
+// (normalised) values.
 __device__ __forceinline__ void stage_digits(unsigned char *xd, int ld, const int64_t *__restrict__ xg, int N, int Kp,
-                                             const int64_t *__restrict__ nrm_w) {
+                                             const int64_t *__restrict__ nrm_w, i128 *xsum = nullptr) {
     __shared__ uint64_t red[64];
     const int64_t inv = nrm_w ? cta_rms_inv(xg, N, red) : 0;
+    i128 xs = 0;
     // each thread: 4 consecutive x values -> 8 digit words (one per digit row)
     for (int k = 4 * threadIdx.x; k < Kp; k += 4 * blockDim.x) {
         uint64_t xu[4];
@@ -341,6 +473,7 @@ __device__ __forceinline__ void stage_digits(unsigned char *xd, int ld, const in
         for (int i = 0; i < 4; i++) {
             int64_t xv = k + i < N ? __ldg(xg + k + i) : 0;
             if (nrm_w && k + i < N) xv = d_mul(d_mul(xv, inv), __ldg(nrm_w + k + i));
+            xs += (i128)xv;
             xu[i] = (uint64_t)xv ^ 0x8000000000000000ull;
         }
 #pragma unroll
@@ -351,21 +484,29 @@ __device__ __forceinline__ void stage_digits(unsigned char *xd, int ld, const in
             *reinterpret_cast<uint32_t *>(xd + j * ld + k) = v;
         }
     }
+    if (xsum) *xsum = cta_sum_i128(xs, red);   // ends with a barrier-ordered read of red
     __syncthreads();
 }
 
 // Weight tiles in flight per warp: a register ring of D tiles, deeper when a
 // tile is smaller (fewer planes), so the bytes in flight stay about constant.
 // The ring is indexed statically (the unit loop is unrolled by D).
-template <int NP>
+// (bf16 form: 2 x 16 bytes per lane and tile, like a 2-plane window.)
+#ifndef IQ_BF_RING
+#define IQ_BF_RING 6
+#endif
+template <int NP, bool BF = false>
 __host__ __device__ constexpr int ring_depth() {
-    return NP <= 2 ? 6 : NP == 3 ? 4 : NP == 4 ? 3 : 2;
+    return BF ? IQ_BF_RING : NP <= 2 ? 6 : NP == 3 ? 4 : NP == 4 ? 3 : 2;
 }
+// 16-byte loads per lane and tile
+template <int NP, bool BF>
+__host__ __device__ constexpr int tile_loads() { return BF ? 2 : NP; }
 
-template <int NP>
-__device__ __forceinline__ void load_tile(uint4 (&dst)[NP], const uint4 *src) {
+template <int NL>
+__device__ __forceinline__ void load_tile(uint4 (&dst)[NL], const uint4 *src) {
 #pragma unroll
-    for (int p = 0; p < NP; p++) dst[p] = ld_stream_u4(src + p * 32);
+    for (int p = 0; p < NL; p++) dst[p] = ld_stream_u4(src + p * 32);
 }
 
 template <int NP>
@@ -374,6 +515,98 @@ __device__ __forceinline__ void mma_tile(int (&c)[NP][4], const uint4 (&a)[NP], 
     for (int p = 0; p < NP - 1; p++) mma_i8<false>(c[p], a[p], b0, b1);
     mma_i8<true>(c[NP - 1], a[NP - 1], b0, b1);  // top plane: signed
 }
+// bf16 form: the lane's 16 weights -> u's three unsigned planes -> 3 MMAs
+__device__ __forceinline__ void mma_tile_bf(int (&c)[3][4], const uint4 (&w)[2], uint32_t b0, uint32_t b1) {
+    uint4 a[3];
+    bf_quad(w[0].x, w[0].y, a[0].x, a[1].x, a[2].x);
+    bf_quad(w[0].z, w[0].w, a[0].y, a[1].y, a[2].y);
+    bf_quad(w[1].x, w[1].y, a[0].z, a[1].z, a[2].z);
+    bf_quad(w[1].z, w[1].w, a[0].w, a[1].w, a[2].w);
+#pragma unroll
+    for (int p = 0; p < 3; p++) mma_i8<false>(c[p], a[p], b0, b1);
+}
+template <int NP, bool BF, int NL>
+__device__ __forceinline__ void mma_any(int (&c)[NP][4], const uint4 (&a)[NL], uint32_t b0, uint32_t b1) {
+    if constexpr (BF) {
+        static_assert(NP == 3 && NL == 2, "bf16 form: 3 planes from 2 loads");
+        mma_tile_bf(c, a, b0, b1);
+    } else {
+        mma_tile<NP>(c, a, b0, b1);
+    }
+}
+
+// End of a warp's segment of row tile rt (column tiles k0 .. k1-1): the 4 lanes
+// of each row group sum their digits' partials, then the row's writer either
+// owns the whole row (k0 == 0, k1 == KT) or meets the other segments in the
+// RowAcc scratch, and the one completing the row writes it. Kept out of line:
+// inlined into every slot of the unrolled ring it multiplied the code size and
+// the kernel stalled on instruction fetch.
+__device__ __noinline__ void flush_segment(i128 r0, i128 r1, int rt, int k0, int k1, int KT, int M, int add,
+                                           int64_t *__restrict__ out, RowAcc *__restrict__ racc, const PackedRes R,
+                                           const unsigned char *xd, int ld, const int64_t *__restrict__ xg, i128 xs,
+                                           int g, int t) {
+    // the 4 lanes of a row group hold the 8 digits: reduce over t
+#pragma unroll
+    for (int m = 1; m <= 2; m <<= 1) {
+        r0 += shfl_xor_i128(r0, m);
+        r1 += shfl_xor_i128(r1, m);
+    }
+    if (t == 0 && add == IQ_EPI_SWIGLU) {
+        // rows g (gate) and g + 8 (up) complete together: one counter
+        const int row = rt * 16 + g;
+        i128 f0 = r0, f1 = r1;
+        bool write = k0 == 0 && k1 == KT;
+        if (!write) {
+            RowAcc *ra = racc + row, *rb = racc + row + 8;
+            atomic_add_i128(ra, r0);
+            atomic_add_i128(rb, r1);
+            cuda::atomic_ref<unsigned int, cuda::thread_scope_device> done(ra->done);
+            unsigned int prev = done.fetch_add((unsigned int)(k1 - k0), cuda::memory_order_acq_rel);
+            if (prev + (unsigned int)(k1 - k0) == (unsigned int)KT) {
+                unsigned long long alo = atomicExch(&ra->lo, 0ull), ahi = atomicExch(&ra->hi, 0ull);
+                unsigned long long blo = atomicExch(&rb->lo, 0ull), bhi = atomicExch(&rb->hi, 0ull);
+                atomicExch(&ra->done, 0u);
+                f0 = (i128)(((u128)ahi << 64) | alo);
+                f1 = (i128)(((u128)bhi << 64) | blo);
+                write = true;
+            }
+        }
+        if (write) {
+            const int64_t gate = finish_row(f0, row, R, xd, ld, xg, xs);
+            const int64_t up = finish_row(f1, row + 8, R, xd, ld, xg, xs);
+            out[rt * 8 + g] = d_mul(d_silu(gate), up);
+        }
+    } else if (t == 0) {
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int row = rt * 16 + g + 8 * h;
+            if (row >= M) continue;
+            i128 part = h ? r1 : r0;
+            i128 fin = 0;
+            bool write = false;
+            if (k0 == 0 && k1 == KT) { fin = part; write = true; }
+            else {
+                RowAcc *ra = racc + row;
+                atomic_add_i128(ra, part);
+                // release our partial / acquire everyone else's with the counter
+                cuda::atomic_ref<unsigned int, cuda::thread_scope_device> done(ra->done);
+                unsigned int prev = done.fetch_add((unsigned int)(k1 - k0), cuda::memory_order_acq_rel);
+                if (prev + (unsigned int)(k1 - k0) == (unsigned int)KT) {
+                    unsigned long long lo = atomicExch(&ra->lo, 0ull);
+                    unsigned long long hi = atomicExch(&ra->hi, 0ull);
+                    atomicExch(&ra->done, 0u);
+                    fin = (i128)(((u128)hi << 64) | lo);
+                    write = true;
+                }
+            }
+            if (write) {
+                int64_t val = finish_row(fin, row, R, xd, ld, xg, xs);
+                // add != 0: residual epilogue out += result (int64 wrap, llama_int.c:1535, 1556)
+                out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)val) : val;
+            }
+        }
+    }
+}
 
 // Stream-K kernel. XSMEM: digits staged in shared memory (Kp small enough),
 // else gathered from x in global memory (L1-cached) per column tile.
@@ -381,14 +614,16 @@ __device__ __forceinline__ void mma_tile(int (&c)[NP][4], const uint4 (&a)[NP], 
 // order) with ring_depth<NP>() tiles in flight; the first D-1 are requested
 // before griddepcontrol.wait (weights are static), overlapping the previous
 // kernel's tail and the digit staging.
-template <int NP, bool XSMEM>
+template <int NP, bool XSMEM, bool BF = false>
 __global__ void __launch_bounds__(256, 2)
 k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const PackedRes R,
                 const int64_t *__restrict__ xg, int M, int N, int Kp, int add, RowAcc *__restrict__ racc,
                 const int64_t *__restrict__ nrm_w) {
     extern __shared__ __align__(16) unsigned char xd[];  // [8][Kp + 16] digit rows
-    constexpr int D = ring_depth<NP>();
-    constexpr int TS = NP * 32;  // uint4 per packed tile
+    static_assert(!BF || XSMEM, "the bf16 form needs the staged activations (their sum)");
+    constexpr int D = ring_depth<NP, BF>();
+    constexpr int NL = tile_loads<NP, BF>();
+    constexpr int TS = NL * 32;  // uint4 per packed tile
     const int ld = Kp + 16;
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int KT = Kp / 32, RT = (M + 15) / 16;
@@ -400,13 +635,14 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
     // own prologue now; it waits (griddepcontrol.wait) for this grid's results.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const uint4 *pl = planes + lane;
-    uint4 buf[D][NP];
+    uint4 buf[D][NL];
 #pragma unroll
     for (int s = 0; s < D - 1; s++)
-        if (u0 + s < u1) load_tile<NP>(buf[s], pl + (size_t)(u0 + s) * TS);
+        if (u0 + s < u1) load_tile<NL>(buf[s], pl + (size_t)(u0 + s) * TS);
     // x and (with add) out are produced by the previous kernel
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (XSMEM) stage_digits(xd, ld, xg, N, Kp, nrm_w);
+    i128 xs = 0;
+    if (XSMEM) stage_digits(xd, ld, xg, N, Kp, nrm_w, BF ? &xs : nullptr);
     const unsigned char *xb = xd + g * ld + 4 * t;
 
     int c[NP][4];
@@ -416,14 +652,18 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
         for (int q = 0; q < 4; q++) c[p][q] = 0;
     i128 r0 = 0, r1 = 0;
     int since_fold = 0;
-    int rt = (int)(u0 / KT), k0 = (int)(u0 - (int64_t)rt * KT);
-    for (int64_t ub = u0; ub < u1; ub += D) {
+    // current row tile and column tile; the segment of rt this warp owns began at k0
+    int rt = (int)(u0 / KT), kt = (int)(u0 - (int64_t)rt * KT), k0 = kt;
+    // units are consecutive tiles in memory: the ring's next request walks linearly
+    const uint4 *pnext = pl + (size_t)(u0 + D - 1) * TS;
+    const uint4 *const pend = pl + (size_t)u1 * TS;
+    const int n = (int)(u1 - u0);
+    for (int ib = 0; ib < n; ib += D) {
 #pragma unroll
         for (int s = 0; s < D; s++) {
-            const int64_t u = ub + s;
-            if (u >= u1) break;
-            if (u + D - 1 < u1) load_tile<NP>(buf[(s + D - 1) % D], pl + (size_t)(u + D - 1) * TS);
-            const int kt = (int)(u - (int64_t)rt * KT);
+            if (ib + s >= n) break;
+            if (pnext < pend) load_tile<NL>(buf[(s + D - 1) % D], pnext);
+            pnext += TS;
             const int kk = kt * 32;
             uint32_t b0, b1;
             if (XSMEM) {
@@ -433,80 +673,89 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
                 b0 = digit_word(xg, N, kk + 4 * t, g);
                 b1 = digit_word(xg, N, kk + 16 + 4 * t, g);
             }
-            mma_tile<NP>(c, buf[s], b0, b1);
-            if (++since_fold >= 1024) { fold_planes(c, t, r0, r1); since_fold = 0; }
-            if ((u + 1 == u1) || (kt + 1 == KT)) {  // segment end: flush this row tile's part
-                const int k1 = kt + 1;
+            mma_any<NP, BF, NL>(c, buf[s], b0, b1);
+            // staged rows have KT <= 399 tiles, so a segment never reaches the
+            // 1024 tiles after which the int32 plane sums must be folded
+            if (!XSMEM && ++since_fold >= 1024) { fold_planes(c, t, r0, r1); since_fold = 0; }
+            if (++kt == KT) {  // row tile complete: flush this warp's part of it
                 fold_planes(c, t, r0, r1);
                 since_fold = 0;
-                // the 4 lanes of a row group hold the 8 digits: reduce over t
-#pragma unroll
-                for (int m = 1; m <= 2; m <<= 1) {
-                    r0 += shfl_xor_i128(r0, m);
-                    r1 += shfl_xor_i128(r1, m);
-                }
-                if (t == 0 && add == IQ_EPI_SWIGLU) {
-                    // rows g (gate) and g + 8 (up) complete together: one counter
-                    const int row = rt * 16 + g;
-                    i128 f0 = r0, f1 = r1;
-                    bool write = k0 == 0 && k1 == KT;
-                    if (!write) {
-                        RowAcc *ra = racc + row, *rb = racc + row + 8;
-                        atomic_add_i128(ra, r0);
-                        atomic_add_i128(rb, r1);
-                        cuda::atomic_ref<unsigned int, cuda::thread_scope_device> done(ra->done);
-                        unsigned int prev = done.fetch_add((unsigned int)(k1 - k0), cuda::memory_order_acq_rel);
-                        if (prev + (unsigned int)(k1 - k0) == (unsigned int)KT) {
-                            unsigned long long alo = atomicExch(&ra->lo, 0ull), ahi = atomicExch(&ra->hi, 0ull);
-                            unsigned long long blo = atomicExch(&rb->lo, 0ull), bhi = atomicExch(&rb->hi, 0ull);
-                            atomicExch(&ra->done, 0u);
-                            f0 = (i128)(((u128)ahi << 64) | alo);
-                            f1 = (i128)(((u128)bhi << 64) | blo);
-                            write = true;
-                        }
-                    }
-                    if (write) {
-                        const int64_t gate = finish_row(f0, row, R, XSMEM ? xd : nullptr, ld, xg);
-                        const int64_t up = finish_row(f1, row + 8, R, XSMEM ? xd : nullptr, ld, xg);
-                        out[rt * 8 + g] = d_mul(d_silu(gate), up);
-                    }
-                } else if (t == 0) {
-#pragma unroll
-                    for (int h = 0; h < 2; h++) {
-                        const int row = rt * 16 + g + 8 * h;
-                        if (row >= M) continue;
-                        i128 part = h ? r1 : r0;
-                        i128 fin = 0;
-                        bool write = false;
-                        if (k0 == 0 && k1 == KT) { fin = part; write = true; }
-                        else {
-                            RowAcc *ra = racc + row;
-                            atomic_add_i128(ra, part);
-                            // release our partial / acquire everyone else's with the counter
-                            cuda::atomic_ref<unsigned int, cuda::thread_scope_device> done(ra->done);
-                            unsigned int prev = done.fetch_add((unsigned int)(k1 - k0), cuda::memory_order_acq_rel);
-                            if (prev + (unsigned int)(k1 - k0) == (unsigned int)KT) {
-                                unsigned long long lo = atomicExch(&ra->lo, 0ull);
-                                unsigned long long hi = atomicExch(&ra->hi, 0ull);
-                                atomicExch(&ra->done, 0u);
-                                fin = (i128)(((u128)hi << 64) | lo);
-                                write = true;
-                            }
-                        }
-                        if (write) {
-                            int64_t val = finish_row(fin, row, R, XSMEM ? xd : nullptr, ld, xg);
-                            // add != 0: residual epilogue out += result (int64 wrap, llama_int.c:1535, 1556)
-                            out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)val) : val;
-                        }
-                    }
-                }
+                flush_segment(r0, r1, rt, k0, KT, KT, M, add, out, racc, R, XSMEM ? xd : nullptr, ld, xg, xs, g, t);
                 r0 = 0;
                 r1 = 0;
                 rt += 1;
+                kt = 0;
                 k0 = 0;
             }
         }
     }
+    if (kt != k0) {  // the warp's range ended inside row tile rt
+        fold_planes(c, t, r0, r1);
+        flush_segment(r0, r1, rt, k0, kt, KT, M, add, out, racc, R, XSMEM ? xd : nullptr, ld, xg, xs, g, t);
+    }
+}
+
+// End of a row tile in k_matvec_rows (every thread of the CTA calls it): the
+// warps' partials meet in shared memory, then (S > 1) the CTAs' in rank 0's
+// over distributed shared memory, and 16 threads finish and write the rows.
+// Returns true for cluster ranks > 0, which are done (one tile per cluster).
+// Out of line, as flush_segment, so the unrolled ring stays small.
+__device__ __noinline__ bool rows_tile_end(i128 r0, i128 r1, int rt, int rt0, const RowPre pre0, uint32_t S,
+                                           uint32_t crank, int M, int add, int64_t *__restrict__ out,
+                                           const PackedRes R, const unsigned char *xd, int ld,
+                                           const int64_t *__restrict__ xg, i128 xs, unsigned long long *wpart,
+                                           unsigned long long *cpart) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int m = 1; m <= 2; m <<= 1) {  // the 4 lanes of a row group hold the 8 digits
+        r0 += shfl_xor_i128(r0, m);
+        r1 += shfl_xor_i128(r1, m);
+    }
+    // wpart [8 warps][16 rows][2], cpart [8 ranks][16 rows][2]
+    if (t == 0) {
+        wpart[(warp * 16 + g) * 2] = (uint64_t)r0; wpart[(warp * 16 + g) * 2 + 1] = (uint64_t)((u128)r0 >> 64);
+        wpart[(warp * 16 + g + 8) * 2] = (uint64_t)r1;
+        wpart[(warp * 16 + g + 8) * 2 + 1] = (uint64_t)((u128)r1 >> 64);
+    }
+    __syncthreads();
+    i128 v = 0;
+    if (threadIdx.x < 16) {
+#pragma unroll
+        for (int w = 0; w < 8; w++)
+            v += (i128)(((u128)wpart[(w * 16 + threadIdx.x) * 2 + 1] << 64) | wpart[(w * 16 + threadIdx.x) * 2]);
+    }
+    if (S > 1) {
+        asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+        if (threadIdx.x < 16) {
+            uint32_t remote;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, 0;"
+                         : "=r"(remote)
+                         : "r"((uint32_t)__cvta_generic_to_shared(&cpart[(crank * 16 + threadIdx.x) * 2])));
+            asm volatile("st.shared::cluster.v2.u64 [%0], {%1, %2};"
+                         :: "r"(remote), "l"((uint64_t)v), "l"((uint64_t)((u128)v >> 64)) : "memory");
+        }
+        asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+        asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+        if (crank != 0) return true;
+        if (threadIdx.x < 16) {
+            v = 0;
+            for (uint32_t r = 0; r < S; r++)
+                v += (i128)(((u128)cpart[(r * 16 + threadIdx.x) * 2 + 1] << 64) | cpart[(r * 16 + threadIdx.x) * 2]);
+        }
+    }
+    const int row = rt * 16 + (int)threadIdx.x;
+    int64_t val = 0;
+    if (threadIdx.x < 16 && row < M) {
+        const RowPre pre = rt != rt0 ? row_pre(row, R) : pre0;
+        val = finish_row(v, pre, R, xd, ld, xg, xs);
+        if (add != IQ_EPI_SWIGLU) out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)val) : val;
+    }
+    if (add == IQ_EPI_SWIGLU && warp == 0) {  // tile rows g (gate) and g + 8 (up)
+        const int64_t up = __shfl_down_sync(0xffffffffu, val, 8);
+        if (lane < 8 && rt * 16 + lane < M) out[rt * 8 + lane] = d_mul(d_silu(val), up);
+    }
+    __syncthreads();  // wpart is rewritten by the next tile
+    return false;
 }
 
 // Row-owned variant: a cluster of S CTAs (S = 1, 2, 4 or 8) owns one 16-row
@@ -519,15 +768,16 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
 // unit steps (ntiles * nk, empty ones skipped), so the per-tile barriers are
 // reached in step. Staged digits only (Kp <= 12784: fewer than 1024 column
 // tiles per warp, so the int32 plane sums cannot overflow before the fold).
-template <int NP>
+template <int NP, bool BF = false>
 __global__ void __launch_bounds__(256, 2)
 k_matvec_rows(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const PackedRes R,
               const int64_t *__restrict__ xg, int M, int N, int Kp, int add, const int64_t *__restrict__ nrm_w) {
     extern __shared__ __align__(16) unsigned char xd[];  // [8][Kp + 16] digit rows
     __shared__ __align__(16) unsigned long long wpart[8][16][2];  // per warp: 16 row partials (lo, hi)
     __shared__ __align__(16) unsigned long long cpart[8][16][2];  // per cluster rank (read in rank 0)
-    constexpr int D = ring_depth<NP>();
-    constexpr int TS = NP * 32;  // uint4 per packed tile
+    constexpr int D = ring_depth<NP, BF>();
+    constexpr int NL = tile_loads<NP, BF>();
+    constexpr int TS = NL * 32;  // uint4 per packed tile
     const int ld = Kp + 16;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
     const int KT = Kp / 32, RT = (M + 15) / 16;
@@ -549,11 +799,11 @@ k_matvec_rows(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const
     int pj = 0;
     const uint4 *pbase = planes + lane + ((size_t)rt0 * KT + k0) * TS;
     const size_t tile_step = (size_t)stride * KT * TS;
-    auto prefetch = [&](uint4 (&dst)[NP]) {
-        if (k0 + pj < k1) load_tile<NP>(dst, pbase + (size_t)pj * TS);
+    auto prefetch = [&](uint4 (&dst)[NL]) {
+        if (k0 + pj < k1) load_tile<NL>(dst, pbase + (size_t)pj * TS);
         if (++pj == nk) { pj = 0; pbase += tile_step; }
     };
-    uint4 buf[D][NP];
+    uint4 buf[D][NL];
 #pragma unroll
     for (int s = 0; s < D - 1; s++)
         if (s < total) prefetch(buf[s]);
@@ -562,7 +812,8 @@ k_matvec_rows(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const
     if (threadIdx.x < 16 && ntiles > 0 && rt0 * 16 + (int)threadIdx.x < M) pre = row_pre(rt0 * 16 + threadIdx.x, R);
     // x and (with add) out are produced by the previous kernel
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    stage_digits(xd, ld, xg, N, Kp, nrm_w);
+    i128 xs = 0;
+    stage_digits(xd, ld, xg, N, Kp, nrm_w, BF ? &xs : nullptr);
     const unsigned char *xb = xd + g * ld + 4 * t;
     int c[NP][4];
 #pragma unroll
@@ -580,60 +831,16 @@ k_matvec_rows(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const
             if (kt < k1) {
                 const uint32_t b0 = *reinterpret_cast<const uint32_t *>(xb + kt * 32);
                 const uint32_t b1 = *reinterpret_cast<const uint32_t *>(xb + kt * 32 + 16);
-                mma_tile<NP>(c, buf[s], b0, b1);
+                mma_any<NP, BF, NL>(c, buf[s], b0, b1);
             }
             if (++j < nk) continue;
             // ---- end of this warp's part of tile rt: reduce and write
             j = 0;
             i128 r0 = 0, r1 = 0;
             fold_planes(c, t, r0, r1);
-#pragma unroll
-            for (int m = 1; m <= 2; m <<= 1) {  // the 4 lanes of a row group hold the 8 digits
-                r0 += shfl_xor_i128(r0, m);
-                r1 += shfl_xor_i128(r1, m);
-            }
-            if (t == 0) {
-                wpart[warp][g][0] = (uint64_t)r0; wpart[warp][g][1] = (uint64_t)((u128)r0 >> 64);
-                wpart[warp][g + 8][0] = (uint64_t)r1; wpart[warp][g + 8][1] = (uint64_t)((u128)r1 >> 64);
-            }
-            __syncthreads();
-            i128 v = 0;
-            if (threadIdx.x < 16) {
-#pragma unroll
-                for (int w = 0; w < 8; w++)
-                    v += (i128)(((u128)wpart[w][threadIdx.x][1] << 64) | wpart[w][threadIdx.x][0]);
-            }
-            if (S > 1) {
-                asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
-                if (threadIdx.x < 16) {
-                    uint32_t remote;
-                    asm volatile("mapa.shared::cluster.u32 %0, %1, 0;"
-                                 : "=r"(remote)
-                                 : "r"((uint32_t)__cvta_generic_to_shared(&cpart[crank][threadIdx.x][0])));
-                    asm volatile("st.shared::cluster.v2.u64 [%0], {%1, %2};"
-                                 :: "r"(remote), "l"((uint64_t)v), "l"((uint64_t)((u128)v >> 64)) : "memory");
-                }
-                asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-                asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-                if (crank != 0) return;  // one tile per cluster
-                if (threadIdx.x < 16) {
-                    v = 0;
-                    for (uint32_t r = 0; r < S; r++)
-                        v += (i128)(((u128)cpart[r][threadIdx.x][1] << 64) | cpart[r][threadIdx.x][0]);
-                }
-            }
-            const int row = rt * 16 + (int)threadIdx.x;
-            int64_t val = 0;
-            if (threadIdx.x < 16 && row < M) {
-                if (rt != rt0) pre = row_pre(row, R);
-                val = finish_row(v, pre, R, xd, ld, xg);
-                if (add != IQ_EPI_SWIGLU) out[row] = add ? (int64_t)((uint64_t)out[row] + (uint64_t)val) : val;
-            }
-            if (add == IQ_EPI_SWIGLU && warp == 0) {  // tile rows g (gate) and g + 8 (up)
-                const int64_t up = __shfl_down_sync(0xffffffffu, val, 8);
-                if (lane < 8 && rt * 16 + lane < M) out[rt * 8 + lane] = d_mul(d_silu(val), up);
-            }
-            __syncthreads();  // wpart is rewritten by the next tile
+            if (rows_tile_end(r0, r1, rt, rt0, pre, S, crank, M, add, out, R, xd, ld, xg, xs, &wpart[0][0][0],
+                              &cpart[0][0][0]))
+                return;  // cluster rank > 0: one tile per cluster
             rt += stride;
         }
     }

@@ -42,11 +42,13 @@ SIGNATURES = {
     "iq_matvec_dev": (_I, [_P, _P, _P, _I, _I, _P]),
     "iq_gemm_dev": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "iq_pack_weights_dev": (_I, [_P, _I, _I, _P, _P]),
+    "iq_pack_weights_fmt_dev": (_I, [_P, _I, _I, _I, _P, _P]),
     "iq_packed_free": (_I, [_P]),
     "iq_packed_info": (_I, [_P, _P, _P, _P]),
     "iq_matvec_packed_dev": (_I, [_P, _P, _P, _P]),
     "iq_matvec_packed_noalloc_dev": (_I, [_P, _P, _P, _P]),
     "iq_packed_bytes": (_I, [_P, _P]),
+    "iq_packed_format": (_I, [_P, _P]),
     "iq_pack_weights_tc_dev": (_I, [_P, _I, _I, _P, _P]),
     "iq_packed_tc_free": (_I, [_P]),
     "iq_packed_tc_info": (_I, [_P, _P, _P, _P]),
@@ -226,16 +228,24 @@ def matvec_dev(out, w, x, M, N, stream=None):
 class Packed:
     """Byte-plane packed weights on the device (iq_pack_weights_dev)."""
 
-    def __init__(self, d_w, M, N, stream=None):
+    def __init__(self, d_w, M, N, stream=None, fmt=None):
+        """fmt: None = the library's choice, 'planes' or 'bf16'."""
         self.h = ctypes.c_void_p()
         self.M, self.N = M, N
-        _call("iq_pack_weights_dev", _dp(d_w), M, N, _sp(stream), ctypes.byref(self.h))
+        f = {None: -1, "planes": 0, "bf16": 1}[fmt]
+        _call("iq_pack_weights_fmt_dev", _dp(d_w), M, N, f, _sp(stream), ctypes.byref(self.h))
 
     def info(self):
         """(np, p0, residual_entries): stored planes p0 .. p0+np-1 and the sparse residual size."""
         a, b, c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
         _call("iq_packed_info", self.h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c))
         return a.value, b.value, c.value
+
+    def fmt(self):
+        """'planes' (byte-plane window) or 'bf16' (2 bytes per weight)."""
+        f = ctypes.c_int()
+        _call("iq_packed_format", self.h, ctypes.byref(f))
+        return ("planes", "bf16")[f.value]
 
     def nbytes(self):
         """Bytes of the stored form one matvec launch reads (iq_packed_bytes)."""

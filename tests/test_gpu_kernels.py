@@ -227,6 +227,12 @@ def test_matvec_packed_vs_oracle(M, N, dist):
         x = orc.synth_acts(1, f"x:{M}x{N}", (N,))
     want = orc.matmul_vec(w, x)
     pk = iq.Packed(dev(w), M, N)
+    # full-range weights keep byte planes; config weights take the 2-byte bf16
+    # form on the config shapes (rows too long to stage keep planes)
+    if dist == "full" or N > 12768:
+        assert pk.fmt() == "planes"
+    elif M * N >= 256 * 2048:
+        assert pk.fmt() == "bf16"
     dx = dev(x)
     for _ in range(2):
         do = torch.zeros(M, dtype=torch.int64, device="cuda")
@@ -296,7 +302,7 @@ def test_plane_window_config_weights():
     the few weights with nonzero low bytes into the sparse residual."""
     import torch
     w = orc.synth_weights(1, "w:window", (2048, 2048))
-    pk = iq.Packed(dev(w), 2048, 2048)
+    pk = iq.Packed(dev(w), 2048, 2048, fmt="planes")
     np_, p0, nnz = pk.info()
     low = (w.view(np.uint64) & np.uint64((1 << 8 * p0) - 1)) != 0
     assert (np_, p0) == (3, 3) and nnz == int(low.sum()) and 0 < nnz < 2048 * 2048 // 1024
@@ -456,3 +462,69 @@ def test_dropin_full_mode_finds_reloaded_layers_by_content():
         iq.weight_cache_limit(64 << 30)
         iq.weight_check_mode("sampled")
         iq.weight_cache_clear()
+
+
+# ------------------------------------------------------------- bf16 form
+
+def _bf16_weights(rng, shape, outliers):
+    """bf16-derived weights (bfloat16_to_q1648 of N(0, 0.02) values) with
+    planted weights the bf16 form cannot hold: |w| >= 0.25, exponent-255 codes
+    (+-32000.0), tiny truncated values, and non-bf16 int64 values, at the first
+    and last rows and columns and in one crowded row."""
+    import torch
+    f = torch.from_numpy(rng.normal(0, 0.02, shape).astype(np.float32)).bfloat16()
+    bits = f.view(torch.int16).numpy().astype(np.uint16)
+    conv = np.vectorize(orc.O.iqo_bf16_to_q1648, otypes=[np.int64])
+    w = conv(bits)
+    M, N = shape
+    if outliers:
+        spots = [(0, 0), (M - 1, N - 1), (0, N - 1), (M - 1, 0)] + [(M // 2, k) for k in range(0, N, 7)]
+        vals = [orc.O.iqo_bf16_to_q1648(0x3F00), orc.O.iqo_bf16_to_q1648(0xBF40), orc.O.iqo_bf16_to_q1648(0x7F85),
+                orc.O.iqo_bf16_to_q1648(0xFF80), orc.O.iqo_bf16_to_q1648(0x2A31), orc.O.iqo_bf16_to_q1648(0xAA31),
+                (1 << 40) + 12345, -(1 << 50) - 7]
+        for i, (r, k) in enumerate(spots):
+            w[r, k] = vals[i % len(vals)]
+    return w
+
+
+@pytest.mark.parametrize("M,N", [(1, 1), (17, 33), (300, 2048), (2048, 2048), (256, 2048), (129, 4097),
+                                 (5000, 300), (9600, 64), (64, 12768)])
+@pytest.mark.parametrize("outliers", [False, True])
+def test_bf16_form_vs_oracle(M, N, outliers):
+    """The 2-byte bf16 form (in-kernel bf16 -> byte planes, u = v + 2^22 bias,
+    2^22 sum x correction, whole-weight residual) equals the oracle bit for bit,
+    forced on every shape: row-owned kernel with clusters of 1..8, two waves,
+    stream-K (9600 rows), the longest row it accepts (N = 12768), padding of
+    rows and columns (-0.25 pad weights), and planted weights it cannot hold."""
+    import torch
+    rng = np.random.default_rng(M * 7 + N)
+    w = _bf16_weights(rng, (M, N), outliers)
+    x = rand_full(rng, (N,))
+    want = orc.matmul_vec(w, x)
+    pk = iq.Packed(dev(w), M, N, fmt="bf16")
+    assert pk.fmt() == "bf16"
+    dx = dev(x)
+    for _ in range(2):
+        do = torch.zeros(M, dtype=torch.int64, device="cuda")
+        iq.matvec_packed_dev(do, pk, dx)
+        assert (host(do) == want).all()
+    pk.free()
+
+
+def test_bf16_form_rejects_unstageable_rows_and_full_range_stays_exact():
+    import torch
+    w = torch.zeros((4, 13000), dtype=torch.int64, device="cuda")
+    with pytest.raises(iq.IQError) as e:
+        iq.Packed(w, 4, 13000, fmt="bf16")
+    assert e.value.status == -8   # IQ_ERR_UNSUPPORTED
+    rng = np.random.default_rng(3)
+    w = rand_full(rng, (40, 300))     # nothing representable: every weight in the residual
+    x = rand_full(rng, (300,))
+    pk = iq.Packed(dev(w), 40, 300, fmt="bf16")
+    do = torch.zeros(40, dtype=torch.int64, device="cuda")
+    iq.matvec_packed_dev(do, pk, dev(x))
+    assert (host(do) == orc.matmul_vec(w, x)).all()
+    pk.free()
+    pk = iq.Packed(dev(w), 40, 300)
+    assert pk.fmt() == "planes"       # the automatic choice never picks it here
+    pk.free()

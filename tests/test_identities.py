@@ -97,3 +97,84 @@ def test_limb_score_dot():
             assert -(1 << 63) <= v < (1 << 63)      # int64 partial sums never overflow
         dot = sum((H[i] << (32 + 22 * i)) + (L[i] << (22 * i)) for i in range(3)) + (sum(q) << 31)
         assert dot & M128 == sum(a * b for a, b in zip(q, k)) & M128, trial
+
+
+# ------------------------------------------------------------ bf16 form
+
+def bf_encode(w):
+    """Restates iq_planes.cuh bf_encode: the bf16 bits that hold w exactly as
+    v 2^24 (v in [-2^22, 2^22), <= 8 significant bits), else -1."""
+    if w & 0xFFFFFF:
+        return -1
+    v = w >> 24
+    if not -(1 << 22) <= v < (1 << 22):
+        return -1
+    if v == 0:
+        return 0
+    a = abs(v)
+    e2 = a.bit_length() - 1
+    tz = (a & -a).bit_length() - 1
+    if e2 - tz >= 8:
+        return -1
+    return (0x8000 if v < 0 else 0) | ((e2 + 103) << 7) | (((a << 7) >> e2) & 0x7F)
+
+
+def bf_u(bits):
+    """u = low 23 bits of fp32 fma.rm(f, 2^24, 1.5*2^23) for the bf16 value f:
+    here the exact sum is an integer in [2^23, 2^24), so any rounding mode gives
+    it; numpy's fp32 (round to nearest) shows the bit pattern."""
+    import numpy as np
+    f = np.array([bits << 16], dtype=np.uint32).view(np.float32)[0]
+    r = np.float32(np.float64(f) * 16777216.0 + 12582912.0)
+    assert np.float64(r) == np.float64(f) * 16777216.0 + 12582912.0   # exact
+    return int(np.array([r], dtype=np.float32).view(np.uint32)[0]) & 0x7FFFFF
+
+
+def test_bf16_encode_decode_exact_and_u_bias():
+    import oracle as orc
+    rng = random.Random(5)
+    seen = 0
+    for bits in list(range(0, 0x10000, 37)) + [0xBE80, 0x3E80, 0x0001]:
+        w = orc.O.iqo_bf16_to_q1648(bits)
+        enc = bf_encode(w)
+        if enc < 0:
+            continue
+        seen += 1
+        # the stored bits decode (bfloat16_to_q1648) to the same weight
+        assert orc.O.iqo_bf16_to_q1648(enc) == w, hex(bits)
+        assert bf_u(enc) == (w >> 24) + (1 << 22), hex(bits)
+    assert seen > 1000
+    assert bf_u(0xBE80) == 0            # padding: -0.25 -> u = 0
+    assert bf_u(0) == 1 << 22           # +0.0 -> v = 0
+
+
+def test_bf16_form_dot_identity():
+    """sum x w = 2^24 (sum_k x_u u - 2^63 U - 2^22 X) + residual (mod 2^128), with
+    x_u = x + 2^63, u = v + 2^22, U = sum u, X = sum x; weights the form cannot
+    hold are v = 0 and go to the residual whole."""
+    import oracle as orc
+    rng = random.Random(9)
+    for trial in range(40):
+        n = rng.randint(1, 70)
+        ws = []
+        for _ in range(n):
+            kind = rng.random()
+            if kind < 0.8:   # bf16-derived, config-like
+                ws.append(orc.O.iqo_bf16_to_q1648(rng.choice(range(0x3000, 0x3F00)) | rng.choice([0, 0x8000])))
+            elif kind < 0.9:
+                ws.append(rng.randint(-(1 << 63), (1 << 63) - 1))
+            else:
+                ws.append(orc.O.iqo_bf16_to_q1648(rng.randint(0, 0xFFFF)))
+        xs = [rng.randint(-(1 << 63), (1 << 63) - 1) for _ in range(n)]
+        want = sum(x * w for x, w in zip(xs, ws)) & M128
+        acc = U = X = res = 0
+        for x, w in zip(xs, ws):
+            e = bf_encode(w)
+            v = (w >> 24) if e >= 0 else 0
+            u = v + (1 << 22)
+            acc += (x + (1 << 63)) * u
+            U += u
+            X += x
+            res += x * (w - (v << 24))
+        got = ((acc - (U << 63) - (X << 22)) << 24) + res
+        assert got & M128 == want, trial
