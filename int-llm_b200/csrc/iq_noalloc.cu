@@ -8,8 +8,8 @@
 // iq_matvec_packed_dev grows a per-stream scratch buffer with cudaMalloc on
 // first use; this variant uses a fixed array that lives in the library image.
 //
-// The split-row scratch (one 24-byte RowAcc per output row) is the file-scope
-// device array g_noalloc_rows below: IQ_NOALLOC_MAX_ROWS entries (768 KiB),
+// The split-row scratch (one 32-byte RowAcc per output row) is the file-scope
+// device array g_noalloc_rows below: IQ_NOALLOC_MAX_ROWS entries (1 MiB),
 // held by every GPU that loads the library until the process exits. In host
 // code its name is only a host-side stand-in, so the kernel gets the real
 // device address, fetched once per device by cudaGetSymbolAddress.

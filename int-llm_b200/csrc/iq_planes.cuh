@@ -94,19 +94,27 @@ struct PackedRes {
 };
 
 // Per-row scratch for rows whose columns are split between warps: a 128-bit
-// accumulator and a count of column tiles done. Zero before the first launch;
-// the warp that completes a row resets its entry.
-struct RowAcc { unsigned long long lo, hi; unsigned int done, pad; };
+// accumulator kept as three limbs of 43, 43 and 42 bits in 64-bit words, and a
+// count of column tiles done. Zero before the first launch; the warp that
+// completes a row resets its entry.
+struct RowAcc { unsigned long long l0, l1, l2; unsigned int done, pad; };
 
-// Exact 128-bit atomic accumulate: add the lo word atomically, and fold the
-// carry out of that very addition (known from the returned old value) into
-// the hi word's atomic add; concurrent adders then sum exactly mod 2^128.
-__device__ __forceinline__ void atomic_add_i128(RowAcc *a, i128 v) {
-    unsigned long long lo = (unsigned long long)(uint64_t)v;
-    unsigned long long hi = (unsigned long long)(uint64_t)((u128)v >> 64);
-    unsigned long long old = atomicAdd(&a->lo, lo);
-    hi += (old + lo < old) ? 1ull : 0ull;
-    atomicAdd(&a->hi, hi);
+// Exact 128-bit accumulate without a carry chain: each limb of v (< 2^43)
+// goes to its own word with a fire-and-forget atomic add; a row has at most
+// 1024 adders here (2^53 per word at most), so no word can overflow, and the
+// reader recombines l0 + 2^43 l1 + 2^86 l2 = sum of the v (mod 2^128).
+__device__ __forceinline__ void racc_add(RowAcc *a, i128 v) {
+    const u128 u = (u128)v;
+    const uint64_t m43 = (1ull << 43) - 1;
+    atomicAdd(&a->l0, (unsigned long long)((uint64_t)u & m43));
+    atomicAdd(&a->l1, (unsigned long long)((uint64_t)(u >> 43) & m43));
+    atomicAdd(&a->l2, (unsigned long long)(uint64_t)(u >> 86));
+}
+// Reads the sum and clears the entry (by the adder that completed the row).
+__device__ __forceinline__ i128 racc_take(RowAcc *a) {
+    const u128 l0 = atomicExch(&a->l0, 0ull), l1 = atomicExch(&a->l1, 0ull), l2 = atomicExch(&a->l2, 0ull);
+    atomicExch(&a->done, 0u);
+    return (i128)(l0 + (l1 << 43) + (l2 << 86));
 }
 
 // ---------------------------------------------------------------- packing
@@ -535,6 +543,19 @@ __device__ __forceinline__ void mma_any(int (&c)[NP][4], const uint4 (&a)[NL], u
     }
 }
 
+// Pulls the flush's static row data (row sums, residual offsets) of row tile
+// rt into L1 ahead of its use (lanes t == 0 of the 8 row groups: rows g, g+8).
+__device__ __forceinline__ void prefetch_rows(const PackedRes &R, int rt, int M, int g, int t) {
+    if (t != 0) return;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const int row = rt * 16 + g + 8 * h;
+        if (row >= M) continue;
+        asm volatile("prefetch.global.L1 [%0];" :: "l"(R.rowsum + 2 * row));
+        if (R.ptr) asm volatile("prefetch.global.L1 [%0];" :: "l"(R.ptr + row));
+    }
+}
+
 // End of a warp's segment of row tile rt (column tiles k0 .. k1-1): the 4 lanes
 // of each row group sum their digits' partials, then the row's writer either
 // owns the whole row (k0 == 0, k1 == KT) or meets the other segments in the
@@ -558,16 +579,14 @@ __device__ __noinline__ void flush_segment(i128 r0, i128 r1, int rt, int k0, int
         bool write = k0 == 0 && k1 == KT;
         if (!write) {
             RowAcc *ra = racc + row, *rb = racc + row + 8;
-            atomic_add_i128(ra, r0);
-            atomic_add_i128(rb, r1);
+            racc_add(ra, r0);
+            racc_add(rb, r1);
+            // release our limbs / acquire everyone else's with the counter
             cuda::atomic_ref<unsigned int, cuda::thread_scope_device> done(ra->done);
             unsigned int prev = done.fetch_add((unsigned int)(k1 - k0), cuda::memory_order_acq_rel);
             if (prev + (unsigned int)(k1 - k0) == (unsigned int)KT) {
-                unsigned long long alo = atomicExch(&ra->lo, 0ull), ahi = atomicExch(&ra->hi, 0ull);
-                unsigned long long blo = atomicExch(&rb->lo, 0ull), bhi = atomicExch(&rb->hi, 0ull);
-                atomicExch(&ra->done, 0u);
-                f0 = (i128)(((u128)ahi << 64) | alo);
-                f1 = (i128)(((u128)bhi << 64) | blo);
+                f0 = racc_take(ra);
+                f1 = racc_take(rb);
                 write = true;
             }
         }
@@ -587,15 +606,12 @@ __device__ __noinline__ void flush_segment(i128 r0, i128 r1, int rt, int k0, int
             if (k0 == 0 && k1 == KT) { fin = part; write = true; }
             else {
                 RowAcc *ra = racc + row;
-                atomic_add_i128(ra, part);
-                // release our partial / acquire everyone else's with the counter
+                racc_add(ra, part);
+                // release our limbs / acquire everyone else's with the counter
                 cuda::atomic_ref<unsigned int, cuda::thread_scope_device> done(ra->done);
                 unsigned int prev = done.fetch_add((unsigned int)(k1 - k0), cuda::memory_order_acq_rel);
                 if (prev + (unsigned int)(k1 - k0) == (unsigned int)KT) {
-                    unsigned long long lo = atomicExch(&ra->lo, 0ull);
-                    unsigned long long hi = atomicExch(&ra->hi, 0ull);
-                    atomicExch(&ra->done, 0u);
-                    fin = (i128)(((u128)hi << 64) | lo);
+                    fin = racc_take(ra);
                     write = true;
                 }
             }
@@ -658,6 +674,7 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
     const uint4 *pnext = pl + (size_t)(u0 + D - 1) * TS;
     const uint4 *const pend = pl + (size_t)u1 * TS;
     const int n = (int)(u1 - u0);
+    if (n > 0) prefetch_rows(R, rt, M, g, t);
     for (int ib = 0; ib < n; ib += D) {
 #pragma unroll
         for (int s = 0; s < D; s++) {
@@ -686,6 +703,7 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
                 rt += 1;
                 kt = 0;
                 k0 = 0;
+                if (ib + s + 1 < n) prefetch_rows(R, rt, M, g, t);
             }
         }
     }
