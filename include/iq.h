@@ -300,6 +300,25 @@ IQ_API int iq_decode_steps_timed(iq_model *m, int pos0, int steps, float *ms);
  * the single-kernel form does not fit shared memory at this max_seq_len. */
 IQ_API int iq_model_set_attention(iq_model *m, int short_max);
 
+/* Decode-step implementation (no reference counterpart; identical bits either
+ * way). mode 0 (default): one kernel per operation, the step captured in a
+ * CUDA graph. mode 1: at batch 1 without tensor parallelism, when every decode
+ * matrix is in the bf16 form, a decode step is ONE persistent cooperative
+ * kernel (all SMs resident, grid-wide barriers between the layer's phases);
+ * elsewhere mode 1 falls back to mode 0. On B200 mode 1 is slower today (each
+ * barrier costs ~2.5 us and the phases are latency-bound), so it is off by
+ * default. iq_model_decode_info reports whether the persistent kernel is in
+ * use and its grid size. */
+IQ_API int iq_model_set_decode(iq_model *m, int mode);
+IQ_API int iq_model_decode_info(iq_model *m, int *persistent, int *grid);
+/* Diagnostics of the persistent kernel: microseconds per grid barrier with
+ * `grid` CTAs (mode 0); and, with IQ_DEC_STAMPS set in the environment when
+ * the model first prepares it, the last step's event times (ns since its
+ * start, event tag in the top byte; slots 400+ / 700+ of a 1024-entry buffer:
+ * per matvec phase the latest staging end / loop end over all warps). */
+IQ_API int iq_bench_grid_sync(int grid, int iters, int mode, float *us);
+IQ_API int iq_model_decode_stamps(iq_model *m, int64_t *out, int n);
+
 /* Bytes of stored weights this rank's decode step reads per token at batch 1
  * (every projection's matvec form plus the LM head; not the KV cache), and the
  * bytes of the GEMM forms (prefill / batched decode). The numerators of the

@@ -25,6 +25,7 @@
 #include <nccl.h>
 #include "iq_common.cuh"
 #include "iq_layer.cuh"
+#include "iq_decode.cuh"
 
 using namespace iq;
 
@@ -104,6 +105,16 @@ struct iq_model {
     int64_t att_scale = 0;  // fp_inv_sqrt(fp_from_int(head_dim))
     bool loaded_globals = false;
     std::vector<bool> loaded_layer;
+    // persistent decode kernel (k_decode_token) for batch 1 without tensor
+    // parallelism: requested mode, and its state once prepared
+    int dec_mode = 0;           // 1 = use it where it applies, 0 = per-kernel path (default: faster today)
+    bool dec_ready = false;     // prepared for the current weights
+    DecParams dec{};
+    DecLayer *d_layers = nullptr;
+    GridBar *bar = nullptr;
+    unsigned long long *argv = nullptr;
+    int dec_grid = 0;
+    size_t dec_smem = 0;
 };
 
 static int dalloc(void **p, size_t bytes) {
@@ -390,7 +401,89 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
     return IQ_OK;
 }
 
+static MvView mv_view(const Packed &P) {
+    return MvView{(const uint4 *)P.planes, packed_res(P), P.M, P.N, P.Kp};
+}
+
+// Prepares the persistent decode kernel when it applies: batch 1, no tensor
+// parallelism, every decode matrix in the bf16 form (so one instantiation of
+// the matvec serves all), SwiGLU fused (pair-interleaved gate|up) and the
+// phased-attention scratch present. Must run outside stream capture.
+static int dec_prepare(iq_model *m) {
+    if (m->dec_ready || m->dec_mode == 0) return IQ_OK;
+    const iq_config &c = m->c;
+    const Shard &S = m->sh;
+    if (m->max_batch != 1 || S.P != 1 || !m->att_phased || S.it_l % 8 || c.head_dim > 256) return IQ_OK;
+    auto bf = [](const Packed &P) { return P.fmt == IQ_FMT_BF16 && (size_t)8 * (P.Kp + 16) <= 100 * 1024; };
+    if (!bf(m->plm)) return IQ_OK;
+    for (int l = 0; l < c.num_layers; l++)
+        if (!bf(m->pqkv[l]) || !bf(m->po[l]) || !bf(m->pgu[l]) || !bf(m->pdown[l])) return IQ_OK;
+    std::vector<DecLayer> hl(c.num_layers);
+    size_t kmax = m->plm.Kp;
+    for (int l = 0; l < c.num_layers; l++) {
+        hl[l] = DecLayer{mv_view(m->pqkv[l]), mv_view(m->po[l]), mv_view(m->pgu[l]), mv_view(m->pdown[l]),
+                         m->norm1[l], m->norm2[l], m->kc[l], m->vc[l]};
+        for (const Packed *P : {&m->pqkv[l], &m->po[l], &m->pgu[l], &m->pdown[l]}) kmax = std::max(kmax, (size_t)P->Kp);
+    }
+    const int att_short = 256;
+    const size_t hd = c.head_dim;
+    m->dec_smem = std::max({(size_t)8 * (kmax + 16), (3 * hd + std::max<size_t>(att_short, IQ_DEC_THREADS)) * 8,
+                            (2 * hd + DEC_TILE) * 8});
+    IQ_CUDA(cudaFuncSetAttribute(k_decode_token, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->dec_smem));
+    int occ = 0;
+    IQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_decode_token, IQ_DEC_THREADS, m->dec_smem));
+    if (occ < 1) return IQ_OK;
+    static const int per_sm = getenv("IQ_DEC_PER_SM") ? atoi(getenv("IQ_DEC_PER_SM")) : 2;
+    const int grid = dev_info().sms * std::max(1, std::min(occ, per_sm));
+    if (!m->d_layers) DALLOC(m->d_layers, (size_t)c.num_layers * sizeof(DecLayer));
+    IQ_CUDA(cudaMemcpy(m->d_layers, hl.data(), hl.size() * sizeof(DecLayer), cudaMemcpyHostToDevice));
+    if (!m->bar) DALLOC(m->bar, sizeof(GridBar));
+    IQ_CUDA(cudaMemset(m->bar, 0, sizeof(GridBar)));
+    if (m->dec_grid < grid) {
+        if (m->argv) cudaFree(m->argv);
+        m->argv = nullptr;
+        DALLOC(m->argv, (size_t)grid * 2 * sizeof(unsigned long long));
+    }
+    m->dec_grid = grid;
+    DecParams &p = m->dec;
+    p.L = c.num_layers; p.d = c.hidden_dim; p.nh = c.num_heads; p.nkv = c.num_kv_heads; p.hd = c.head_dim;
+    p.inter = c.intermediate_dim; p.V = c.vocab_size; p.max_seq = c.max_seq_len; p.att_short = att_short;
+    p.hist_stride = c.max_seq_len + 1;
+    p.scale = m->att_scale;
+    p.layers = m->d_layers;
+    p.lm = mv_view(m->plm);
+    p.embed = m->embed; p.fnorm = m->fnorm; p.rcos = m->rcos; p.rsin = m->rsin;
+    p.hidden = m->hidden; p.qkv = m->qkv; p.att = m->att; p.act = m->act; p.logits = m->logits;
+    p.racc = m->racc;
+    p.asc = m->asc; p.amx = m->amx; p.asum = (unsigned long long *)m->asum; p.argv = m->argv;
+    p.d_tok = m->d_tok; p.d_pos = m->d_pos; p.d_arg = m->d_arg; p.d_hist = m->d_hist;
+    p.bar = m->bar;
+    p.stamps = nullptr;
+    p.prefetch = getenv("IQ_DEC_PREFETCH") ? atoi(getenv("IQ_DEC_PREFETCH")) : 1;
+    if (getenv("IQ_DEC_STAMPS")) {   // profiling aid: barrier exit times of the last step
+        static unsigned long long *st = nullptr;
+        if (!st) DALLOC(st, 1024 * 8);
+        p.stamps = st;
+    }
+    m->dec_ready = true;
+    return IQ_OK;
+}
+
 static int enqueue_step(iq_model *m, int B, int tmax) {
+    if (B == 1 && m->dec_ready && m->dec_mode) {
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.gridDim = dim3((unsigned)m->dec_grid);
+        cfg.blockDim = dim3(IQ_DEC_THREADS);
+        cfg.dynamicSmemBytes = m->dec_smem;
+        cfg.stream = m->s;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        IQ_CUDA(cudaLaunchKernelEx(&cfg, k_decode_token, m->dec));
+        return IQ_OK;
+    }
     return enqueue_rows(m, B, m->d_tok, m->d_pos, m->d_seq, 0, 1, tmax);
 }
 
@@ -401,6 +494,8 @@ static cudaGraphExec_t &step_graph(iq_model *m, int tmax) {
 static int ensure_graph(iq_model *m, int tmax) {
     cudaGraphExec_t &gx = step_graph(m, tmax);
     if (gx) return IQ_OK;
+    int prc = dec_prepare(m);   // outside the capture: it allocates and copies
+    if (prc) return prc;
     const int tcap = tmax > 0 && tmax <= m->att_short ? m->att_short : 0;
     cudaGraph_t g;
     IQ_CUDA(cudaStreamBeginCapture(m->s, cudaStreamCaptureModeThreadLocal));
@@ -427,6 +522,15 @@ static int h2d(void *dst, const void *src, size_t bytes) {
     return IQ_OK;
 }
 
+// Weights are about to change: captured step graphs and the persistent decode
+// kernel's parameters hold pointers to the packed copies, so drop them.
+static void invalidate_exec(iq_model *m) {
+    cudaStreamSynchronize(m->s);
+    if (m->graph) { cudaGraphExecDestroy(m->graph); m->graph = nullptr; }
+    if (m->graph_s) { cudaGraphExecDestroy(m->graph_s); m->graph_s = nullptr; }
+    m->dec_ready = false;
+}
+
 static int repack(iq_model *m, Packed *P, const int64_t *W, int M, int N) {
     if (P->planes) { IQ_CUDA(cudaStreamSynchronize(m->s)); free_packed(P); }
     int rc = pack_weights(W, M, N, m->s, P);
@@ -443,6 +547,7 @@ static int repack_tc(iq_model *m, PackedTC *P, const int64_t *W, int M, int N) {
 }
 // Packs layer l's projections in both formats, then frees its raw int64 copies.
 static int repack_layer(iq_model *m, int l) {
+    invalidate_exec(m);
     const iq_config &c = m->c;
     const Shard &S = m->sh;
     int rc, d = c.hidden_dim, it = c.intermediate_dim;
@@ -646,7 +751,7 @@ IQ_API int iq_model_destroy(iq_model *m) {
     void *bufs[] = {m->embed, m->fnorm, m->lm, m->rcos, m->rsin, m->hidden, m->normed, m->qkv, m->att,
                     m->gu, m->act, m->logits, m->att_l, m->proj_l, m->act_l, m->logits_l, m->gath,
                     m->proj_full, m->d_tok, m->d_pos, m->d_arg, m->d_hist, m->racc, m->digits, m->gpart, m->asc, m->amx, m->asum, m->d_seq,
-                    m->d_ptok, m->d_ppos, m->d_pseq};
+                    m->d_ptok, m->d_ppos, m->d_pseq, m->d_layers, m->bar, m->argv};
     for (void *p : bufs) if (p) cudaFree(p);
     for (auto *v : {&m->norm1, &m->wqkv, &m->wo, &m->norm2, &m->wgu, &m->wdown, &m->kc, &m->vc})
         for (int64_t *p : *v) if (p) cudaFree(p);
@@ -668,6 +773,7 @@ IQ_API int iq_model_load_globals(iq_model *m, const int64_t *embed, const int64_
                                  const int64_t *lm_head) {
     if (!m || !embed || !final_norm || !lm_head) return IQ_ERR_ARG;
     IQ_CUDA(cudaSetDevice(m->dev));
+    invalidate_exec(m);
     if (!m->lm) DALLOC(m->lm, (size_t)m->sh.v_l * m->c.hidden_dim * 8);
     std::vector<TensorPlan> plan = tensor_plan(m);
     const int64_t *src[3] = {embed, lm_head, final_norm};
@@ -701,6 +807,8 @@ IQ_API int iq_model_reset(iq_model *m) {
         IQ_CUDA(cudaMemsetAsync(m->kc[l], 0, kvb, m->s));
         IQ_CUDA(cudaMemsetAsync(m->vc[l], 0, kvb, m->s));
     }
+    // a persistent decode kernel that gave up on a barrier left it abandoned
+    if (m->bar) IQ_CUDA(cudaMemsetAsync(m->bar, 0, sizeof(GridBar), m->s));
     IQ_CUDA(cudaStreamSynchronize(m->s));
     return IQ_OK;
 }
@@ -954,6 +1062,78 @@ IQ_API int iq_model_set_attention(iq_model *m, int short_max) {
     IQ_CUDA(cudaStreamSynchronize(m->s));
     if (m->graph_s) { cudaGraphExecDestroy(m->graph_s); m->graph_s = nullptr; }
     m->att_short = short_max;
+    return IQ_OK;
+}
+
+IQ_API int iq_model_set_decode(iq_model *m, int mode) {
+    if (!m || mode < 0 || mode > 1) return IQ_ERR_ARG;
+    IQ_CUDA(cudaSetDevice(m->dev));
+    invalidate_exec(m);
+    m->dec_mode = mode;
+    return IQ_OK;
+}
+
+// Diagnostic: microseconds per grid barrier of the persistent decode kernel
+// (k_bar_bench) with `grid` co-resident CTAs of 256 threads (mode must be 0).
+IQ_API int iq_bench_grid_sync(int grid, int iters, int mode, float *us) {
+    if (grid < 1 || iters < 1 || mode != 0 || !us) return IQ_ERR_ARG;
+    int dev, rc;
+    if ((rc = cur_device(&dev))) return rc;
+    GridBar *b = nullptr;
+    IQ_CUDA(cudaMalloc(&b, sizeof(GridBar)));
+    cudaMemset(b, 0, sizeof(GridBar));
+    void (*k)(GridBar *, int) = k_bar_bench;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(256);
+    cfg.stream = lib_stream();
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k, b, 10);
+    if (e == cudaSuccess) e = cudaEventRecord(e0, lib_stream());
+    if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, k, b, iters);
+    if (e == cudaSuccess) e = cudaEventRecord(e1, lib_stream());
+    if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+    float ms = 0;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaFree(b);
+    if (e != cudaSuccess) return cuda_fail(e);
+    *us = ms * 1000.0f / iters;
+    return take_dev_error();
+}
+
+// Profiling aid (IQ_DEC_STAMPS set): copies the last persistent step's barrier
+// exit times (ns since its start) into out[n], returns the count.
+IQ_API int iq_model_decode_stamps(iq_model *m, int64_t *out, int n) {
+    if (!m || !out || n < 1 || !m->dec_ready || !m->dec.stamps) return IQ_ERR_STATE;
+    unsigned long long h[1024];
+    IQ_CUDA(cudaStreamSynchronize(m->s));
+    IQ_CUDA(cudaMemcpy(h, m->dec.stamps, sizeof(h), cudaMemcpyDeviceToHost));
+    const int cnt = (int)std::min<unsigned long long>(h[0], std::min(n, 1022));
+    const unsigned long long mask = (1ull << 56) - 1;
+    for (int i = 0; i < cnt; i++) out[i] = (int64_t)(((h[2 + i] >> 56) << 56) | ((h[2 + i] & mask) - h[1]));
+    // slots 400.. / 700..: per matvec phase, the latest staging end / loop end over all warps
+    if (n >= 1024)
+        for (int i = 400; i < 1000; i++) out[i] = h[i] ? (int64_t)((h[i] & mask) - h[1]) : 0;
+    return cnt;
+}
+
+IQ_API int iq_model_decode_info(iq_model *m, int *persistent, int *grid) {
+    if (!m || !persistent || !grid) return IQ_ERR_ARG;
+    if (!model_ready(m)) return IQ_ERR_STATE;
+    IQ_CUDA(cudaSetDevice(m->dev));
+    int rc = dec_prepare(m);
+    if (rc) return rc;
+    *persistent = m->dec_ready && m->dec_mode ? 1 : 0;
+    *grid = *persistent ? m->dec_grid : 0;
     return IQ_OK;
 }
 

@@ -630,12 +630,18 @@ __device__ __noinline__ void flush_segment(i128 r0, i128 r1, int rt, int k0, int
 // order) with ring_depth<NP>() tiles in flight; the first D-1 are requested
 // before griddepcontrol.wait (weights are static), overlapping the previous
 // kernel's tail and the digit staging.
-template <int NP, bool XSMEM, bool BF = false>
-__global__ void __launch_bounds__(256, 2)
-k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const PackedRes R,
-                const int64_t *__restrict__ xg, int M, int N, int Kp, int add, RowAcc *__restrict__ racc,
-                const int64_t *__restrict__ nrm_w) {
-    extern __shared__ __align__(16) unsigned char xd[];  // [8][Kp + 16] digit rows
+// Profiling hook of the persistent decode kernel (defined there).
+__device__ __forceinline__ void mv_mark(int tag);
+
+// The stream-K matvec over warps gw of nwarps (the whole grid for a kernel
+// launch; a persistent kernel passes its own). xd: the CTA's digit staging
+// area. PDL: programmatic dependent launch (the first ring loads go out
+// before waiting for the previous kernel).
+template <int NP, bool XSMEM, bool BF, bool PDL>
+__device__ __forceinline__ void mv_stream(int64_t *__restrict__ out, const uint4 *__restrict__ planes,
+                                          const PackedRes &R, const int64_t *__restrict__ xg, int M, int N, int Kp,
+                                          int add, RowAcc *__restrict__ racc, const int64_t *__restrict__ nrm_w,
+                                          unsigned char *xd, int64_t gw, int64_t nwarps) {
     static_assert(!BF || XSMEM, "the bf16 form needs the staged activations (their sum)");
     constexpr int D = ring_depth<NP, BF>();
     constexpr int NL = tile_loads<NP, BF>();
@@ -643,22 +649,21 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
     const int ld = Kp + 16;
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int KT = Kp / 32, RT = (M + 15) / 16;
-    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-    const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int64_t total = (int64_t)RT * KT;
     const int64_t u0 = total * gw / nwarps, u1 = total * (gw + 1) / nwarps;
     // Programmatic dependent launch: let the next kernel in the stream start its
     // own prologue now; it waits (griddepcontrol.wait) for this grid's results.
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (PDL) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const uint4 *pl = planes + lane;
     uint4 buf[D][NL];
 #pragma unroll
     for (int s = 0; s < D - 1; s++)
         if (u0 + s < u1) load_tile<NL>(buf[s], pl + (size_t)(u0 + s) * TS);
     // x and (with add) out are produced by the previous kernel
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (PDL) asm volatile("griddepcontrol.wait;" ::: "memory");
     i128 xs = 0;
     if (XSMEM) stage_digits(xd, ld, xg, N, Kp, nrm_w, BF ? &xs : nullptr);
+    if (!PDL) mv_mark(6);
     const unsigned char *xb = xd + g * ld + 4 * t;
 
     int c[NP][4];
@@ -711,6 +716,19 @@ k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, con
         fold_planes(c, t, r0, r1);
         flush_segment(r0, r1, rt, k0, kt, KT, M, add, out, racc, R, XSMEM ? xd : nullptr, ld, xg, xs, g, t);
     }
+    if (!PDL) mv_mark(7);
+}
+
+
+template <int NP, bool XSMEM, bool BF = false>
+__global__ void __launch_bounds__(256, 2)
+k_matvec_planes(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const PackedRes R,
+                const int64_t *__restrict__ xg, int M, int N, int Kp, int add, RowAcc *__restrict__ racc,
+                const int64_t *__restrict__ nrm_w) {
+    extern __shared__ __align__(16) unsigned char xd[];  // [8][Kp + 16] digit rows
+    mv_stream<NP, XSMEM, BF, true>(out, planes, R, xg, M, N, Kp, add, racc, nrm_w, xd,
+                                   (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5),
+                                   (int64_t)gridDim.x * (blockDim.x >> 5));
 }
 
 // End of a row tile in k_matvec_rows (every thread of the CTA calls it): the

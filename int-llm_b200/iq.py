@@ -77,6 +77,10 @@ SIGNATURES = {
     "iq_decode_steps_timed": (_I, [_P, _I, _I, _P]),
     "iq_model_set_attention": (_I, [_P, _I]),
     "iq_model_weight_bytes": (_I, [_P, _P, _P]),
+    "iq_model_set_decode": (_I, [_P, _I]),
+    "iq_model_decode_info": (_I, [_P, _P, _P]),
+    "iq_bench_grid_sync": (_I, [_I, _I, _I, _P]),
+    "iq_model_decode_stamps": (_I, [_P, _P, _I]),
     "iq_tensor_seed": (ctypes.c_uint64, [_I, ctypes.c_char_p]),
     "iq_synth_weights": (_I, [ctypes.c_uint64, _P, _I64]),
     "iq_synth_acts": (_I, [ctypes.c_uint64, _P, _I64]),
@@ -434,6 +438,16 @@ class Model:
     def set_attention(self, short_max):
         """Contexts up to short_max use the single-kernel attention (0 = phased only)."""
         _call("iq_model_set_attention", self.h, short_max)
+
+    def set_decode(self, mode):
+        """1 = persistent decode kernel where it applies (default), 0 = one kernel per op."""
+        _call("iq_model_set_decode", self.h, mode)
+
+    def decode_info(self):
+        """(persistent kernel in use, its grid size)."""
+        a, b = ctypes.c_int(), ctypes.c_int()
+        _call("iq_model_decode_info", self.h, ctypes.byref(a), ctypes.byref(b))
+        return bool(a.value), b.value
 
     def weight_bytes(self):
         """(decode bytes per token, GEMM-form bytes) of this rank's stored weights."""

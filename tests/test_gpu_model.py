@@ -215,3 +215,52 @@ def test_cfg3_geometry_batched_decode_matches_reference_golden():
     got2 = m.generate_batch(prompts, g["max_new"])
     assert [t[g["prompt_len"]:] for t in got2] == g["tokens"]
     m.close()
+
+
+# ------------------------------------------------- persistent decode kernel
+
+def test_persistent_decode_kernel_matches_goldens():
+    """Decode mode 1 (one cooperative kernel per step, grid barriers between
+    phases) gives the reference's tokens and every-logit hash: the tiny model
+    (short-context attention, one CTA per head) and the 7B-geometry model from
+    position 370 on (contexts above 256: attention split over 64-position
+    tiles in three barrier-separated steps)."""
+    g = gold("tiny_model.json")
+    c, w, m = _load_model(g)
+    m.set_decode(1)
+    assert m.decode_info()[0]
+    toks, lh = m.generate(np.array(g["prompt"]), g["max_new"], logit_hash=True)
+    assert toks == g["tokens"] and lh == g["logit_hash"]
+    toks2, _ = m.generate(np.array(g["prompt"]), g["max_new"])
+    assert toks2 == g["tokens"]
+    assert iq.device_status() == 0
+    m.close()
+    g = gold("geom7b_model.json")
+    c, w, m = _load_model(g)
+    m.set_decode(1)
+    assert m.decode_info()[0]
+    prompt = orc.synth_tokens(g["cfg_index"], g["prompt_name"], g["prompt_len"], c["vocab"])
+    toks, lh = m.generate(prompt, g["max_new"], logit_hash=True)
+    assert toks[g["prompt_len"]:] == g["tokens"] and lh == g["logit_hash"]
+    assert iq.device_status() == 0
+    m.close()
+
+
+def test_persistent_decode_crosses_into_tiled_attention():
+    """A decode that starts below and ends above the 256-position switch of the
+    persistent kernel's attention equals the oracle, every logit hashed; and
+    mode 0 gives the same."""
+    c = dict(configs.TINY_TEST, n_layers=1, max_seq=300)
+    w = helpers.model_weights(9, c)
+    m = iq.Model(c)
+    m.load(w)
+    o = helpers.OracleModel(c, w)
+    pr = orc.synth_tokens(9, "prompt:cross", 240, c["vocab"])
+    want, wlh = o.generate(pr, 40)
+    for mode in (1, 0):
+        m.set_decode(mode)
+        assert m.decode_info()[0] == (mode == 1)
+        t1, h1 = m.generate(pr, 40, logit_hash=True)
+        t2, _ = m.generate(pr, 40)
+        assert t1 == t2 == want and h1 == wlh, mode
+    m.close(); o.close()
