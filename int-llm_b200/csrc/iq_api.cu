@@ -392,7 +392,12 @@ int launch_matvec_rows(int64_t *out, const Packed &P, const int64_t *x, cudaStre
     static const int waves = getenv("IQ_MV_ROWS_WAVES") ? atoi(getenv("IQ_MV_ROWS_WAVES")) : 2;
     if (RT > slots && (mode < 2 || RT > (int64_t)waves * slots)) return IQ_ERR_UNSUPPORTED;
     int S = 1;
-    while (S < 8 && (int64_t)RT * S * 2 <= slots && KT >= 2 * 8 * S * 2) S *= 2;
+    static const int s_env = getenv("IQ_MV_CLUSTER") ? atoi(getenv("IQ_MV_CLUSTER")) : 0;
+    if (s_env > 0) {   // forced cluster size (measurement aid)
+        while (S < s_env && (int64_t)RT * S * 2 <= 2 * slots) S *= 2;
+    } else {
+        while (S < 8 && (int64_t)RT * S * 2 <= slots && KT >= 2 * 8 * S * 2) S *= 2;
+    }
     const int64_t grid = RT > slots ? slots : (int64_t)RT * S;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
