@@ -646,8 +646,8 @@ int launch_gemm_tc(int64_t *out, const PackedTC &P, const int64_t *X, int R, cud
     if (rc) return rc;
     IQ_CUDA(cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
     const int ks = part ? gemm_ksplit(P, R) : 1;
-    dim3 grid(P.Mpad / TC_BM, Rpad / TC_BR, ks);
-    k_gemm_tc<<<grid, 192, TC_SMEM, s>>>(P.mapA, mapB, out, packed_res(P), X, P.K, P.M, R, P.Mpad, P.Kpad, add,
+    dim3 grid(Rpad / TC_BR, P.Mpad / TC_BM, ks);
+    k_gemm_tc<<<grid, TC_THREADS, TC_SMEM, s>>>(P.mapA, mapB, out, packed_res(P), X, P.K, P.M, R, P.Mpad, P.Kpad, add,
                                          part, Rpad, P.np);
     IQ_CHECK_LAUNCH();
     if (ks > 1) {

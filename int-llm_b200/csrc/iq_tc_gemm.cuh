@@ -15,17 +15,22 @@
 // ([(row, digit)][Kpad] bytes, K-major, row = 8*r + j), so the MMA's N
 // columns are (x-row, digit) pairs: N = 256 covers 32 x-rows.
 //
-// CTA tile: 128 output rows of W x 32 rows of X. Warp roles (192 threads):
-//   warp 0      TMA producer: for each plane p and 128-byte K block, loads A
-//               (128 x 128 B) and B (256 x 128 B) into a 4-stage ring;
-//   warp 1      owns TMEM (512 columns) and issues the MMAs from one thread:
-//               4 x (M=128, N=256, K=32) per stage into accumulator buffer p&1,
-//               committing each stage's smem back to the producer and each
-//               finished plane to the epilogue;
-//   warps 2..5  epilogue: per plane, read the 128 x 256 int32 tile from TMEM
-//               (warp w reads lanes 32*(w%4)..+31) and fold it into 32
-//               128-bit sums per thread (thread = one W row, 32 x-rows), then
-//               release the buffer; finally subtract 2^63*rowsum and store.
+// CTA tile: 128 output rows of W x 32 rows of X. Planes go in pairs
+// (2q, 2q+1) that share every staged digit tile: per pair and 128-byte K
+// block one stage holds A of both planes (2 x 128 x 128 B) and B (256 x 128 B),
+// 64 KB for 8 MMAs, against 48 KB for 4 when each plane re-staged the digits
+// (the GEMM was bound by delivering operands). Warp roles (320 threads):
+//   warp 0      TMA producer: 3-stage ring of pair stages;
+//   warp 1      owns TMEM (512 columns: one 256-column accumulator per plane
+//               of the pair) and issues the MMAs from one thread,
+//               4 x 2 x (M=128, N=256, K=32) per stage, committing each stage's
+//               smem back to the producer and each finished pair to the
+//               epilogue;
+//   warps 2..9  epilogue: per pair, read the two 128 x 256 int32 tiles from
+//               TMEM (warp w reads lanes 32*(w%4)..+31, half of the columns)
+//               and fold them into 16 128-bit sums per thread (thread = one W
+//               row, 16 x-rows), then release TMEM; finally subtract
+//               2^63*rowsum and store.
 // K per plane pass <= 32768 keeps every int32 partial exact (|u8*u8| <= 65025).
 #pragma once
 #include "iq_sync.cuh"
@@ -33,11 +38,14 @@
 
 namespace iq {
 
-constexpr int TC_BM = 128, TC_BR = 32, TC_BK = 128, TC_STAGES = 4;
-constexpr int TC_A_BYTES = TC_BM * TC_BK;            // 16 KB
+constexpr int TC_BM = 128, TC_BR = 32, TC_BK = 128, TC_STAGES = 3;
+constexpr int TC_A_BYTES = TC_BM * TC_BK;            // 16 KB per plane
 constexpr int TC_B_BYTES = TC_BR * 8 * TC_BK;        // 32 KB
-constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
+constexpr int TC_STAGE_BYTES = 2 * TC_A_BYTES + TC_B_BYTES;   // two planes share one digit tile
 constexpr size_t TC_SMEM = 1024 + (size_t)TC_STAGES * TC_STAGE_BYTES + 256;
+constexpr int TC_EPI_WARPS = 8;                          // 2 per TMEM lane quadrant
+constexpr int TC_THREADS = 32 * (2 + TC_EPI_WARPS);      // producer, MMA issuer, epilogue
+constexpr int TC_HR = TC_BR / 2;                         // x-rows per epilogue warp
 
 // W [M][K] int64 -> planes [np][Mpad][Kpad] bytes p0 .. p0+np-1 (zero padded; top plane signed)
 __global__ void k_pack_rowplanes(uint8_t *__restrict__ out, const int64_t *__restrict__ W, int M, int K,
@@ -62,7 +70,7 @@ __global__ void k_x_digits(uint8_t *__restrict__ out, const int64_t *__restrict_
     }
 }
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(TC_THREADS, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
           int64_t *__restrict__ out, const PackedRes res, const int64_t *__restrict__ X, int K, int M, int R,
           int Mpad, int Kpad, int add, int64_t *__restrict__ part, int Rpad, int np) {
@@ -77,15 +85,21 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUte
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(aempty + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * TC_BM, r0 = blockIdx.y * TC_BR;
+    // grid x walks the X-row tiles, so the CTAs resident together share one
+    // W tile (read once from HBM, then from L2) and the digit matrix stays in L2
+    const int m0 = blockIdx.y * TC_BM, r0 = blockIdx.x * TC_BR;
     // split-K: this CTA covers K blocks [kb0, kb0 + KB) of every plane
     const int KBall = Kpad / TC_BK, KS = gridDim.z, ks = blockIdx.z;
     const int kb0 = (int)((int64_t)KBall * ks / KS), KB = (int)((int64_t)KBall * (ks + 1) / KS) - kb0;
-    const int total = np * KB;
+
+    // planes are taken in pairs (2q, 2q+1) that share each staged digit tile
+    const int ngrp = (np + 1) / 2;
+    const int total = ngrp * KB;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < TC_STAGES; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        for (int b = 0; b < 2; b++) { mbar_init(&afull[b], 1); mbar_init(&aempty[b], 4); }
+        mbar_init(&afull[0], 1);
+        mbar_init(&aempty[0], TC_EPI_WARPS);
         fence_mbar_init();
     }
     if (warp == 1) tmem_alloc(tmem_slot, 512);
@@ -98,12 +112,15 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUte
         if (lane == 0) {
             int it = 0;
             for (; it < total; it++) {
-                const int p = it / KB, kb = it % KB, s = it % TC_STAGES;
+                const int q = it / KB, kb = it % KB, s = it % TC_STAGES;
+                const bool pair = 2 * q + 1 < np;
                 if (it >= TC_STAGES && !mbar_wait(&empty[s], (uint32_t)((it / TC_STAGES) - 1) & 1u)) break;
-                mbar_expect_tx(&full[s], TC_STAGE_BYTES);
+                mbar_expect_tx(&full[s], (pair ? 2 : 1) * TC_A_BYTES + TC_B_BYTES);
                 unsigned char *a = stage + (size_t)s * TC_STAGE_BYTES;
-                tma_load_2d(a, &mapA, (kb0 + kb) * TC_BK, p * Mpad + m0, &full[s]);
-                tma_load_2d(a + TC_A_BYTES, &mapB, (kb0 + kb) * TC_BK, r0 * 8, &full[s]);
+                const int kx = (kb0 + kb) * TC_BK;
+                tma_load_2d(a, &mapA, kx, (2 * q) * Mpad + m0, &full[s]);
+                if (pair) tma_load_2d(a + TC_A_BYTES, &mapA, kx, (2 * q + 1) * Mpad + m0, &full[s]);
+                tma_load_2d(a + 2 * TC_A_BYTES, &mapB, kx, r0 * 8, &full[s]);
             }
             // drain: the last copies into each stage have landed before the CTA can exit
             for (int j = (it > TC_STAGES ? it - TC_STAGES : 0); j < it; j++)
@@ -112,67 +129,76 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUte
     } else if (warp == 1) {
         if (lane == 0) {
             bool ok = true;
-            for (int p = 0; p < np && ok; p++) {
-                const int buf = p & 1;
-                if (p >= 2 && !mbar_wait(&aempty[buf], (uint32_t)((p / 2) - 1) & 1u)) break;
+            for (int q = 0; q < ngrp && ok; q++) {
+                const bool pair = 2 * q + 1 < np;
+                // the epilogue must have read the previous pair's accumulators
+                if (q >= 1 && !mbar_wait(&aempty[0], (uint32_t)(q - 1) & 1u)) break;
                 tc_fence_after();
-                const uint32_t idesc = idesc_i8(p == np - 1, false, TC_BM, TC_BR * 8);  // top plane signed
-                const uint32_t d = tmem + (uint32_t)(buf * 256);
+                const uint32_t id0 = idesc_i8(2 * q == np - 1, false, TC_BM, TC_BR * 8);  // top plane signed
+                const uint32_t id1 = idesc_i8(2 * q + 1 == np - 1, false, TC_BM, TC_BR * 8);
                 for (int kb = 0; kb < KB; kb++) {
-                    const int it = p * KB + kb, s = it % TC_STAGES;
+                    const int it = q * KB + kb, s = it % TC_STAGES;
                     if (!mbar_wait(&full[s], (uint32_t)(it / TC_STAGES) & 1u)) { ok = false; break; }
                     tc_fence_after();
                     const unsigned char *a = stage + (size_t)s * TC_STAGE_BYTES;
-                    const uint64_t ad = smem_desc_sw128(a), bd = smem_desc_sw128(a + TC_A_BYTES);
+                    const uint64_t a0 = smem_desc_sw128(a), a1 = smem_desc_sw128(a + TC_A_BYTES),
+                                   bd = smem_desc_sw128(a + 2 * TC_A_BYTES);
 #pragma unroll
-                    for (int k = 0; k < TC_BK / 32; k++)  // advance 32 bytes of K = 2 descriptor units
-                        tc_mma_i8(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+                    for (int k = 0; k < TC_BK / 32; k++) {  // advance 32 bytes of K = 2 descriptor units
+                        tc_mma_i8(tmem, a0 + 2 * k, bd + 2 * k, id0, (kb | k) != 0);
+                        if (pair) tc_mma_i8(tmem + 256u, a1 + 2 * k, bd + 2 * k, id1, (kb | k) != 0);
+                    }
                     tc_commit(&empty[s]);
                 }
-                if (ok) tc_commit(&afull[buf]);
+                if (ok) tc_commit(&afull[0]);
             }
         }
     } else {
-        // epilogue warps: TMEM lane quadrant = warp % 4
-        const int quad = warp & 3;
+        // epilogue warps: TMEM lane quadrant = warp % 4; the two warps of a
+        // quadrant take x-rows 0..15 and 16..31 (columns 0..127 / 128..255)
+        const int quad = warp & 3, half = (warp - 2) >> 2;
         const int row = m0 + quad * 32 + lane;
-        i128 acc[TC_BR];
+        const int rb = r0 + half * TC_HR;   // this warp's first x-row
+        i128 acc[TC_HR];
 #pragma unroll
-        for (int r = 0; r < TC_BR; r++) acc[r] = 0;
+        for (int r = 0; r < TC_HR; r++) acc[r] = 0;
         bool ok = true;
-        for (int p = 0; p < np && ok; p++) {
-            const int buf = p & 1;
-            if (!mbar_wait(&afull[buf], (uint32_t)(p / 2) & 1u)) { ok = false; break; }
+        for (int q = 0; q < ngrp && ok; q++) {
+            if (!mbar_wait(&afull[0], (uint32_t)q & 1u)) { ok = false; break; }
             tc_fence_after();
+            for (int h = 0; h < 2; h++) {
+                const int p = 2 * q + h;
+                if (p >= np) break;
 #pragma unroll
-            for (int c = 0; c < 8; c++) {  // 32 columns = 4 x-rows x 8 digits
-                uint32_t v[32];
-                tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * 256 + c * 32), v);
-                tmem_ld_wait();
-                // digits 0..3 and 4..7 of one x-row each sum exactly in 64 bits
-                // (|v| < 2^31, shifts <= 24: < 2^57), then one 128-bit
-                // shift-add per x-row: sum_j v_j 2^(8(p0+p+j))
-                const int sh = 8 * (res.p0 + p);
+                for (int c = 0; c < 4; c++) {  // 32 columns = 4 x-rows x 8 digits
+                    uint32_t v[32];
+                    tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(h * 256 + half * 128 + c * 32), v);
+                    tmem_ld_wait();
+                    // digits 0..3 and 4..7 of one x-row each sum exactly in 64 bits
+                    // (|v| < 2^31, shifts <= 24: < 2^57), then one 128-bit
+                    // shift-add per x-row: sum_j v_j 2^(8(p0+p+j))
+                    const int sh = 8 * (res.p0 + p);
 #pragma unroll
-                for (int rr = 0; rr < 4; rr++) {
-                    int64_t lo = 0, hi = 0;
+                    for (int rr = 0; rr < 4; rr++) {
+                        int64_t lo = 0, hi = 0;
 #pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        lo += (int64_t)(int32_t)v[rr * 8 + j] * (1ll << (8 * j));
-                        hi += (int64_t)(int32_t)v[rr * 8 + 4 + j] * (1ll << (8 * j));
+                        for (int j = 0; j < 4; j++) {
+                            lo += (int64_t)(int32_t)v[rr * 8 + j] * (1ll << (8 * j));
+                            hi += (int64_t)(int32_t)v[rr * 8 + 4 + j] * (1ll << (8 * j));
+                        }
+                        acc[4 * c + rr] += (i128)((u128)((i128)lo + (i128)((u128)(i128)hi << 32)) << sh);
                     }
-                    acc[4 * c + rr] += (i128)((u128)((i128)lo + (i128)((u128)(i128)hi << 32)) << sh);
                 }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&aempty[buf]);
+            if (lane == 0) mbar_arrive(&aempty[0]);
         }
         if (ok && KS > 1) {
             // split-K: store this CTA's 128-bit partial sums; k_gemm_reduce finishes
 #pragma unroll
-            for (int r = 0; r < TC_BR; r++) {
-                int64_t *pp = part + (((size_t)ks * Rpad + r0 + r) * Mpad + row) * 2;
+            for (int r = 0; r < TC_HR; r++) {
+                int64_t *pp = part + (((size_t)ks * Rpad + rb + r) * Mpad + row) * 2;
                 pp[0] = (int64_t)(uint64_t)acc[r];
                 pp[1] = (int64_t)(uint64_t)((u128)acc[r] >> 64);
             }
@@ -183,17 +209,17 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUte
                     const int k = res.col[e];
                     const int64_t wl = res.val[e];
 #pragma unroll
-                    for (int r = 0; r < TC_BR; r++)
-                        if (r0 + r < R) acc[r] += mul_wide(X[(size_t)(r0 + r) * K + k], wl);
+                    for (int r = 0; r < TC_HR; r++)
+                        if (rb + r < R) acc[r] += mul_wide(X[(size_t)(rb + r) * K + k], wl);
                 }
             }
             const i128 ws = (i128)(((u128)(uint64_t)rowsum[2 * row + 1] << 64) | (uint64_t)rowsum[2 * row]);
             const u128 bias = (u128)ws << 63;
 #pragma unroll
-            for (int r = 0; r < TC_BR; r++) {
-                if (r0 + r < R) {
+            for (int r = 0; r < TC_HR; r++) {
+                if (rb + r < R) {
                     int64_t v = (int64_t)((i128)((u128)acc[r] - bias) >> 48);
-                    int64_t *o = out + (size_t)(r0 + r) * M + row;
+                    int64_t *o = out + (size_t)(rb + r) * M + row;
                     *o = add ? (int64_t)((uint64_t)*o + (uint64_t)v) : v;  // fused residual add
                 }
             }
