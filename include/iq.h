@@ -310,6 +310,19 @@ IQ_API int iq_model_set_attention(iq_model *m, int short_max);
  * default. iq_model_decode_info reports whether the persistent kernel is in
  * use and its grid size. */
 IQ_API int iq_model_set_decode(iq_model *m, int mode);
+
+/* Bounded host waits under tensor parallelism (no reference counterpart; the
+ * reference has no collectives). Every host wait of a multi-GPU model polls
+ * its stream together with NCCL's asynchronous error state; a communicator
+ * error returns IQ_ERR_NCCL, and a step that does not finish within the
+ * timeout (default 60 s: a peer rank that died or stopped calling) returns
+ * IQ_ERR_TIMEOUT. Both abort the communicator (ncclCommAbort), which ends the
+ * pending collectives; the model is then unusable (IQ_ERR_STATE) and must be
+ * destroyed. iq_selftest_watchdog runs that wait logic on scripted events
+ * without a GPU (scenario 0: completes; 1: communicator error; 2: never
+ * completes; 3: stream error) and reports whether it aborted. */
+IQ_API int iq_model_set_timeout(iq_model *m, int64_t ms);
+IQ_API int iq_selftest_watchdog(int scenario, int *aborted, int *polls);
 IQ_API int iq_model_decode_info(iq_model *m, int *persistent, int *grid);
 /* Diagnostics of the persistent kernel: microseconds per grid barrier with
  * `grid` CTAs (mode 0); and, with IQ_DEC_STAMPS set in the environment when

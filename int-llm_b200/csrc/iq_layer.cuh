@@ -421,6 +421,59 @@ __global__ void k_argmax(int *__restrict__ result, const int64_t *__restrict__ l
     }
 }
 
+// Tensor-parallel decode: the first maximum of this rank's logit rows
+// [row][v_l] (columns v_lo .. v_lo + v_l - 1 of the vocabulary) as a
+// (value, global index) pair per row, one CTA per row. The pairs of all ranks
+// are then all-gathered (16 bytes per row and rank instead of the logits).
+__global__ void k_argmax_local(int64_t *__restrict__ pairs, const int64_t *__restrict__ logits, int v_l, int v_lo) {
+    __shared__ int64_t bv[32];
+    __shared__ int bi[32];
+    const int b = blockIdx.x;
+    const int64_t *lg = logits + (size_t)b * v_l;
+    int64_t best = INT64_MIN;
+    int idx = 0x7fffffff;
+    for (int i = threadIdx.x; i < v_l; i += blockDim.x) {
+        const int64_t v = lg[i];
+        if (v > best) { best = v; idx = i; }
+    }
+    for (int m = 16; m >= 1; m >>= 1) {
+        const int64_t ov = __shfl_xor_sync(0xffffffffu, best, m);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, m);
+        if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
+    }
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) { bv[w] = best; bi[w] = idx; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 0; k < (int)(blockDim.x >> 5); k++)
+            if (bv[k] > best || (bv[k] == best && bi[k] < idx)) { best = bv[k]; idx = bi[k]; }
+        pairs[2 * b] = best;
+        pairs[2 * b + 1] = (int64_t)v_lo + idx;
+    }
+}
+
+// The global first maximum from the gathered pairs g [P][B][2] (rank p holds
+// the lower vocabulary block when p is lower, so among equal values the lowest
+// index wins, llama_int.c:2888-2893), then the decode-state update of k_argmax.
+__global__ void k_argmax_pairs(int *__restrict__ result, const int64_t *__restrict__ g, int P, int B,
+                               int *__restrict__ tokens, int *__restrict__ pos_arr, int *__restrict__ hist,
+                               int hist_stride) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    int64_t best = INT64_MIN, idx = INT64_MAX;
+    for (int p = 0; p < P; p++) {
+        const int64_t v = g[((size_t)p * B + b) * 2], i = g[((size_t)p * B + b) * 2 + 1];
+        if (v > best || (v == best && i < idx)) { best = v; idx = i; }
+    }
+    result[b] = (int)idx;
+    if (tokens) tokens[b] = (int)idx;
+    if (pos_arr) {
+        const int np1 = pos_arr[b] + 1;
+        if (hist) hist[(size_t)b * hist_stride + np1] = (int)idx;
+        pos_arr[b] = np1;
+    }
+}
+
 // After a prefill: the argmax of the sequence's last prompt row becomes its
 // next token at position L, recorded in the history (llama_int.c:3087-3089).
 __global__ void k_prefill_done(const int *__restrict__ arg, int *__restrict__ tokens, int *__restrict__ pos_arr,

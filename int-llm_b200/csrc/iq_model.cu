@@ -22,6 +22,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <vector>
+#include <chrono>
 #include <nccl.h>
 #include "iq_common.cuh"
 #include "iq_layer.cuh"
@@ -107,6 +108,10 @@ struct iq_model {
     std::vector<bool> loaded_layer;
     // persistent decode kernel (k_decode_token) for batch 1 without tensor
     // parallelism: requested mode, and its state once prepared
+    bool failed = false;        // the communicator was aborted: the model is unusable
+    int64_t timeout_ms = 60000; // bounded host waits under tensor parallelism
+    bool want_logits = false;   // decode steps also gather the full logits (TP; hashing callers)
+    int64_t *pairs_l = nullptr, *pairs_g = nullptr;   // TP argmax: local pair, gathered pairs
     int dec_mode = 0;           // 1 = use it where it applies, 0 = per-kernel path (default: faster today)
     bool dec_ready = false;     // prepared for the current weights
     DecParams dec{};
@@ -216,6 +221,8 @@ static int model_alloc(iq_model *m) {
         DALLOC(m->logits_l, (size_t)B * S.v_l * 8);
         DALLOC(m->gath, (size_t)B * wmax * 8);
         DALLOC(m->proj_full, (size_t)B * d * 8);
+        DALLOC(m->pairs_l, (size_t)B * 2 * 8);
+        DALLOC(m->pairs_g, (size_t)S.P * B * 2 * 8);
     }
     const int NB = m->max_batch;
     DALLOC(m->d_tok, (size_t)NB * 4);
@@ -386,6 +393,16 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
     const int64_t *fin = m->hidden + (size_t)(R - LR) * d;   // the rows the LM head reads
     if (tp) {
         if ((rc = norm_proj(m->logits_l, m->plm, m->tlm, fin, m->fnorm, LR))) return rc;
+        if (decode && !m->want_logits) {
+            // sharded argmax: each rank's first maximum, then (value, index) pairs
+            k_argmax_local<<<LR, 1024, 0, s>>>(m->pairs_l, m->logits_l, S.v_l, S.r * S.v_l);
+            IQ_CHECK_LAUNCH();
+            IQ_NCCL(ncclAllGather(m->pairs_l, m->pairs_g, (size_t)LR * 2, ncclInt64, m->comm, s));
+            k_argmax_pairs<<<(LR + 127) / 128, 128, 0, s>>>(m->d_arg, m->pairs_g, S.P, LR, m->d_tok, m->d_pos,
+                                                          m->d_hist, c.max_seq_len + 1);
+            IQ_CHECK_LAUNCH();
+            return IQ_OK;
+        }
         if ((rc = gather_rows(m, m->logits_l, m->logits, LR, S.v_l))) return rc;
     } else if ((rc = norm_proj(m->logits, m->plm, m->tlm, fin, m->fnorm, LR))) {
         return rc;
@@ -398,6 +415,77 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
                                     nullptr, nullptr, nullptr, 0);
     }
     IQ_CHECK_LAUNCH();
+    return IQ_OK;
+}
+
+static void invalidate_exec(iq_model *m);
+
+static int64_t ms_now() {
+    return std::chrono::duration_cast<std::chrono::milliseconds>(
+               std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+// Bounded wait: polls done() (1 finished, 0 pending, < 0 failed) and
+// async_err() (a communicator error) until done, calling abort() on an
+// asynchronous error or after timeout_ms without completion. Pure host logic
+// (the callables are the CUDA / NCCL queries), so it is testable without a
+// GPU (iq_selftest_watchdog).
+template <class Done, class AsyncErr, class Abort, class Now>
+static int watch_wait(Done done, AsyncErr async_err, Abort abort, Now now_ms, int64_t timeout_ms, int *polls) {
+    const int64_t t0 = now_ms();
+    for (int n = 1;; n++) {
+        if (polls) *polls = n;
+        const int d = done();
+        if (d > 0) return IQ_OK;
+        if (d < 0) return IQ_ERR_CUDA;
+        if (async_err()) { abort(); return IQ_ERR_NCCL; }
+        if (now_ms() - t0 > timeout_ms) { abort(); return IQ_ERR_TIMEOUT; }
+        if (n > 64) std::this_thread::yield();
+    }
+}
+
+// Host wait for the model's stream. Without tensor parallelism a plain
+// synchronise. With it, a peer that stopped posting its half of a collective
+// would block the NCCL kernels (and a plain synchronise) forever: the stream is
+// polled together with NCCL's asynchronous error state, and an error or a wait
+// beyond the model's timeout aborts the communicator (ncclCommAbort), which
+// ends the pending collectives; the model is then marked failed and every
+// later call returns IQ_ERR_STATE.
+static int wait_stream(iq_model *m) {
+    if (m->failed) return IQ_ERR_STATE;
+    if (m->sh.P == 1 || !m->comm) {
+        IQ_CUDA(cudaStreamSynchronize(m->s));
+        return IQ_OK;
+    }
+    return watch_wait(
+        [&]() {
+            const cudaError_t e = cudaStreamQuery(m->s);
+            if (e == cudaSuccess) return 1;
+            if (e == cudaErrorNotReady) return 0;
+            cuda_fail(e);
+            return -1;
+        },
+        [&]() {
+            ncclResult_t r = ncclSuccess;
+            if (ncclCommGetAsyncError(m->comm, &r) != ncclSuccess) return true;
+            return r != ncclSuccess && r != ncclInProgress;
+        },
+        [&]() {
+            ncclCommAbort(m->comm);
+            m->comm = nullptr;
+            m->failed = true;
+        },
+        ms_now, m->timeout_ms, nullptr);
+}
+#define IQ_WAIT(m) do { int _w = wait_stream(m); if (_w) return _w; } while (0)
+
+// Whether decode steps must leave the full logits in m->logits (only hashing
+// callers need them under tensor parallelism; otherwise ranks exchange argmax
+// pairs). Captured step graphs bake the choice in, so a change drops them.
+static int set_want_logits(iq_model *m, bool want) {
+    if (m->sh.P == 1 || m->want_logits == want) return IQ_OK;
+    invalidate_exec(m);
+    m->want_logits = want;
     return IQ_OK;
 }
 
@@ -510,7 +598,7 @@ static int ensure_graph(iq_model *m, int tmax) {
 }
 
 static bool model_ready(iq_model *m) {
-    if (!m || !m->loaded_globals) return false;
+    if (!m || !m->loaded_globals || m->failed) return false;
     for (bool b : m->loaded_layer) if (!b) return false;
     return true;
 }
@@ -751,7 +839,7 @@ IQ_API int iq_model_destroy(iq_model *m) {
     void *bufs[] = {m->embed, m->fnorm, m->lm, m->rcos, m->rsin, m->hidden, m->normed, m->qkv, m->att,
                     m->gu, m->act, m->logits, m->att_l, m->proj_l, m->act_l, m->logits_l, m->gath,
                     m->proj_full, m->d_tok, m->d_pos, m->d_arg, m->d_hist, m->racc, m->digits, m->gpart, m->asc, m->amx, m->asum, m->d_seq,
-                    m->d_ptok, m->d_ppos, m->d_pseq, m->d_layers, m->bar, m->argv};
+                    m->d_ptok, m->d_ppos, m->d_pseq, m->d_layers, m->bar, m->argv, m->pairs_l, m->pairs_g};
     for (void *p : bufs) if (p) cudaFree(p);
     for (auto *v : {&m->norm1, &m->wqkv, &m->wo, &m->norm2, &m->wgu, &m->wdown, &m->kc, &m->vc})
         for (int64_t *p : *v) if (p) cudaFree(p);
@@ -896,7 +984,7 @@ static int enqueue_prefill(iq_model *m, int sq, const int *prompt, int L, std::v
             IQ_CUDA(cudaMemcpyAsync(hv->data() + old, m->logits, cnt * 8, cudaMemcpyDeviceToHost, m->s));
         }
         // the pinned row arrays are reused by the next chunk only after these copies ran
-        IQ_CUDA(cudaStreamSynchronize(m->s));
+        IQ_WAIT(m);
     }
     k_prefill_done<<<1, 32, 0, m->s>>>(m->d_arg, m->d_tok, m->d_pos, m->d_hist, m->c.max_seq_len + 1, sq, L);
     IQ_CHECK_LAUNCH();
@@ -907,7 +995,7 @@ IQ_API int iq_forward(iq_model *m, int token, int pos, int64_t *logits, int *arg
     if (!model_ready(m)) return m ? IQ_ERR_STATE : IQ_ERR_ARG;
     if (token < 0 || token >= m->c.vocab_size || pos < 0 || pos >= m->c.max_seq_len) return IQ_ERR_RANGE;
     IQ_CUDA(cudaSetDevice(m->dev));
-    IQ_CUDA(cudaStreamSynchronize(m->s));
+    IQ_WAIT(m);
     int rc;
     int *h = m->h_rows;
     h[0] = token; h[1] = pos; h[2] = 0;
@@ -917,7 +1005,7 @@ IQ_API int iq_forward(iq_model *m, int token, int pos, int64_t *logits, int *arg
     if ((rc = enqueue_rows(m, 1, m->d_ptok, m->d_ppos, m->d_pseq, 0, 0, pos + 1))) return rc;
     if (logits) IQ_CUDA(cudaMemcpyAsync(m->h_logits, m->logits, (size_t)m->c.vocab_size * 8, cudaMemcpyDeviceToHost, m->s));
     IQ_CUDA(cudaMemcpyAsync(m->h_pin, m->d_arg, 4, cudaMemcpyDeviceToHost, m->s));
-    IQ_CUDA(cudaStreamSynchronize(m->s));
+    IQ_WAIT(m);
     if (logits) memcpy(logits, m->h_logits, (size_t)m->c.vocab_size * 8);
     if (argmax_out) *argmax_out = m->h_pin[0];
     return take_dev_error();
@@ -957,6 +1045,7 @@ IQ_API int iq_generate(iq_model *m, const int *prompt, int plen, int max_new, in
     const bool hash = logit_hash != nullptr;
     const int V = c.vocab_size;
     uint64_t h = 1469598103934665603ULL;
+    if ((rc = set_want_logits(m, hash))) return rc;
     memcpy(out, prompt, (size_t)plen * sizeof(int));
     // prefill: every prompt position in batched rows (== the M=1 loop of llama_int.c:3081-3092)
     std::vector<int64_t> hv;
@@ -967,13 +1056,13 @@ IQ_API int iq_generate(iq_model *m, const int *prompt, int plen, int max_new, in
     const int steps = std::min(max_new - 1, c.max_seq_len - plen);
     if (hash) {
         IQ_CUDA(cudaMemcpyAsync(m->h_pin, m->d_tok, 4, cudaMemcpyDeviceToHost, m->s));
-        IQ_CUDA(cudaStreamSynchronize(m->s));
+        IQ_WAIT(m);
         out[total++] = m->h_pin[0];  // prefill's sample is appended unconditionally
         for (int i = 1; i <= steps; i++) {
             if ((rc = run_step(m, 1, plen + i))) return rc;  // d_tok / d_pos advanced on the device
             IQ_CUDA(cudaMemcpyAsync(m->h_logits, m->logits, (size_t)V * 8, cudaMemcpyDeviceToHost, m->s));
             IQ_CUDA(cudaMemcpyAsync(m->h_pin, m->d_arg, 4, cudaMemcpyDeviceToHost, m->s));
-            IQ_CUDA(cudaStreamSynchronize(m->s));
+            IQ_WAIT(m);
             h = fnv_mix(h, m->h_logits, V);
             const int nx = m->h_pin[0];
             if (nx == 2) break;  // LLAMA_EOS (llama_int.c:3046, 3110)
@@ -985,7 +1074,7 @@ IQ_API int iq_generate(iq_model *m, const int *prompt, int plen, int max_new, in
             if ((rc = run_step(m, 1, plen + i))) return rc;
         std::vector<int> hist(steps + 1);
         IQ_CUDA(cudaMemcpyAsync(hist.data(), m->d_hist + plen, (size_t)(steps + 1) * 4, cudaMemcpyDeviceToHost, m->s));
-        IQ_CUDA(cudaStreamSynchronize(m->s));
+        IQ_WAIT(m);
         out[total++] = hist[0];
         for (int i = 1; i <= steps; i++) {
             if (hist[i] == 2) break;
@@ -1010,6 +1099,7 @@ IQ_API int iq_generate_batch(iq_model *m, const int *prompts, int plen, int max_
     const bool hash = logit_hashes != nullptr;
     const int V = c.vocab_size;
     std::vector<int64_t> hv;
+    if ((rc = set_want_logits(m, hash))) return rc;
     for (int b = 0; b < B; b++) {  // each sequence's prompt as batched rows
         if ((rc = enqueue_prefill(m, b, prompts + (size_t)b * plen, plen, hash ? &hv : nullptr))) return rc;
         if (hash) {
@@ -1028,7 +1118,7 @@ IQ_API int iq_generate_batch(iq_model *m, const int *prompts, int plen, int max_
         // including) the step that samples EOS, as the reference's loop forwards
         IQ_CUDA(cudaMemcpyAsync(lg.data(), m->logits, lg.size() * 8, cudaMemcpyDeviceToHost, m->s));
         IQ_CUDA(cudaMemcpyAsync(argm.data(), m->d_arg, (size_t)B * 4, cudaMemcpyDeviceToHost, m->s));
-        IQ_CUDA(cudaStreamSynchronize(m->s));
+        IQ_WAIT(m);
         for (int b = 0; b < B; b++) {
             if (!live[b]) continue;
             logit_hashes[b] = fnv_mix(logit_hashes[b], lg.data() + (size_t)b * V, V);
@@ -1038,7 +1128,7 @@ IQ_API int iq_generate_batch(iq_model *m, const int *prompts, int plen, int max_
     const int stride = c.max_seq_len + 1;
     std::vector<int> hist((size_t)B * stride);
     IQ_CUDA(cudaMemcpyAsync(hist.data(), m->d_hist, hist.size() * 4, cudaMemcpyDeviceToHost, m->s));
-    IQ_CUDA(cudaStreamSynchronize(m->s));
+    IQ_WAIT(m);
     const int ow = plen + max_new;
     for (int b = 0; b < B; b++) {
         int *o = out + (size_t)b * ow;
@@ -1063,6 +1153,28 @@ IQ_API int iq_model_set_attention(iq_model *m, int short_max) {
     if (m->graph_s) { cudaGraphExecDestroy(m->graph_s); m->graph_s = nullptr; }
     m->att_short = short_max;
     return IQ_OK;
+}
+
+IQ_API int iq_model_set_timeout(iq_model *m, int64_t ms) {
+    if (!m || ms < 1) return IQ_ERR_ARG;
+    m->timeout_ms = ms;
+    return IQ_OK;
+}
+
+// The bounded-wait logic of tensor-parallel steps on scripted events (no GPU):
+// scenario 0 completes at the third poll; 1 reports a communicator error at
+// the second; 2 never completes (a simulated clock advances 10 ms per poll,
+// limit 100 ms); 3 fails the stream query.
+IQ_API int iq_selftest_watchdog(int scenario, int *aborted, int *polls) {
+    if (!aborted || !polls || scenario < 0 || scenario > 3) return IQ_ERR_ARG;
+    int n = 0;
+    int64_t clock = 0;
+    *aborted = 0;
+    return watch_wait(
+        [&]() { n++; return scenario == 3 ? -1 : (scenario == 0 && n >= 3) ? 1 : 0; },
+        [&]() { return scenario == 1 && n >= 2; },
+        [&]() { (*aborted)++; },
+        [&]() { clock += 10; return clock; }, 100, polls);
 }
 
 IQ_API int iq_model_set_decode(iq_model *m, int mode) {
@@ -1157,7 +1269,7 @@ IQ_API int iq_decode_steps_timed(iq_model *m, int pos0, int steps, float *ms) {
     IQ_CUDA(cudaSetDevice(m->dev));
     int rc;
     std::vector<int> tok(m->max_batch), pos(m->max_batch, pos0);
-    IQ_CUDA(cudaStreamSynchronize(m->s));
+    IQ_WAIT(m);
     IQ_CUDA(cudaMemcpy(tok.data(), m->d_tok, tok.size() * 4, cudaMemcpyDeviceToHost));
     if ((rc = set_tok_pos(m, tok.data(), pos.data(), m->max_batch, 0))) return rc;
     if ((rc = ensure_graph(m, pos0 + 1)) || (rc = ensure_graph(m, pos0 + steps))) return rc;
@@ -1167,7 +1279,7 @@ IQ_API int iq_decode_steps_timed(iq_model *m, int pos0, int steps, float *ms) {
     IQ_CUDA(cudaEventRecord(e0, m->s));
     for (int i = 0; i < steps; i++) IQ_CUDA(cudaGraphLaunch(step_graph(m, pos0 + i + 1), m->s));
     IQ_CUDA(cudaEventRecord(e1, m->s));
-    IQ_CUDA(cudaEventSynchronize(e1));
+    IQ_WAIT(m);
     IQ_CUDA(cudaEventElapsedTime(ms, e0, e1));
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);

@@ -78,6 +78,8 @@ SIGNATURES = {
     "iq_model_set_attention": (_I, [_P, _I]),
     "iq_model_weight_bytes": (_I, [_P, _P, _P]),
     "iq_model_set_decode": (_I, [_P, _I]),
+    "iq_model_set_timeout": (_I, [_P, _I64]),
+    "iq_selftest_watchdog": (_I, [_I, _P, _P]),
     "iq_model_decode_info": (_I, [_P, _P, _P]),
     "iq_bench_grid_sync": (_I, [_I, _I, _I, _P]),
     "iq_model_decode_stamps": (_I, [_P, _P, _I]),

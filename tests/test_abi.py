@@ -66,3 +66,21 @@ def test_synth_generator_matches_oracle():
     L = iq.lib()
     for b in range(0, 65536, 5):
         assert L.iq_bf16_to_q1648(b) == orc.O.iqo_bf16_to_q1648(b)
+
+
+def test_watchdog_logic_without_gpu():
+    """The bounded wait of tensor-parallel steps (iq_selftest_watchdog runs the
+    library's own wait loop on scripted events): completion returns IQ_OK
+    without abort; a communicator error returns IQ_ERR_NCCL and aborts; a step
+    that never completes times out (IQ_ERR_TIMEOUT) and aborts; a failed stream
+    query is a CUDA error."""
+    L = iq.lib()
+    ab, polls = ctypes.c_int(), ctypes.c_int()
+    assert L.iq_selftest_watchdog(0, ctypes.byref(ab), ctypes.byref(polls)) == 0
+    assert ab.value == 0 and polls.value == 3
+    assert L.iq_selftest_watchdog(1, ctypes.byref(ab), ctypes.byref(polls)) == -4
+    assert ab.value == 1 and polls.value == 2
+    assert L.iq_selftest_watchdog(2, ctypes.byref(ab), ctypes.byref(polls)) == -5
+    assert ab.value == 1 and polls.value == 11   # 10 ms per poll, limit 100 ms
+    assert L.iq_selftest_watchdog(3, ctypes.byref(ab), ctypes.byref(polls)) == -2
+    assert ab.value == 0
