@@ -167,6 +167,17 @@ IQ_API int iq_packed_tc_free(iq_packed_tc *p);
 IQ_API int iq_packed_tc_info(const iq_packed_tc *p, int *np, int *p0, int *residual_entries);
 IQ_API int iq_gemm_tc_dev(int64_t *d_out, const iq_packed_tc *w, const int64_t *d_X, int rows, void *stream);
 
+/* sample_token (llama_int.c:2958-3039) on the device for each row of
+ * d_logits [rows][V]: temperature (Q16.48; below 0.01 the argmax), top-k (0 =
+ * off), top-p (Q16.48; 0 or >= 1.0 = off), then a draw from the row's
+ * xoroshiro128+ state rng [rows][2] (host, advanced in place exactly as the
+ * reference advances sample_params_t.rng). out [rows] (host) receives the
+ * token ids, identical to the reference's. */
+IQ_API int iq_sample_dev(const int64_t *d_logits, int rows, int V, int64_t temperature, int top_k, int64_t top_p,
+                         uint64_t *rng, int *out);
+/* rng_seed (llama_int.c:2909-2919): SplitMix64 seeding of a state {s0, s1}. */
+IQ_API int iq_rng_seed(uint64_t seed, uint64_t state[2]);
+
 /* Synchronises the current device and returns (and clears) the status that
  * kernels with bounded waits record: IQ_OK or IQ_ERR_TIMEOUT. */
 IQ_API int iq_device_status(void);
@@ -276,6 +287,17 @@ IQ_API int iq_forward(iq_model *m, int token, int pos, int64_t *logits, int *arg
  * step). */
 IQ_API int iq_generate(iq_model *m, const int *prompt, int prompt_len, int max_new,
                        int *out_tokens, int *n_out, uint64_t *logit_hash);
+
+/* generate() with sampling parameters (llama_int.c:3067-3135 with a
+ * sample_params_t): temperature and top_p in Q16.48 (the values the reference
+ * holds after parsing its CLI floats), top_k (0 = off), and the generator seed
+ * (rng_seed once per call, llama_int.c:2909-2919). Every sample -- the one at
+ * the end of the prompt and each decode step's -- is sample_token
+ * (llama_int.c:2958-3039) computed on the device; tokens equal the
+ * reference's. Other arguments as iq_generate. */
+IQ_API int iq_generate_sampled(iq_model *m, const int *prompt, int prompt_len, int max_new, int64_t temperature,
+                               int top_k, int64_t top_p, uint64_t seed, int *out_tokens, int *n_out,
+                               uint64_t *logit_hash);
 
 /* Batched greedy decode of B = max_batch independent sequences in lockstep
  * (the reference runs each sequence alone; rows are independent, so results

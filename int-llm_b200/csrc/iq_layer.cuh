@@ -474,6 +474,209 @@ __global__ void k_argmax_pairs(int *__restrict__ result, const int64_t *__restri
     }
 }
 
+// ---------------------------------------------------------------- sampling
+
+// Sampling parameters and generator state of one sequence (sample_params_t,
+// llama_int.c:2936-2941; the xoroshiro128+ state of rng_state_t).
+struct SampleState {
+    int64_t temperature;  // Q16.48; below 0.01 (FP_ONE / 100) the argmax is taken
+    int64_t top_p;        // Q16.48; 0 or >= FP_ONE: off
+    int top_k, pad;       // 0 or >= vocab: off
+    uint64_t s0, s1;      // generator state, advanced once per sampled token
+};
+
+#define IQ_SAMPLE_THREADS 1024
+
+// First maximum of v[0..n) (strict >, lowest index among equals) over the CTA.
+__device__ int cta_argmax(const int64_t *v, int n) {
+    __shared__ int64_t bv[32];
+    __shared__ int bi[32];
+    int64_t best = INT64_MIN;
+    int idx = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+        if (v[i] > best) { best = v[i]; idx = i; }
+    for (int m = 16; m >= 1; m >>= 1) {
+        const int64_t ov = __shfl_xor_sync(0xffffffffu, best, m);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, m);
+        if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
+    }
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) { bv[threadIdx.x >> 5] = best; bi[threadIdx.x >> 5] = idx; }
+    __syncthreads();
+    for (int k = 0; k < (int)(blockDim.x >> 5); k++)
+        if (bv[k] > best || (bv[k] == best && bi[k] < idx)) { best = bv[k]; idx = bi[k]; }
+    __syncthreads();
+    return idx;
+}
+
+// CTA-wide exclusive prefix sum of one uint64 per thread (thread order).
+__device__ uint64_t cta_exclusive_scan(uint64_t v, uint64_t *total) {
+    __shared__ uint64_t ws[32];
+    const int l = threadIdx.x & 31, w = threadIdx.x >> 5;
+    uint64_t x = v;
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint64_t y = __shfl_up_sync(0xffffffffu, x, o);
+        if (l >= o) x += y;
+    }
+    __syncthreads();
+    if (l == 31) ws[w] = x;
+    __syncthreads();
+    uint64_t base = 0, all = 0;
+    for (int k = 0; k < (int)(blockDim.x >> 5); k++) {
+        if (k < w) base += ws[k];
+        all += ws[k];
+    }
+    __syncthreads();
+    if (total) *total = all;
+    return base + x - v;
+}
+
+// The k-th largest of v[0..n) (radix selection on the order-preserving
+// unsigned image of the int64 values, one byte per pass).
+__device__ int64_t cta_kth_largest(const int64_t *v, int n, int k) {
+    __shared__ unsigned int hist[256];
+    uint64_t prefix = 0;
+    unsigned int need = (unsigned int)k;
+    for (int d = 7; d >= 0; d--) {
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const uint64_t u = (uint64_t)v[i] ^ 0x8000000000000000ull;
+            if (d == 7 || (u >> (8 * (d + 1))) == prefix) atomicAdd(&hist[(u >> (8 * d)) & 0xFF], 1u);
+        }
+        __syncthreads();
+        unsigned int cum = 0;
+        int b = 255;
+        for (; b > 0; b--) {
+            if (cum + hist[b] >= need) break;
+            cum += hist[b];
+        }
+        prefix = (prefix << 8) | (uint64_t)b;
+        need -= cum;
+        __syncthreads();
+    }
+    return (int64_t)(prefix ^ 0x8000000000000000ull);
+}
+
+// sum of v[i] over i with v[i] >= lo (v >= 0 here), CTA-wide
+__device__ uint64_t cta_sum_at_least(const int64_t *v, int n, int64_t lo, uint64_t *red) {
+    uint64_t s = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+        if (v[i] >= lo && v[i] > 0) s += (uint64_t)v[i];
+    return (uint64_t)cta_sum_i128((i128)(u128)s, red);
+}
+
+// sample_token (llama_int.c:2958-3039) for row b of logits [rows][V], one CTA
+// (IQ_SAMPLE_THREADS threads) per row, with the state of sequence seq_of(b);
+// work [rows][V] is scratch. Same result as the reference, step for step:
+//   temperature below 0.01: argmax; else w = fp_div(logit, T);
+//   top-k: w < (k-th largest) -> INT64_MIN / 2;  softmax;
+//   top-p: the reference adds the largest remaining probability (lowest index
+//     among equals) until the running sum reaches p. That set is found
+//     directly: t* = the largest t with sum_{w >= t} w >= p (bitwise search),
+//     all w > t* and the first j of the w == t* (index order) with
+//     j = ceil((p - sum_{w > t*} w) / t*); if all positive mass stays below p,
+//     every positive w. Others are zeroed, kept ones renormalised (fp_div);
+//   draw r = xoroshiro128+ >> 16; the first index whose running sum exceeds r,
+//     else the argmax of the probabilities.
+// Outputs as k_argmax (result, and the decode-state update when tokens != 0).
+__global__ void __launch_bounds__(IQ_SAMPLE_THREADS)
+k_sample(int *__restrict__ result, const int64_t *__restrict__ logits, int V, SampleState *__restrict__ st,
+         int st_stride, int64_t *__restrict__ work, int *__restrict__ tokens, int *__restrict__ pos_arr,
+         int *__restrict__ hist, int hist_stride) {
+    __shared__ uint64_t red[64];
+    __shared__ int sel_s;
+    const int b = blockIdx.x;
+    SampleState *S = st + (size_t)b * st_stride;
+    const int64_t *lg = logits + (size_t)b * V;
+    int64_t *w = work + (size_t)b * V;
+    const int64_t ONE = (int64_t)1 << 48;
+    const int64_t T = S->temperature;
+    int sel;
+    if (T <= 0 || T < ONE / 100) {
+        sel = cta_argmax(lg, V);
+    } else {
+        for (int i = threadIdx.x; i < V; i += blockDim.x) w[i] = d_div(lg[i], T);
+        __syncthreads();
+        const int k = S->top_k;
+        if (k > 0 && k < V) {
+            const int64_t thr = cta_kth_largest(w, V, k);
+            for (int i = threadIdx.x; i < V; i += blockDim.x)
+                if (w[i] < thr) w[i] = INT64_MIN / 2;
+            __syncthreads();
+        }
+        cta_softmax(w, V, red);
+        __syncthreads();
+        const int64_t P = S->top_p;
+        if (P > 0 && P < ONE) {
+            const uint64_t all = cta_sum_at_least(w, V, 1, red);
+            int64_t tstar = 0;   // 0: keep every positive probability
+            uint64_t s_gt = 0;
+            int64_t j = 0;
+            if (all >= (uint64_t)P) {
+                for (int bit = 48; bit >= 0; bit--) {
+                    const int64_t cand = tstar | ((int64_t)1 << bit);
+                    if (cta_sum_at_least(w, V, cand, red) >= (uint64_t)P) tstar = cand;
+                }
+                s_gt = cta_sum_at_least(w, V, tstar + 1, red);
+                j = (int64_t)(((uint64_t)P - s_gt + (uint64_t)tstar - 1) / (uint64_t)tstar);
+            }
+            // ties at t*: keep the first j in index order (a contiguous chunk per thread)
+            const int C = (V + blockDim.x - 1) / blockDim.x, i0 = threadIdx.x * C, i1 = min(V, i0 + C);
+            uint64_t eq = 0;
+            for (int i = i0; i < i1; i++) eq += (tstar > 0 && w[i] == tstar);
+            uint64_t before = cta_exclusive_scan(eq, nullptr);
+            uint64_t kept = 0;
+            for (int i = i0; i < i1; i++) {
+                const int64_t v = w[i];
+                bool keep = tstar == 0 ? v > 0 : (v > tstar || (v == tstar && (int64_t)before++ < j));
+                w[i] = keep ? v : 0;
+                kept += keep ? (uint64_t)v : 0;
+            }
+            const int64_t sum = (int64_t)(uint64_t)cta_sum_i128((i128)(u128)kept, red);
+            __syncthreads();
+            if (sum > 0)
+                for (int i = threadIdx.x; i < V; i += blockDim.x)
+                    if (w[i] > 0) w[i] = d_div(w[i], sum);
+            __syncthreads();
+        }
+        // draw: one generator step (rng_next, llama_int.c:2921-2929)
+        __shared__ int64_t r_s;
+        if (threadIdx.x == 0) {
+            const uint64_t s0 = S->s0;
+            uint64_t s1 = S->s1;
+            const uint64_t res = s0 + s1;
+            s1 ^= s0;
+            S->s0 = ((s0 << 55) | (s0 >> 9)) ^ s1 ^ (s1 << 14);
+            S->s1 = (s1 << 36) | (s1 >> 28);
+            r_s = (int64_t)(res >> 16);
+            sel_s = 0x7fffffff;
+        }
+        __syncthreads();
+        const int64_t r = r_s;
+        const int C = (V + blockDim.x - 1) / blockDim.x, i0 = threadIdx.x * C, i1 = min(V, i0 + C);
+        uint64_t part = 0;
+        for (int i = i0; i < i1; i++) part += (uint64_t)w[i];
+        uint64_t run = cta_exclusive_scan(part, nullptr);
+        for (int i = i0; i < i1; i++) {
+            run += (uint64_t)w[i];
+            if ((int64_t)run > r) { atomicMin(&sel_s, i); break; }
+        }
+        __syncthreads();
+        sel = sel_s;
+        if (sel == 0x7fffffff) sel = cta_argmax(w, V);
+    }
+    if (threadIdx.x == 0) {
+        result[b] = sel;
+        if (tokens) tokens[b] = sel;
+        if (pos_arr) {
+            const int np1 = pos_arr[b] + 1;
+            if (hist) hist[(size_t)b * hist_stride + np1] = sel;
+            pos_arr[b] = np1;
+        }
+    }
+}
+
 // After a prefill: the argmax of the sequence's last prompt row becomes its
 // next token at position L, recorded in the history (llama_int.c:3087-3089).
 __global__ void k_prefill_done(const int *__restrict__ arg, int *__restrict__ tokens, int *__restrict__ pos_arr,

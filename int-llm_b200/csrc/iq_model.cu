@@ -111,6 +111,10 @@ struct iq_model {
     bool failed = false;        // the communicator was aborted: the model is unusable
     int64_t timeout_ms = 60000; // bounded host waits under tensor parallelism
     bool want_logits = false;   // decode steps also gather the full logits (TP; hashing callers)
+    bool sampling = false;      // steps draw with sample_token instead of argmax
+    SampleState *d_samp = nullptr;   // [max_batch] sampling parameters and generator states
+    int64_t *swork = nullptr;        // [rmax][vocab] sampling scratch
+    int prefill_seq = 0;             // sequence of the prefill chunk being enqueued
     int64_t *pairs_l = nullptr, *pairs_g = nullptr;   // TP argmax: local pair, gathered pairs
     int dec_mode = 0;           // 1 = use it where it applies, 0 = per-kernel path (default: faster today)
     bool dec_ready = false;     // prepared for the current weights
@@ -230,6 +234,8 @@ static int model_alloc(iq_model *m) {
     DALLOC(m->d_seq, (size_t)NB * 4);
     DALLOC(m->d_arg, (size_t)B * 4);
     DALLOC(m->d_hist, (size_t)NB * (c.max_seq_len + 1) * 4);
+    DALLOC(m->d_samp, (size_t)NB * sizeof(SampleState));
+    DALLOC(m->swork, (size_t)NB * c.vocab_size * 8);
     DALLOC(m->d_ptok, (size_t)B * 4);
     DALLOC(m->d_ppos, (size_t)B * 4);
     DALLOC(m->d_pseq, (size_t)B * 4);
@@ -393,7 +399,7 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
     const int64_t *fin = m->hidden + (size_t)(R - LR) * d;   // the rows the LM head reads
     if (tp) {
         if ((rc = norm_proj(m->logits_l, m->plm, m->tlm, fin, m->fnorm, LR))) return rc;
-        if (decode && !m->want_logits) {
+        if (decode && !m->want_logits && !m->sampling) {
             // sharded argmax: each rank's first maximum, then (value, index) pairs
             k_argmax_local<<<LR, 1024, 0, s>>>(m->pairs_l, m->logits_l, S.v_l, S.r * S.v_l);
             IQ_CHECK_LAUNCH();
@@ -407,7 +413,15 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
     } else if ((rc = norm_proj(m->logits, m->plm, m->tlm, fin, m->fnorm, LR))) {
         return rc;
     }
-    if (decode) {
+    if (m->sampling) {   // sample_token with each sequence's parameters and generator
+        if (decode)
+            k_sample<<<LR, IQ_SAMPLE_THREADS, 0, s>>>(m->d_arg, m->logits, c.vocab_size, m->d_samp, 1, m->swork,
+                                                      m->d_tok, m->d_pos, m->d_hist, c.max_seq_len + 1);
+        else
+            k_sample<<<1, IQ_SAMPLE_THREADS, 0, s>>>(m->d_arg, m->logits + (size_t)(LR - 1) * c.vocab_size,
+                                                     c.vocab_size, m->d_samp + m->prefill_seq, 1, m->swork,
+                                                     nullptr, nullptr, nullptr, 0);
+    } else if (decode) {
         k_argmax<<<LR, 1024, 0, s>>>(m->d_arg, m->logits, c.vocab_size, m->d_tok, m->d_pos, m->d_hist,
                                      c.max_seq_len + 1);
     } else {
@@ -839,7 +853,8 @@ IQ_API int iq_model_destroy(iq_model *m) {
     void *bufs[] = {m->embed, m->fnorm, m->lm, m->rcos, m->rsin, m->hidden, m->normed, m->qkv, m->att,
                     m->gu, m->act, m->logits, m->att_l, m->proj_l, m->act_l, m->logits_l, m->gath,
                     m->proj_full, m->d_tok, m->d_pos, m->d_arg, m->d_hist, m->racc, m->digits, m->gpart, m->asc, m->amx, m->asum, m->d_seq,
-                    m->d_ptok, m->d_ppos, m->d_pseq, m->d_layers, m->bar, m->argv, m->pairs_l, m->pairs_g};
+                    m->d_ptok, m->d_ppos, m->d_pseq, m->d_layers, m->bar, m->argv, m->pairs_l, m->pairs_g,
+                    m->d_samp, m->swork};
     for (void *p : bufs) if (p) cudaFree(p);
     for (auto *v : {&m->norm1, &m->wqkv, &m->wo, &m->norm2, &m->wgu, &m->wdown, &m->kc, &m->vc})
         for (int64_t *p : *v) if (p) cudaFree(p);
@@ -969,6 +984,7 @@ static int set_tok_pos(iq_model *m, const int *tok, const int *pos, int B, int s
 // Ends with the sequence's decode state at position L (k_prefill_done).
 static int enqueue_prefill(iq_model *m, int sq, const int *prompt, int L, std::vector<int64_t> *hv) {
     int *h = m->h_rows;
+    m->prefill_seq = sq;
     for (int p = 0; p < L; p++) { h[p] = prompt[p]; h[L + p] = p; h[2 * L + p] = sq; }
     int rc;
     for (int p0 = 0; p0 < L; p0 += m->rmax) {
@@ -1045,7 +1061,7 @@ IQ_API int iq_generate(iq_model *m, const int *prompt, int plen, int max_new, in
     const bool hash = logit_hash != nullptr;
     const int V = c.vocab_size;
     uint64_t h = 1469598103934665603ULL;
-    if ((rc = set_want_logits(m, hash))) return rc;
+    if ((rc = set_want_logits(m, hash || m->sampling))) return rc;
     memcpy(out, prompt, (size_t)plen * sizeof(int));
     // prefill: every prompt position in batched rows (== the M=1 loop of llama_int.c:3081-3092)
     std::vector<int64_t> hv;
@@ -1083,6 +1099,28 @@ IQ_API int iq_generate(iq_model *m, const int *prompt, int plen, int max_new, in
     }
     *n_out = total;
     return take_dev_error();
+}
+
+IQ_API int iq_generate_sampled(iq_model *m, const int *prompt, int plen, int max_new, int64_t temperature,
+                               int top_k, int64_t top_p, uint64_t seed, int *out, int *n_out, uint64_t *logit_hash) {
+    if (!model_ready(m)) return m ? IQ_ERR_STATE : IQ_ERR_ARG;
+    IQ_CUDA(cudaSetDevice(m->dev));
+    SampleState st{};
+    st.temperature = temperature;
+    st.top_k = top_k;
+    st.top_p = top_p;
+    uint64_t rs[2];
+    iq_rng_seed(seed, rs);   // rng_seed once per generation (llama_int.c:4783-4789)
+    st.s0 = rs[0];
+    st.s1 = rs[1];
+    IQ_WAIT(m);
+    IQ_CUDA(cudaMemcpy(m->d_samp, &st, sizeof(st), cudaMemcpyHostToDevice));
+    invalidate_exec(m);   // the step graphs bake in argmax or sampling
+    m->sampling = true;
+    int rc = iq_generate(m, prompt, plen, max_new, out, n_out, logit_hash);
+    invalidate_exec(m);
+    m->sampling = false;
+    return rc;
 }
 
 IQ_API int iq_generate_batch(iq_model *m, const int *prompts, int plen, int max_new, int *out, int *n_out,
@@ -1152,6 +1190,42 @@ IQ_API int iq_model_set_attention(iq_model *m, int short_max) {
     IQ_CUDA(cudaStreamSynchronize(m->s));
     if (m->graph_s) { cudaGraphExecDestroy(m->graph_s); m->graph_s = nullptr; }
     m->att_short = short_max;
+    return IQ_OK;
+}
+
+IQ_API int iq_sample_dev(const int64_t *d_logits, int rows, int V, int64_t temperature, int top_k, int64_t top_p,
+                         uint64_t *rng, int *out) {
+    if (!d_logits || rows < 1 || V < 1 || !rng || !out) return IQ_ERR_ARG;
+    int dev, rc;
+    if ((rc = cur_device(&dev))) return rc;
+    std::vector<SampleState> h(rows);
+    for (int r = 0; r < rows; r++) {
+        h[r].temperature = temperature;
+        h[r].top_k = top_k;
+        h[r].top_p = top_p;
+        h[r].s0 = rng[2 * r];
+        h[r].s1 = rng[2 * r + 1];
+    }
+    SampleState *d_st = nullptr;
+    int64_t *work = nullptr;
+    int *d_out = nullptr;
+    cudaStream_t s = lib_stream();
+    cudaError_t e = cudaMalloc(&d_st, rows * sizeof(SampleState));
+    if (e == cudaSuccess) e = cudaMalloc(&work, (size_t)rows * V * 8);
+    if (e == cudaSuccess) e = cudaMalloc(&d_out, rows * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d_st, h.data(), rows * sizeof(SampleState), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) {
+        k_sample<<<rows, IQ_SAMPLE_THREADS, 0, s>>>(d_out, d_logits, V, d_st, 1, work, nullptr, nullptr, nullptr, 0);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, d_out, rows * sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(h.data(), d_st, rows * sizeof(SampleState), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    cudaFree(d_st);
+    cudaFree(work);
+    cudaFree(d_out);
+    if (e != cudaSuccess) return cuda_fail(e);
+    for (int r = 0; r < rows; r++) { rng[2 * r] = h[r].s0; rng[2 * r + 1] = h[r].s1; }
     return IQ_OK;
 }
 

@@ -33,6 +33,15 @@ inline int64_t mul_q48(int64_t a, int64_t b) { return (int64_t)(((__int128)a * b
 
 extern "C" {
 
+IQ_API int iq_rng_seed(uint64_t seed, uint64_t state[2]) {
+    if (!state) return IQ_ERR_ARG;
+    Xoro r;
+    xseed(&r, seed);
+    state[0] = r.s0;
+    state[1] = r.s1;
+    return IQ_OK;
+}
+
 IQ_API uint16_t iq_q1648_to_bf16(int64_t w) {
     if (w == 0) return 0;
     uint16_t sgn = w < 0 ? 0x8000 : 0;

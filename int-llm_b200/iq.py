@@ -74,6 +74,9 @@ SIGNATURES = {
     "iq_forward": (_I, [_P, _I, _I, _P, _P]),
     "iq_generate": (_I, [_P, _P, _I, _I, _P, _P, _P]),
     "iq_generate_batch": (_I, [_P, _P, _I, _I, _P, _P, _P]),
+    "iq_generate_sampled": (_I, [_P, _P, _I, _I, _I64, _I, _I64, ctypes.c_uint64, _P, _P, _P]),
+    "iq_sample_dev": (_I, [_P, _I, _I, _I64, _I, _I64, _P, _P]),
+    "iq_rng_seed": (_I, [ctypes.c_uint64, _P]),
     "iq_decode_steps_timed": (_I, [_P, _I, _I, _P]),
     "iq_model_set_attention": (_I, [_P, _I]),
     "iq_model_weight_bytes": (_I, [_P, _P, _P]),
@@ -304,6 +307,14 @@ def gemm_tc_dev(out, packed, X, rows, stream=None):
     _call("iq_gemm_tc_dev", _dp(out), packed.h, _dp(X), rows, _sp(stream))
 
 
+def sample_dev(d_logits, rows, V, temperature, top_k, top_p, rng):
+    """sample_token per row on the device; rng: uint64 [rows][2], advanced in place."""
+    out = np.zeros(rows, dtype=np.int32)
+    assert rng.dtype == np.uint64 and rng.flags.c_contiguous
+    _call("iq_sample_dev", _dp(d_logits), rows, V, temperature, top_k, top_p, _hp(rng), _hp(out))
+    return out
+
+
 def device_status():
     """IQ_OK, or the timeout status a kernel's bounded wait recorded (then cleared)."""
     return lib().iq_device_status()
@@ -423,6 +434,16 @@ class Model:
         h = ctypes.c_uint64(0)
         _call("iq_generate", self.h, _hp(pr), len(pr), max_new, _hp(out), ctypes.byref(n),
               ctypes.byref(h) if logit_hash else None)
+        return out[:n.value].tolist(), (h.value if logit_hash else None)
+
+    def generate_sampled(self, prompt, max_new, temperature, top_k, top_p, seed, logit_hash=False):
+        """generate() with sample_token (temperature / top_p in Q16.48)."""
+        pr = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(len(pr) + max_new, dtype=np.int32)
+        n = ctypes.c_int(0)
+        h = ctypes.c_uint64(0)
+        _call("iq_generate_sampled", self.h, _hp(pr), len(pr), max_new, temperature, top_k, top_p, seed, _hp(out),
+              ctypes.byref(n), ctypes.byref(h) if logit_hash else None)
         return out[:n.value].tolist(), (h.value if logit_hash else None)
 
     def generate_batch(self, prompts, max_new, logit_hash=False):

@@ -652,3 +652,107 @@ uint64_t iqo_fnv_array(uint64_t h, const int64_t *v, int64_t n) {
     for (int64_t i = 0; i < n; i++) h = iqo_fnv_mix_i64(h, v[i]);
     return h;
 }
+
+/* ---------------- sampling ---------------- */
+
+/* first maximum (strict >). llama_int.c:2888-2893 */
+static int o_argmax(const int64_t *v, int n) {
+    int b = 0;
+    for (int i = 1; i < n; i++) if (v[i] > v[b]) b = i;
+    return b;
+}
+static int o_cmp_desc(const void *a, const void *b) {
+    int64_t x = *(const int64_t *)a, y = *(const int64_t *)b;
+    return (y > x) - (y < x);
+}
+
+/* sample_token (llama_int.c:2958-3039): below a temperature of 0.01 the argmax;
+ * else work = fp_div(logit, T); top-k keeps values >= the k-th largest (others
+ * INT64_MIN / 2); softmax; top-p keeps the largest probabilities (first index
+ * among equals) until their running int64 sum reaches p, zeroes the rest and
+ * renormalises with fp_div; then the first index whose running sum exceeds
+ * r = xoroshiro128+ >> 16, else the argmax of the probabilities.
+ * rng: the generator state {s0, s1}, advanced once per sampled token. */
+int iqo_sample_token(const int64_t *logits, int V, int64_t temp, int top_k, int64_t top_p, uint64_t rng[2]) {
+    if (temp <= 0 || temp < ONE / 100) return o_argmax(logits, V);
+    int64_t *w = (int64_t *)malloc((size_t)V * 8);
+    for (int i = 0; i < V; i++) w[i] = o_div(logits[i], temp);
+    if (top_k > 0 && top_k < V) {
+        int64_t *srt = (int64_t *)malloc((size_t)V * 8);
+        memcpy(srt, w, (size_t)V * 8);
+        qsort(srt, (size_t)V, 8, o_cmp_desc);
+        const int64_t thr = srt[top_k - 1];
+        free(srt);
+        for (int i = 0; i < V; i++) if (w[i] < thr) w[i] = INT64_MIN / 2;
+    }
+    iqo_softmax(w, V);
+    if (top_p > 0 && top_p < ONE) {
+        int64_t cum = 0;
+        while (cum < top_p) {
+            int best = -1;
+            for (int i = 0; i < V; i++) {
+                if (w[i] <= 0) continue;
+                if (best < 0 || w[i] > w[best]) best = i;
+            }
+            if (best < 0) break;
+            cum += w[best];
+            w[best] = -w[best];
+        }
+        for (int i = 0; i < V; i++) w[i] = w[i] < 0 ? -w[i] : 0;
+        int64_t sum = 0;
+        for (int i = 0; i < V; i++) sum += w[i];
+        if (sum > 0) for (int i = 0; i < V; i++) if (w[i] > 0) w[i] = o_div(w[i], sum);
+    }
+    orng r = {rng[0], rng[1]};
+    const int64_t thr = (int64_t)(r_next(&r) >> 16);
+    rng[0] = r.s0;
+    rng[1] = r.s1;
+    int64_t cum = 0;
+    int sel = -1;
+    for (int i = 0; i < V; i++) {
+        cum += w[i];
+        if (cum > thr) { sel = i; break; }
+    }
+    if (sel < 0) sel = o_argmax(w, V);
+    free(w);
+    return sel;
+}
+
+/* rng_seed (llama_int.c:2909-2919) into {s0, s1}. */
+void iqo_rng_seed(uint64_t seed, uint64_t rng[2]) {
+    orng r;
+    r_seed(&r, seed);
+    rng[0] = r.s0;
+    rng[1] = r.s1;
+}
+
+/* generate() with sampling parameters (llama_int.c:3067-3135 with sp != NULL):
+ * the generator is seeded once (rng_seed), every prefill-end and decode sample
+ * goes through sample_token, EOS stops. */
+int iqo_model_generate_sampled(void *h, const int *prompt, int plen, int max_new, int64_t temp, int top_k,
+                               int64_t top_p, uint64_t seed, int *out, uint64_t *logit_hash_out) {
+    omodel *m = (omodel *)h;
+    iqo_model_reset(m);
+    uint64_t rng[2];
+    iqo_rng_seed(seed, rng);
+    int64_t *lg = (int64_t *)malloc((size_t)m->vocab * 8);
+    uint64_t lh = 1469598103934665603ULL;
+    memcpy(out, prompt, (size_t)plen * sizeof(int));
+    int total = plen;
+    for (int p = 0; p < plen; p++) {
+        if (iqo_model_forward(m, out[p], p, lg) < 0) { free(lg); return -1; }
+        for (int i = 0; i < m->vocab; i++) lh = iqo_fnv_mix_i64(lh, lg[i]);
+        if (p == plen - 1) out[total++] = iqo_sample_token(lg, m->vocab, temp, top_k, top_p, rng);
+    }
+    for (int i = 1; i < max_new; i++) {
+        int p = plen + i - 1;
+        if (iqo_model_forward(m, out[p], p, lg) < 0) break;
+        for (int j = 0; j < m->vocab; j++) lh = iqo_fnv_mix_i64(lh, lg[j]);
+        int a = iqo_sample_token(lg, m->vocab, temp, top_k, top_p, rng);
+        if (a == 2) break;
+        out[total++] = a;
+    }
+    free(lg);
+    if (logit_hash_out) *logit_hash_out = lh;
+    return total;
+}

@@ -50,4 +50,8 @@ int iqo_model_forward(void *m, int token, int pos, int64_t *logits_out);
 int iqo_model_generate(void *m, const int *prompt, int prompt_len, int max_new, int *out_tokens,
                        uint64_t *logit_hash_out);
 void iqo_model_free(void *m);
+int iqo_sample_token(const int64_t *logits, int V, int64_t temp, int top_k, int64_t top_p, uint64_t rng[2]);
+void iqo_rng_seed(uint64_t seed, uint64_t rng[2]);
+int iqo_model_generate_sampled(void *h, const int *prompt, int plen, int max_new, int64_t temp, int top_k,
+                               int64_t top_p, uint64_t seed, int *out, uint64_t *logit_hash_out);
 #endif

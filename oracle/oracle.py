@@ -58,6 +58,9 @@ def _load_oracle():
         "iqo_model_forward": (_I, [_P, _I, _I, _P]),
         "iqo_model_generate": (_I, [_P, _P, _I, _I, _P, _P]),
         "iqo_model_free": (None, [_P]),
+        "iqo_sample_token": (_I, [_P, _I, _I64, _I, _I64, _P]),
+        "iqo_rng_seed": (None, [_U64, _P]),
+        "iqo_model_generate_sampled": (_I, [_P, _P, _I, _I, _I64, _I, _I64, _U64, _P, _P]),
     }
     for k, (r, a) in sig.items():
         f = getattr(L, k)
@@ -86,6 +89,9 @@ _REF_SIG = {
     "ref_model_free": (None, [_P]),
     "ref_model_open_mgw": (_P, [ctypes.c_char_p, _I]),
     "ref_model_close_mgw": (None, [_P]),
+    "ref_sample_token": (_I, [_P, _I, _I64, _I, _I64, _P]),
+    "ref_rng_seed": (None, [_U64, _P]),
+    "ref_model_generate_sampled": (_I, [_P, _P, _I, _I, _I64, _I, _I64, _U64, _P]),
 }
 
 

@@ -16,6 +16,8 @@
  *   ref_rope_tables    -> rope_init             llama_int.c:960-986
  *   ref_model_*        -> llama_forward / generate on caller-owned weights
  *                         llama_int.c:2807-2886, 3067-3135
+ *   ref_sample_token   -> sample_token with sample_params_t   llama_int.c:2958-3039
+ *   ref_model_generate_sampled -> generate(..., sp)          llama_int.c:3067-3135
  *   ref_model_open_mgw -> mgw_load (mmap, layers cached) or mgw_load_streaming
  *                         (layers pread into fresh buffers and freed after
  *                         every layer), llama_int.c:2344-2803
@@ -200,4 +202,36 @@ REFAPI void ref_model_close_mgw(void *h) {
         if (m->native_stream_fd >= 0) close(m->native_stream_fd);
     }
     free(m);
+}
+
+/* sample_token on caller logits with the given parameters and generator
+ * state {s0, s1} (advanced in place). */
+REFAPI int ref_sample_token(const int64_t *logits, int V, int64_t temp, int top_k, int64_t top_p, uint64_t *rng) {
+    sample_params_t sp;
+    sp.temperature = temp;
+    sp.top_k = top_k;
+    sp.top_p = top_p;
+    sp.rng.s[0] = rng[0];
+    sp.rng.s[1] = rng[1];
+    int t = sample_token(logits, V, &sp);
+    rng[0] = sp.rng.s[0];
+    rng[1] = sp.rng.s[1];
+    return t;
+}
+
+REFAPI void ref_rng_seed(uint64_t seed, uint64_t *rng) {
+    rng_state_t r;
+    rng_seed(&r, seed);
+    rng[0] = r.s[0];
+    rng[1] = r.s[1];
+}
+
+REFAPI int ref_model_generate_sampled(void *h, const int *prompt, int prompt_len, int max_new, int64_t temp,
+                                      int top_k, int64_t top_p, uint64_t seed, int *out_tokens) {
+    sample_params_t sp;
+    sp.temperature = temp;
+    sp.top_k = top_k;
+    sp.top_p = top_p;
+    rng_seed(&sp.rng, seed);
+    return generate((llama_model_t *)h, prompt, prompt_len, max_new, out_tokens, &sp);
 }

@@ -12,6 +12,7 @@ inputs, whose generator is cross-checked against the reference's bf16 decoder.
   python tests/golden/make_golden.py --geom7b   # head_dim-128 MHA model, 400 positions
   python tests/golden/make_golden.py --cfg3     # config-3 geometry, 8 sequences at T~2100 (minutes, 8 processes)
   python tests/golden/make_golden.py --eos      # a model made to emit EOS (token 2) mid-generation
+  python tests/golden/make_golden.py --sampled  # config-0 generate() with sampling, 3 parameter sets (minutes)
 """
 import json
 import os
@@ -208,6 +209,31 @@ def cfg0_logits(R):
                                           "llama_forward, called in generate()'s order"))
 
 
+SAMPLED = [dict(temperature=(1 << 48) * 4 // 5, top_k=40, top_p=(1 << 48) * 9 // 10, seed=42),
+           dict(temperature=(1 << 48) * 3 // 2, top_k=0, top_p=(1 << 48) // 2, seed=7),
+           dict(temperature=(1 << 48), top_k=5, top_p=1 << 48, seed=2026)]
+
+
+def cfg0_sampled(R):
+    """Config-0 model, 8-token prompt, 32 tokens drawn by the reference's own
+    generate() with sampling parameters (sample_token, llama_int.c:2958-3039)."""
+    c = configs.TINYLLAMA
+    w = helpers.model_weights(0, c)
+    mr = helpers.OracleModel(c, w, lib=R, prefix="ref_")
+    prompt = np.ascontiguousarray(orc.synth_tokens(0, "prompt:0", 8, c["vocab"]), dtype=np.int32)
+    runs = []
+    for sp in SAMPLED:
+        t0 = time.time()
+        out = np.zeros(8 + 32, np.int32)
+        n = R.ref_model_generate_sampled(mr.h, orc.p(prompt), 8, 32, sp["temperature"], sp["top_k"], sp["top_p"],
+                                         sp["seed"], orc.p(out))
+        runs.append(dict(sp, tokens=[int(t) for t in out[:n]]))
+        print("sampled run", time.time() - t0)
+    mr.close()
+    save("cfg0_sampled.json", dict(prompt=[int(t) for t in prompt], max_new=32, runs=runs,
+                                   note="temperature / top_p in Q16.48; tokens from the reference's generate(sp)"))
+
+
 def cfg2(R):
     res = []
     rows = configs.CFG2_ROWS
@@ -234,6 +260,8 @@ if __name__ == "__main__":
         cfg2(R)
     if "--cfg0" in sys.argv:
         cfg0_logits(R)
+    if "--sampled" in sys.argv:
+        cfg0_sampled(R)
     if "--geom7b" in sys.argv:
         geom7b(R)
     if "--eos" in sys.argv:

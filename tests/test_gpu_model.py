@@ -264,3 +264,73 @@ def test_persistent_decode_crosses_into_tiled_attention():
         t2, _ = m.generate(pr, 40)
         assert t1 == t2 == want and h1 == wlh, mode
     m.close(); o.close()
+
+
+# ------------------------------------------------------------------ sampling
+
+ONE = 1 << 48
+SAMPLE_PARAMS = [(0, 0, ONE), (ONE // 200, 0, ONE), (ONE // 100, 0, ONE), (ONE, 0, ONE), (ONE // 2, 5, ONE),
+                 (ONE * 3 // 2, 40, ONE * 9 // 10), (ONE, 0, ONE // 2), (ONE * 2, 1, ONE), (ONE, 0, 1),
+                 (ONE // 3, 100, ONE * 3 // 4), (ONE, 31999, ONE * 99 // 100)]
+
+
+def test_sample_token_device_vs_oracle():
+    """k_sample equals the oracle's sample_token (itself pinned to the
+    reference's) on random logits: vocabulary sizes 1..32000, ties planted at
+    the maximum and at the top-k / top-p boundaries, every parameter regime,
+    three consecutive draws per generator state."""
+    import torch
+    rng = np.random.default_rng(17)
+    for trial, V in enumerate([1, 7, 600, 5000, 32000]):
+        rows = 3
+        lg = rng.integers(-(8 << 48), 8 << 48, (rows, V)).astype(np.int64)
+        if V > 20:
+            lg[0, rng.integers(0, V, 9)] = lg[0].max()
+            lg[1, rng.integers(0, V, 40)] = np.sort(lg[1])[-30]     # ties inside the top k
+            lg[2] = lg[2] >> 20                                     # narrow spread: flat softmax
+        d = torch.from_numpy(lg).cuda()
+        for temp, k, p in SAMPLE_PARAMS:
+            st = np.zeros((rows, 2), np.uint64)
+            for r in range(rows):
+                orc.O.iqo_rng_seed(trial * 100 + r + k, orc.p(st[r]))
+            ost = st.copy()
+            for draw in range(3):
+                got = iq.sample_dev(d, rows, V, temp, k, p, st)
+                for r in range(rows):
+                    s2 = np.ascontiguousarray(ost[r])
+                    want = orc.O.iqo_sample_token(orc.p(np.ascontiguousarray(lg[r])), V, temp, k, p, orc.p(s2))
+                    ost[r] = s2
+                    assert got[r] == want, (V, temp, k, p, draw, r)
+                assert (st == ost).all()
+
+
+def test_generate_sampled_matches_oracle_and_reference_golden():
+    """generate() with sampling: the tiny model against the oracle (tokens and
+    every-logit hash) for several parameter sets, and the config-0 model
+    against the reference's own sampled generate (golden)."""
+    c = dict(configs.TINY_TEST, max_seq=64)
+    w = helpers.model_weights(9, c)
+    m = iq.Model(c)
+    m.load(w)
+    o = helpers.OracleModel(c, w)
+    pr = np.ascontiguousarray(orc.synth_tokens(9, "prompt:sample", 8, c["vocab"]), dtype=np.int32)
+    for temp, k, p in SAMPLE_PARAMS[:8]:
+        toks, lh = m.generate_sampled(pr, 24, temp, k, p, 99, logit_hash=True)
+        out = np.zeros(8 + 24, np.int32)
+        import ctypes
+        h = ctypes.c_uint64()
+        n = orc.O.iqo_model_generate_sampled(o.h, orc.p(pr), 8, 24, temp, k, p, 99, orc.p(out), ctypes.byref(h))
+        assert toks == out[:n].tolist() and lh == h.value, (temp, k, p)
+        toks2, _ = m.generate_sampled(pr, 24, temp, k, p, 99)
+        assert toks2 == toks
+    g, _ = m.generate(pr, 24)   # greedy again afterwards
+    assert g == o.generate(pr, 24)[0]
+    m.close(); o.close()
+    gs = gold("cfg0_sampled.json")
+    m = iq.Model(configs.TINYLLAMA)
+    m.synth(0)
+    for run in gs["runs"]:
+        toks, _ = m.generate_sampled(np.array(gs["prompt"]), gs["max_new"], run["temperature"], run["top_k"],
+                                     run["top_p"], run["seed"])
+        assert toks == run["tokens"], run["seed"]
+    m.close()

@@ -71,3 +71,66 @@ def test_tp2_generate_matches_goldens():
             if p.is_alive():
                 p.kill()
     assert res == {0: (True, None), 1: (True, None)}, res
+
+
+def _rank_leave(rank, world, nid, q):
+    """Rank 1 finishes one generate and leaves between steps (no collective in
+    flight); rank 0's next generate finds no peer and must return an error
+    within its timeout instead of blocking forever."""
+    import torch
+    torch.cuda.set_device(rank)
+    try:
+        g = json.load(open(os.path.join(GOLD, "tiny_model.json")))
+        c = g["config"]
+        w = helpers.model_weights(g["cfg_index"], c)
+        m = iq.Model(c, device=rank, tp_rank=rank, tp_size=world, nccl_id=nid)
+        m.load(w)
+        toks, _ = m.generate(np.array(g["prompt"]), 8)
+        if rank == 1:
+            q.put((rank, toks == g["tokens"][:len(toks)], "left"))
+            os._exit(0)   # leaves without destroying its communicator
+        iq.lib().iq_model_set_timeout(m.h, 3000)
+        try:
+            m.generate(np.array(g["prompt"]), 8)
+            status = 0
+        except iq.IQError as e:
+            status = e.status
+        try:
+            m.generate(np.array(g["prompt"]), 8)
+            after = 0
+        except iq.IQError as e:
+            after = e.status
+        m.close()
+        q.put((rank, status in (-4, -5) and after == -7, (status, after)))
+    except Exception as e:
+        q.put((rank, False, repr(e)))
+
+
+def test_tp2_peer_leaving_between_steps_times_out_cleanly():
+    """Failure detection without a GPU fault: the surviving rank's collective
+    is ended by the library's bounded wait (ncclCommAbort after the timeout or
+    on NCCL's asynchronous error), the call returns IQ_ERR_TIMEOUT or
+    IQ_ERR_NCCL, and the model refuses further work (IQ_ERR_STATE). NVLS is
+    off in both ranks."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    nid = iq.nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_leave, args=(r, 2, nid, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in procs:
+            r, ok, info = q.get(timeout=300)
+            res[r] = (ok, info)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    assert res[1][0] and res[0][0], res

@@ -179,3 +179,54 @@ def test_tiny_model_logits_vs_reference():
     assert a.forward(c["vocab"], 0)[0] == -1 and b.forward(c["vocab"], 0)[0] == -1
     assert a.forward(0, c["max_seq"])[0] == -1 and b.forward(0, c["max_seq"])[0] == -1
     a.close(); b.close()
+
+
+# ------------------------------------------------------------------ sampling
+
+def _params():
+    ONE_ = 1 << 48
+    return [(0, 0, ONE_), (ONE_ // 200, 0, ONE_), (ONE_ // 100, 0, ONE_), (ONE_, 0, ONE_),
+            (ONE_ // 2, 5, ONE_), (ONE_ * 3 // 2, 40, ONE_ * 9 // 10), (ONE_, 0, ONE_ // 2),
+            (ONE_ * 2, 1, ONE_), (ONE_, 0, 1), (ONE_ // 3, 100, ONE_ * 3 // 4)]
+
+
+@pytest.mark.skipif(orc.ref() is None, reason="oracle/_ref not built")
+def test_sample_token_restatement_vs_reference():
+    """The oracle's sample_token restatement equals the reference's own
+    (llama_int.c:2958-3039) on random logits, with ties planted, over
+    temperature (below/at the 0.01 floor), top-k, top-p, and consecutive draws
+    from one generator state."""
+    import ctypes
+    R = orc.ref()
+    rng = np.random.default_rng(5)
+    for trial in range(30):
+        V = int(rng.integers(1, 600))
+        lg = (rng.integers(-(8 << 48), 8 << 48, V)).astype(np.int64)
+        if V > 10:
+            lg[rng.integers(0, V, 5)] = lg.max()    # ties at the maximum
+        for temp, k, p in _params():
+            s1 = np.zeros(2, np.uint64)
+            orc.O.iqo_rng_seed(trial * 7 + k, orc.p(s1))
+            s2 = s1.copy()
+            for draw in range(3):
+                a = orc.O.iqo_sample_token(orc.p(lg), V, temp, k, p, orc.p(s1))
+                b = R.ref_sample_token(orc.p(lg), V, temp, k, p, orc.p(s2))
+                assert a == b, (trial, temp, k, p, draw)
+                assert (s1 == s2).all()
+
+
+@pytest.mark.skipif(orc.ref() is None, reason="oracle/_ref not built")
+def test_generate_sampled_restatement_vs_reference():
+    c = dict(configs.TINY_TEST, n_layers=1, max_seq=64)
+    w = helpers.model_weights(9, c)
+    pr = np.ascontiguousarray(orc.synth_tokens(9, "prompt:sample", 8, c["vocab"]), dtype=np.int32)
+    R = orc.ref()
+    mo = helpers.OracleModel(c, w)
+    mr = helpers.OracleModel(c, w, lib=R, prefix="ref_")
+    for temp, k, p in _params()[:7]:
+        o1 = np.zeros(8 + 20, np.int32)
+        o2 = np.zeros(8 + 20, np.int32)
+        n1 = orc.O.iqo_model_generate_sampled(mo.h, orc.p(pr), 8, 20, temp, k, p, 1234, orc.p(o1), None)
+        n2 = R.ref_model_generate_sampled(mr.h, orc.p(pr), 8, 20, temp, k, p, 1234, orc.p(o2))
+        assert n1 == n2 and (o1[:n1] == o2[:n2]).all(), (temp, k, p)
+    mo.close(); mr.close()
