@@ -333,6 +333,16 @@ IQ_API int iq_model_set_attention(iq_model *m, int short_max);
  * use and its grid size. */
 IQ_API int iq_model_set_decode(iq_model *m, int mode);
 
+/* Packed KV cache, the reference's --kv-packed KbVb (llama_int.c:1078-1235,
+ * 1392-1501): each (position, kv head) vector is stored as b-bit codes
+ * against its L-inf magnitude, K codes of k_bits (1..8) in bytes, V codes of
+ * v_bits (1..16) in 16-bit words, and attention reads the reconstructed
+ * values. Lossy against the exact cache but the same integers as the
+ * reference with the same flag, so tokens and logits still equal its output.
+ * (0, 0) returns to the exact cache. Resets the cache; the persistent decode
+ * kernel is not used in this mode. */
+IQ_API int iq_model_set_kv_packed(iq_model *m, int k_bits, int v_bits);
+
 /* Bounded host waits under tensor parallelism (no reference counterpart; the
  * reference has no collectives). Every host wait of a multi-GPU model polls
  * its stream together with NCCL's asynchronous error state; a communicator

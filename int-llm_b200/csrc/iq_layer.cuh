@@ -219,6 +219,68 @@ k_attention_gqa(int64_t *__restrict__ out, const int64_t *__restrict__ qkv, cons
 }
 
 // ---------------------------------------------------------------------------
+// Packed KV cache (the reference's --kv-packed KbVb, llama_int.c:1197-1235,
+// 1392-1411, 1435-1501): per (position, kv head) vector an L-inf magnitude M
+// and b-bit codes q = ((x + M) * 2^b) / (2M) (int128, truncating, clamped to
+// [0, 2^b - 1]); attention reads back ((2q + 1) M) / 2^b - M. Lossy, but the
+// same integers as the reference, so still bit-exact against it.
+struct KVView {
+    const int64_t *x;       // exact cache (packed == 0)
+    const uint8_t *k8;      // K codes (packed, keys)
+    const uint16_t *v16;    // V codes (packed, values)
+    const int64_t *mag;     // [seq][max_seq][nkv] magnitudes
+    int bits, nkv, hd;
+    // element e of vector vec (= (seq * max_seq + t) * nkv + head)
+    __device__ __forceinline__ int64_t at(size_t elem, size_t vec) const {
+        if (!k8 && !v16) return x[elem];
+        const int64_t M = mag[vec];
+        if (M == 0) return 0;
+        const int64_t q = k8 ? (int64_t)k8[elem] : (int64_t)v16[elem];
+        // (2q + 1) M >= 0: the division by 2^b is a floor, i.e. a shift
+        return (int64_t)(((i128)(2 * q + 1) * M) >> bits) - M;
+    }
+};
+
+// kv_pack_vector (llama_int.c:1197-1218) for the rows' K and V at their
+// positions: one warp per (row, kv head), reading the exact values k_rope_kv
+// wrote into the exact cache.
+__global__ void k_kv_pack(uint8_t *__restrict__ kq, uint16_t *__restrict__ vq, int64_t *__restrict__ kmag,
+                          int64_t *__restrict__ vmag, const int64_t *__restrict__ kc, const int64_t *__restrict__ vc,
+                          const int *__restrict__ pos_arr, const int *__restrict__ seq_arr, int R, int nkv, int hd,
+                          int max_seq, int kbits, int vbits) {
+    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (gw >= R * nkv) return;
+    const int r = gw / nkv, h = gw % nkv;
+    const size_t vec = ((size_t)seq_arr[r] * max_seq + pos_arr[r]) * nkv + h;
+    const size_t e0 = vec * hd;
+    for (int which = 0; which < 2; which++) {
+        const int64_t *src = (which ? vc : kc) + e0;
+        const int b = which ? vbits : kbits;
+        int64_t M = 0;
+        for (int i = lane; i < hd; i += 32) {
+            const int64_t x = src[i];
+            const int64_t a = x < 0 ? (int64_t)(0 - (uint64_t)x) : x;   // wraps like -fwrapv
+            if (a > M) M = a;
+        }
+        for (int m = 16; m >= 1; m >>= 1) M = max(M, (int64_t)__shfl_xor_sync(0xffffffffu, M, m));
+        if (lane == 0) (which ? vmag : kmag)[vec] = M;
+        const int64_t Q = (int64_t)1 << b;
+        for (int i = lane; i < hd; i += 32) {
+            int64_t q = 0;
+            if (M != 0) {
+                const i128 num = (i128)(int64_t)((uint64_t)src[i] + (uint64_t)M) * Q;
+                i128 t = d_sdiv128_64(num, (int64_t)((uint64_t)M * 2));
+                if (t < 0) t = 0;
+                if (t >= (i128)Q) t = Q - 1;
+                q = (int64_t)t;
+            }
+            if (which) vq[e0 + i] = (uint16_t)q;
+            else kq[e0 + i] = (uint8_t)q;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Phased exact attention (llama_int.c:1432-1529), parallel over (row, kv
 // group, 64-position tile). Per row b (sequence seq[b], position pos[b]) and
 // query head h the reference computes, in order:
@@ -240,9 +302,10 @@ __global__ void k_attn_init(int64_t *__restrict__ out, int64_t *__restrict__ mx,
 }
 
 // phase 1: scores of one 64-position tile for the grp query heads of kv head g
+// (keys from the exact cache, or unpacked from the packed one: kv)
 __global__ void __launch_bounds__(256)
 k_attn_scores(int64_t *__restrict__ sc, int64_t *__restrict__ mx, const int64_t *__restrict__ qkv,
-              const int64_t *__restrict__ kc, const int *__restrict__ pos_arr, const int *__restrict__ seq_arr,
+              const KVView kv, const int *__restrict__ pos_arr, const int *__restrict__ seq_arr,
               int nh, int nkv, int hd, int max_seq, int Tcap,
               int64_t scale) {
     extern __shared__ __align__(16) int64_t smem[];
@@ -277,9 +340,10 @@ k_attn_scores(int64_t *__restrict__ sc, int64_t *__restrict__ mx, const int64_t 
             if (l == 0) qsum[hh] = t;
         }
     }
-    const int64_t *kb = kc + ((size_t)seq_arr[b] * max_seq + t0) * kvd + g * hd;
+    const size_t vb0 = ((size_t)seq_arr[b] * max_seq + t0) * nkv + g;   // vector of position t0, head g
     for (int e = threadIdx.x; e < nt * hd; e += blockDim.x) {
-        const int64_t v = kb[(size_t)(e / hd) * kvd + e % hd];
+        const size_t vec = vb0 + (size_t)(e / hd) * nkv;
+        const int64_t v = kv.at(vec * hd + e % hd, vec);
         kt[(e / hd) * kld + e % hd] = make_int2((int32_t)(v >> 32), (int32_t)((uint32_t)v ^ 0x80000000u));
     }
     __syncthreads();
@@ -338,14 +402,14 @@ k_attn_exp(int64_t *__restrict__ sc, const int64_t *__restrict__ mx, uint64_t *_
 // sums of fp_mul(p_t, v_t[d]) added atomically into out (wrapping, exact)
 __global__ void __launch_bounds__(256)
 k_attn_pv(int64_t *__restrict__ out, const int64_t *__restrict__ sc, const uint64_t *__restrict__ sm_,
-          const int64_t *__restrict__ vc, const int *__restrict__ pos_arr, const int *__restrict__ seq_arr,
+          const KVView kv, const int *__restrict__ pos_arr, const int *__restrict__ seq_arr,
           int nh, int nkv, int hd, int max_seq, int Tcap) {
     extern __shared__ __align__(16) int64_t smem[];
     const int tile = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int T = pos_arr[b] + 1, t0 = tile * ATT_TILE;
     if (t0 >= T) return;
     const int nt = min(ATT_TILE, T - t0);
-    const int grp = nh / nkv, dim = nh * hd, kvd = nkv * hd;
+    const int grp = nh / nkv, dim = nh * hd;
     int64_t *ps = smem;                // [grp][ATT_TILE]
     int64_t *vt = ps + grp * ATT_TILE; // [ATT_TILE][hd]
     for (int e = threadIdx.x; e < grp * ATT_TILE; e += blockDim.x) {
@@ -359,8 +423,11 @@ k_attn_pv(int64_t *__restrict__ out, const int64_t *__restrict__ sc, const uint6
         }
         ps[e] = p;
     }
-    const int64_t *vb = vc + ((size_t)seq_arr[b] * max_seq + t0) * kvd + g * hd;
-    for (int e = threadIdx.x; e < nt * hd; e += blockDim.x) vt[e] = vb[(size_t)(e / hd) * kvd + e % hd];
+    const size_t vb0 = ((size_t)seq_arr[b] * max_seq + t0) * nkv + g;
+    for (int e = threadIdx.x; e < nt * hd; e += blockDim.x) {
+        const size_t vec = vb0 + (size_t)(e / hd) * nkv;
+        vt[e] = kv.at(vec * hd + e % hd, vec);
+    }
     __syncthreads();
     for (int e = threadIdx.x; e < grp * hd; e += blockDim.x) {
         const int hh = e / hd, dd = e % hd;

@@ -111,6 +111,10 @@ struct iq_model {
     bool failed = false;        // the communicator was aborted: the model is unusable
     int64_t timeout_ms = 60000; // bounded host waits under tensor parallelism
     bool want_logits = false;   // decode steps also gather the full logits (TP; hashing callers)
+    int kv_kbits = 0, kv_vbits = 0;   // packed KV cache (K and V code widths); 0 = exact
+    std::vector<uint8_t *> kq;        // per layer [B][max_seq][kvd] K codes
+    std::vector<uint16_t *> vq;       // per layer V codes
+    std::vector<int64_t *> kmag, vmag; // per layer [B][max_seq][nkv] magnitudes
     bool sampling = false;      // steps draw with sample_token instead of argmax
     SampleState *d_samp = nullptr;   // [max_batch] sampling parameters and generator states
     int64_t *swork = nullptr;        // [rmax][vocab] sampling scratch
@@ -350,21 +354,33 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
         k_rope_kv<<<dim3((pairs + 255) / 256, R), 256, 0, s>>>(m->qkv, m->kc[l], m->vc[l], m->rcos, m->rsin,
                                                                pos, seq, S.nh_l, S.nkv_l, hd, c.max_seq_len);
         IQ_CHECK_LAUNCH();
-        const bool att_short = tmax > 0 && tmax <= m->att_short;
-        if (m->att_phased && !att_short) {
+        const bool packed = m->kv_kbits > 0;
+        if (packed) {   // kv_pack_vector of the rows' K and V (the exact values stay unread)
+            const int nwarp = R * S.nkv_l;
+            k_kv_pack<<<(nwarp + 7) / 8, 256, 0, s>>>(m->kq[l], m->vq[l], m->kmag[l], m->vmag[l], m->kc[l], m->vc[l],
+                                                     pos, seq, R, S.nkv_l, hd, c.max_seq_len, m->kv_kbits,
+                                                     m->kv_vbits);
+            IQ_CHECK_LAUNCH();
+        }
+        const KVView kview{m->kc[l], packed ? m->kq[l] : nullptr, nullptr, packed ? m->kmag[l] : nullptr,
+                           m->kv_kbits, S.nkv_l, hd};
+        const KVView vview{m->vc[l], nullptr, packed ? m->vq[l] : nullptr, packed ? m->vmag[l] : nullptr,
+                           m->kv_vbits, S.nkv_l, hd};
+        const bool att_short = !packed && tmax > 0 && tmax <= m->att_short;
+        if (packed || (m->att_phased && !att_short)) {
             const int grid_t = (c.max_seq_len + ATT_TILE - 1) / ATT_TILE;
             int64_t n = (int64_t)R * S.nh_l * hd;
             k_attn_init<<<(int)std::min<int64_t>((n + 255) / 256, 4096), 256, 0, s>>>(att_out, m->amx, m->asum, R,
                                                                                    S.nh_l, hd);
             IQ_CHECK_LAUNCH();
-            k_attn_scores<<<dim3(grid_t, S.nkv_l, R), 256, m->att_s1, s>>>(m->asc, m->amx, m->qkv, m->kc[l], pos,
+            k_attn_scores<<<dim3(grid_t, S.nkv_l, R), 256, m->att_s1, s>>>(m->asc, m->amx, m->qkv, kview, pos,
                                                                             seq, S.nh_l, S.nkv_l, hd, c.max_seq_len,
                                                                             c.max_seq_len, m->att_scale);
             IQ_CHECK_LAUNCH();
             k_attn_exp<<<dim3((c.max_seq_len + 255) / 256, S.nh_l, R), 256, 0, s>>>(m->asc, m->amx, m->asum, pos,
                                                                                    S.nh_l, c.max_seq_len);
             IQ_CHECK_LAUNCH();
-            k_attn_pv<<<dim3(grid_t, S.nkv_l, R), 256, m->att_s3, s>>>(att_out, m->asc, m->asum, m->vc[l], pos, seq,
+            k_attn_pv<<<dim3(grid_t, S.nkv_l, R), 256, m->att_s3, s>>>(att_out, m->asc, m->asum, vview, pos, seq,
                                                                         S.nh_l, S.nkv_l, hd, c.max_seq_len,
                                                                         c.max_seq_len);
         } else if (m->gqa_smem && !att_short)
@@ -515,7 +531,8 @@ static int dec_prepare(iq_model *m) {
     if (m->dec_ready || m->dec_mode == 0) return IQ_OK;
     const iq_config &c = m->c;
     const Shard &S = m->sh;
-    if (m->max_batch != 1 || S.P != 1 || !m->att_phased || S.it_l % 8 || c.head_dim > 256) return IQ_OK;
+    if (m->max_batch != 1 || S.P != 1 || !m->att_phased || S.it_l % 8 || c.head_dim > 256 || m->kv_kbits)
+        return IQ_OK;
     auto bf = [](const Packed &P) { return P.fmt == IQ_FMT_BF16 && (size_t)8 * (P.Kp + 16) <= 100 * 1024; };
     if (!bf(m->plm)) return IQ_OK;
     for (int l = 0; l < c.num_layers; l++)
@@ -856,8 +873,10 @@ IQ_API int iq_model_destroy(iq_model *m) {
                     m->d_ptok, m->d_ppos, m->d_pseq, m->d_layers, m->bar, m->argv, m->pairs_l, m->pairs_g,
                     m->d_samp, m->swork};
     for (void *p : bufs) if (p) cudaFree(p);
-    for (auto *v : {&m->norm1, &m->wqkv, &m->wo, &m->norm2, &m->wgu, &m->wdown, &m->kc, &m->vc})
+    for (auto *v : {&m->norm1, &m->wqkv, &m->wo, &m->norm2, &m->wgu, &m->wdown, &m->kc, &m->vc, &m->kmag, &m->vmag})
         for (int64_t *p : *v) if (p) cudaFree(p);
+    for (uint8_t *p : m->kq) if (p) cudaFree(p);
+    for (uint16_t *p : m->vq) if (p) cudaFree(p);
     for (auto *v : {&m->pqkv, &m->po, &m->pgu, &m->pdown})
         for (Packed &P : *v) free_packed(&P);
     free_packed(&m->plm);
@@ -909,6 +928,16 @@ IQ_API int iq_model_reset(iq_model *m) {
     for (int l = 0; l < m->c.num_layers; l++) {
         IQ_CUDA(cudaMemsetAsync(m->kc[l], 0, kvb, m->s));
         IQ_CUDA(cudaMemsetAsync(m->vc[l], 0, kvb, m->s));
+    }
+    if (m->kv_kbits) {   // kv_cache_reset also clears the packed arrays (llama_int.c:1160-1172)
+        const size_t ne = (size_t)m->max_batch * m->c.max_seq_len * m->kvd_l;
+        const size_t nv = (size_t)m->max_batch * m->c.max_seq_len * m->sh.nkv_l;
+        for (int l = 0; l < m->c.num_layers; l++) {
+            IQ_CUDA(cudaMemsetAsync(m->kq[l], 0, ne, m->s));
+            IQ_CUDA(cudaMemsetAsync(m->vq[l], 0, ne * 2, m->s));
+            IQ_CUDA(cudaMemsetAsync(m->kmag[l], 0, nv * 8, m->s));
+            IQ_CUDA(cudaMemsetAsync(m->vmag[l], 0, nv * 8, m->s));
+        }
     }
     // a persistent decode kernel that gave up on a barrier left it abandoned
     if (m->bar) IQ_CUDA(cudaMemsetAsync(m->bar, 0, sizeof(GridBar), m->s));
@@ -1227,6 +1256,33 @@ IQ_API int iq_sample_dev(const int64_t *d_logits, int rows, int V, int64_t tempe
     if (e != cudaSuccess) return cuda_fail(e);
     for (int r = 0; r < rows; r++) { rng[2 * r] = h[r].s0; rng[2 * r + 1] = h[r].s1; }
     return IQ_OK;
+}
+
+IQ_API int iq_model_set_kv_packed(iq_model *m, int k_bits, int v_bits) {
+    if (!m) return IQ_ERR_ARG;
+    const bool off = k_bits == 0 && v_bits == 0;
+    if (!off && (k_bits < 1 || k_bits > 8 || v_bits < 1 || v_bits > 16)) return IQ_ERR_ARG;  // llama_int.c:4742-4747
+    if (!off && !m->att_phased) return IQ_ERR_UNSUPPORTED;
+    IQ_CUDA(cudaSetDevice(m->dev));
+    invalidate_exec(m);
+    if (!off && m->kq.empty()) {
+        const size_t ne = (size_t)m->max_batch * m->c.max_seq_len * m->kvd_l;
+        const size_t nv = (size_t)m->max_batch * m->c.max_seq_len * m->sh.nkv_l;
+        const int L = m->c.num_layers;
+        m->kq.assign(L, nullptr);
+        m->vq.assign(L, nullptr);
+        m->kmag.assign(L, nullptr);
+        m->vmag.assign(L, nullptr);
+        for (int l = 0; l < L; l++) {
+            DALLOC(m->kq[l], ne);
+            DALLOC(m->vq[l], ne * 2);
+            DALLOC(m->kmag[l], nv * 8);
+            DALLOC(m->vmag[l], nv * 8);
+        }
+    }
+    m->kv_kbits = k_bits;
+    m->kv_vbits = v_bits;
+    return iq_model_reset(m);
 }
 
 IQ_API int iq_model_set_timeout(iq_model *m, int64_t ms) {

@@ -82,6 +82,7 @@ SIGNATURES = {
     "iq_model_weight_bytes": (_I, [_P, _P, _P]),
     "iq_model_set_decode": (_I, [_P, _I]),
     "iq_model_set_timeout": (_I, [_P, _I64]),
+    "iq_model_set_kv_packed": (_I, [_P, _I, _I]),
     "iq_selftest_watchdog": (_I, [_I, _P, _P]),
     "iq_model_decode_info": (_I, [_P, _P, _P]),
     "iq_bench_grid_sync": (_I, [_I, _I, _I, _P]),
@@ -461,6 +462,10 @@ class Model:
     def set_attention(self, short_max):
         """Contexts up to short_max use the single-kernel attention (0 = phased only)."""
         _call("iq_model_set_attention", self.h, short_max)
+
+    def set_kv_packed(self, k_bits, v_bits):
+        """The reference's --kv-packed KbVb cache (0, 0 = exact)."""
+        _call("iq_model_set_kv_packed", self.h, k_bits, v_bits)
 
     def set_decode(self, mode):
         """1 = persistent decode kernel where it applies (default), 0 = one kernel per op."""

@@ -92,6 +92,7 @@ _REF_SIG = {
     "ref_sample_token": (_I, [_P, _I, _I64, _I, _I64, _P]),
     "ref_rng_seed": (None, [_U64, _P]),
     "ref_model_generate_sampled": (_I, [_P, _P, _I, _I, _I64, _I, _I64, _U64, _P]),
+    "ref_set_kv_packed": (None, [_I, _I]),
 }
 
 

@@ -18,6 +18,7 @@
  *                         llama_int.c:2807-2886, 3067-3135
  *   ref_sample_token   -> sample_token with sample_params_t   llama_int.c:2958-3039
  *   ref_model_generate_sampled -> generate(..., sp)          llama_int.c:3067-3135
+ *   ref_set_kv_packed  -> the --kv-packed switch g_kv_quant  llama_int.c:4740-4751
  *   ref_model_open_mgw -> mgw_load (mmap, layers cached) or mgw_load_streaming
  *                         (layers pread into fresh buffers and freed after
  *                         every layer), llama_int.c:2344-2803
@@ -234,4 +235,13 @@ REFAPI int ref_model_generate_sampled(void *h, const int *prompt, int prompt_len
     sp.top_p = top_p;
     rng_seed(&sp.rng, seed);
     return generate((llama_model_t *)h, prompt, prompt_len, max_new, out_tokens, &sp);
+}
+
+/* The reference's --kv-packed KbVb switch (llama_int.c:4740-4751): affects
+ * models created afterwards (kv_cache_init reads it); (0, 0) turns it off. */
+REFAPI void ref_set_kv_packed(int k_bits, int v_bits) {
+    g_kv_quant.enabled = k_bits > 0;
+    g_kv_quant.packed = k_bits > 0;
+    g_kv_quant.k_bits = k_bits;
+    g_kv_quant.v_bits = v_bits;
 }

@@ -334,3 +334,48 @@ def test_generate_sampled_matches_oracle_and_reference_golden():
                                      run["top_p"], run["seed"])
         assert toks == run["tokens"], run["seed"]
     m.close()
+
+
+# ------------------------------------------------------------- packed KV cache
+
+@pytest.mark.skipif(orc.ref() is None, reason="oracle/_ref not built")
+@pytest.mark.parametrize("kb,vb", [(8, 10), (4, 16), (1, 1)])
+def test_packed_kv_cache_matches_reference(kb, vb):
+    """--kv-packed KbVb (per-vector L-inf magnitude + b-bit codes, llama_int.c:
+    1197-1235, 1392-1501): tokens equal the reference's own generate() with
+    the same switch, every logit hash equals its llama_forward's, for a prompt
+    prefilled in batched rows and decode past several 64-position tiles; the
+    exact cache again afterwards gives the exact goldens."""
+    c = dict(configs.TINY_TEST, max_seq=200)
+    w = helpers.model_weights(9, c)
+    R = orc.ref()
+    pr = orc.synth_tokens(9, "prompt:packed", 90, c["vocab"])
+    R.ref_set_kv_packed(kb, vb)
+    try:
+        mr = helpers.OracleModel(c, w, lib=R, prefix="ref_")
+        want, _ = mr.generate(pr, 60)
+        mr.reset()
+        lh = 1469598103934665603
+        toks = [int(t) for t in pr]
+        for pos in range(len(toks) + 59):
+            a, lg = mr.forward(toks[pos], pos)
+            lh = orc.O.iqo_fnv_array(lh, orc.p(lg), lg.size)
+            if pos >= len(pr) - 1:
+                if pos > len(pr) - 1 and a == 2:
+                    break
+                toks.append(a)
+        mr.close()
+    finally:
+        R.ref_set_kv_packed(0, 0)
+    m = iq.Model(c)
+    m.load(w)
+    m.set_kv_packed(kb, vb)
+    got, glh = m.generate(pr, 60, logit_hash=True)
+    got2, _ = m.generate(pr, 60)
+    assert got == got2 == want
+    assert glh == lh
+    m.set_kv_packed(0, 0)
+    o = helpers.OracleModel(c, w)
+    assert m.generate(pr, 30)[0] == o.generate(pr, 30)[0]
+    o.close()
+    m.close()
