@@ -12,6 +12,7 @@
 #include "iq_gemm.cuh"
 #include "iq_planes.cuh"
 #include "iq_tc_gemm.cuh"
+#include "iq_planes_smem.cuh"
 #include "iq_elem.cuh"
 #include "iq_peak.cuh"
 
@@ -365,8 +366,66 @@ static int rows_setup(RowsKernel *k, int *occ) {
 // still one wave and at least two column tiles per warp; otherwise S = 1 and
 // one wave of CTAs loops over the row tiles. IQ_ERR_UNSUPPORTED = use the
 // stream-K kernel.
+// The bf16-form row-owned matvec with the weight slice bulk-copied into shared
+// memory (k_matvec_rows_smem): used when one wave of CTAs, each holding one
+// row tile's column range, fits; cluster size = the smallest S in 1, 2, 4, 8
+// that fits (IQ_MV_SMEM=0 disables it; IQ_MV_SMEM_S forces S).
+static int launch_matvec_rows_smem(int64_t *out, const Packed &P, const int64_t *x, cudaStream_t s, int add,
+                                   const int64_t *nrm_w) {
+    static const int enabled = getenv("IQ_MV_SMEM") ? atoi(getenv("IQ_MV_SMEM")) : 1;
+    static const int s_force = getenv("IQ_MV_SMEM_S") ? atoi(getenv("IQ_MV_SMEM_S")) : 0;
+    if (!enabled || P.fmt != IQ_FMT_BF16) return IQ_ERR_UNSUPPORTED;
+    static int smem_max[64] = {0};   // per device: the dynamic shared memory the kernel may use
+    int dev = 0;
+    IQ_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return IQ_ERR_UNSUPPORTED;
+    if (!smem_max[dev]) {
+        int optin = 0;
+        cudaFuncAttributes fa;
+        IQ_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+        IQ_CUDA(cudaFuncGetAttributes(&fa, k_matvec_rows_smem));
+        const int lim = optin - (int)fa.sharedSizeBytes;
+        IQ_CUDA(cudaFuncSetAttribute(k_matvec_rows_smem, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
+        smem_max[dev] = lim;
+    }
+    const int RT = P.Mp / 16, KT = P.Kp / 32;
+    const size_t xbytes = ((size_t)8 * (P.Kp + 16) + 127) / 128 * 128;
+    for (int S = 1; S <= 8; S *= 2) {
+        if (s_force && S != s_force) continue;
+        const int per = (KT + S - 1) / S;
+        const size_t smem = xbytes + (size_t)per * 1024;
+        if (smem > (size_t)smem_max[dev]) continue;
+        int occ = 0;
+        IQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_matvec_rows_smem, 256, smem));
+        if (occ < 1 || (int64_t)RT * S > (int64_t)dev_info().sms * occ) continue;
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = (unsigned)S;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        cfg.gridDim = dim3((unsigned)(RT * S));
+        cfg.blockDim = dim3(256);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = s;
+        cfg.attrs = attr;
+        cfg.numAttrs = S > 1 ? 2 : 1;
+        IQ_CUDA(cudaLaunchKernelEx(&cfg, k_matvec_rows_smem, out, (const uint4 *)P.planes, packed_res(P), x, P.M,
+                                   P.N, P.Kp, add, nrm_w, (int)xbytes));
+        IQ_CHECK_LAUNCH();
+        return IQ_OK;
+    }
+    return IQ_ERR_UNSUPPORTED;
+}
+
 int launch_matvec_rows(int64_t *out, const Packed &P, const int64_t *x, cudaStream_t s, int add,
                        const int64_t *nrm_w, size_t smem) {
+    {
+        const int rc = launch_matvec_rows_smem(out, P, x, s, add, nrm_w);
+        if (rc != IQ_ERR_UNSUPPORTED) return rc;
+    }
     // IQ_MV_ROWS: 0 = stream-K only, 1 = row-owned when one wave covers the
     // rows, 2 (default) = row-owned also up to two waves (CTAs loop over tiles)
     static const int mode = getenv("IQ_MV_ROWS") ? atoi(getenv("IQ_MV_ROWS")) : 2;
