@@ -70,10 +70,17 @@ __device__ __forceinline__ i128 d_mul128(int64_t a, int64_t b) {
 // Row b = (sequence seq_arr[b], position pos_arr[b]) attends to positions
 // 0..pos of its sequence: a batched prefill row computes exactly what the
 // reference's sequential call at that position computes.
+// ROPE (decode steps, one row per sequence): the CTA also applies RoPE itself
+// (rope_apply, llama_int.c:997-1008) to its q head and to its kv head's k, and
+// writes the cache row at pos (llama_int.c:1415-1416) before reading the
+// cache; every CTA of a kv group writes the same values, so each reads its own
+// write and no separate RoPE / cache-write kernel runs.
+template <bool ROPE>
 __global__ void k_attention(int64_t *__restrict__ out, const int64_t *__restrict__ qkv,
-                            const int64_t *__restrict__ kc, const int64_t *__restrict__ vc,
+                            int64_t *__restrict__ kc, int64_t *__restrict__ vc,
                             const int *__restrict__ pos_arr, const int *__restrict__ seq_arr, int nh, int nkv,
-                            int hd, int max_seq, int64_t scale) {
+                            int hd, int max_seq, int64_t scale, const int64_t *__restrict__ rcos,
+                            const int64_t *__restrict__ rsin) {
     extern __shared__ __align__(16) int64_t sm[];
     __shared__ uint64_t red[64];
     const int h = blockIdx.x, b = blockIdx.y;
@@ -82,7 +89,23 @@ __global__ void k_attention(int64_t *__restrict__ out, const int64_t *__restrict
     int64_t *qs = sm;            // [hd]
     int64_t *sc = sm + hd;       // [T]
     const int64_t *q = qkv + (size_t)b * (dim + 2 * kvd) + h * hd;
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) qs[d] = q[d];
+    if (ROPE) {
+        const int pos = T - 1, half = hd / 2, sqr = seq_arr[b];
+        const int64_t *c = rcos + (size_t)pos * half, *sn = rsin + (size_t)pos * half;
+        const int64_t *k = qkv + (size_t)b * (dim + 2 * kvd) + dim + kvh * hd;
+        int64_t *kdst = kc + ((size_t)sqr * max_seq + pos) * kvd + kvh * hd;
+        int64_t *vdst = vc + ((size_t)sqr * max_seq + pos) * kvd + kvh * hd;
+        for (int i = threadIdx.x; i < half; i += blockDim.x) {
+            const int64_t x0 = q[i], x1 = q[i + half], k0 = k[i], k1 = k[i + half];
+            qs[i] = d_mul(x0, c[i]) - d_mul(x1, sn[i]);
+            qs[i + half] = d_mul(x1, c[i]) + d_mul(x0, sn[i]);
+            kdst[i] = d_mul(k0, c[i]) - d_mul(k1, sn[i]);
+            kdst[i + half] = d_mul(k1, c[i]) + d_mul(k0, sn[i]);
+        }
+        for (int i = threadIdx.x; i < hd; i += blockDim.x) vdst[i] = k[kvd + i];
+    } else {
+        for (int d = threadIdx.x; d < hd; d += blockDim.x) qs[d] = q[d];
+    }
     __syncthreads();
     const int sq = seq_arr[b];
     const int64_t *kb = kc + (size_t)sq * max_seq * kvd + kvh * hd;

@@ -351,10 +351,15 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
     int64_t *act_out = tp ? m->act_l : m->act;
     for (int l = 0; l < c.num_layers; l++) {
         if ((rc = norm_proj(m->qkv, m->pqkv[l], m->tqkv[l], m->hidden, m->norm1[l], R))) return rc;
-        k_rope_kv<<<dim3((pairs + 255) / 256, R), 256, 0, s>>>(m->qkv, m->kc[l], m->vc[l], m->rcos, m->rsin,
-                                                               pos, seq, S.nh_l, S.nkv_l, hd, c.max_seq_len);
-        IQ_CHECK_LAUNCH();
         const bool packed = m->kv_kbits > 0;
+        // decode rows with short contexts: RoPE and the cache write happen inside
+        // k_attention (one launch fewer per layer)
+        const bool fused_rope = decode && !packed && tmax > 0 && tmax <= m->att_short;
+        if (!fused_rope) {
+            k_rope_kv<<<dim3((pairs + 255) / 256, R), 256, 0, s>>>(m->qkv, m->kc[l], m->vc[l], m->rcos, m->rsin,
+                                                                   pos, seq, S.nh_l, S.nkv_l, hd, c.max_seq_len);
+            IQ_CHECK_LAUNCH();
+        }
         if (packed) {   // kv_pack_vector of the rows' K and V (the exact values stay unread)
             const int nwarp = R * S.nkv_l;
             k_kv_pack<<<(nwarp + 7) / 8, 256, 0, s>>>(m->kq[l], m->vq[l], m->kmag[l], m->vmag[l], m->kc[l], m->vc[l],
@@ -387,10 +392,14 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
             k_attention_gqa<<<dim3(S.nh_l / m->hpc, R), 256, m->gqa_smem, s>>>(
                 att_out, m->qkv, m->kc[l], m->vc[l], pos, seq, S.nh_l, S.nkv_l, hd, c.max_seq_len, c.max_seq_len,
                 m->hpc);
+        else if (fused_rope)
+            k_attention<true><<<dim3(S.nh_l, R), 256, m->attn_smem, s>>>(att_out, m->qkv, m->kc[l], m->vc[l], pos,
+                                                                         seq, S.nh_l, S.nkv_l, hd, c.max_seq_len,
+                                                                         m->att_scale, m->rcos, m->rsin);
         else
-            k_attention<<<dim3(S.nh_l, R), 256, m->attn_smem, s>>>(att_out, m->qkv, m->kc[l], m->vc[l], pos,
-                                                                   seq, S.nh_l, S.nkv_l, hd, c.max_seq_len,
-                                                                   m->att_scale);
+            k_attention<false><<<dim3(S.nh_l, R), 256, m->attn_smem, s>>>(att_out, m->qkv, m->kc[l], m->vc[l], pos,
+                                                                          seq, S.nh_l, S.nkv_l, hd, c.max_seq_len,
+                                                                          m->att_scale, nullptr, nullptr);
         IQ_CHECK_LAUNCH();
         if (tp) {
             if ((rc = gather_rows(m, m->att_l, m->att, R, S.nh_l * hd))) return rc;
@@ -831,7 +840,9 @@ IQ_API int iq_model_create_tp(const iq_config *cfg, int max_batch, int device, i
     }
     if (!m->att_phased && !m->gqa_smem && m->attn_smem > 200 * 1024) { iq_model_destroy(m); return IQ_ERR_UNSUPPORTED; }
     if (m->attn_smem > 48 * 1024 && m->attn_smem <= 200 * 1024) {
-        e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->attn_smem);
+        e = cudaFuncSetAttribute(k_attention<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->attn_smem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_attention<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->attn_smem);
         if (e != cudaSuccess) { iq_model_destroy(m); return cuda_fail(e); }
     }
     {

@@ -99,3 +99,4 @@ k_matvec_rows_smem(int64_t *__restrict__ out, const uint4 *__restrict__ planes, 
 }
 
 }  // namespace iq
+
