@@ -417,7 +417,41 @@ static int launch_matvec_rows_smem(int64_t *out, const Packed &P, const int64_t 
         IQ_CHECK_LAUNCH();
         return IQ_OK;
     }
-    return IQ_ERR_UNSUPPORTED;
+    // a few row tiles per CTA (up to 3 per SM): a ring of whole-row-tile slots
+    // per CTA (measured: 2048 -> 5632 at 10.9 us against 14.7 for the two-wave
+    // row-owned kernel; beyond that stream-K wins, e.g. the 2048 -> 32000 LM
+    // head at 35 us against 53)
+    static const int pipe_on = getenv("IQ_MV_PIPE") ? atoi(getenv("IQ_MV_PIPE")) : 1;
+    if (!pipe_on || RT > 3 * dev_info().sms) return IQ_ERR_UNSUPPORTED;
+    static int pmax[64] = {0};
+    if (!pmax[dev]) {
+        int optin = 0;
+        cudaFuncAttributes fa;
+        IQ_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+        IQ_CUDA(cudaFuncGetAttributes(&fa, k_matvec_rows_pipe));
+        pmax[dev] = optin - (int)fa.sharedSizeBytes;
+        IQ_CUDA(cudaFuncSetAttribute(k_matvec_rows_pipe, cudaFuncAttributeMaxDynamicSharedMemorySize, pmax[dev]));
+    }
+    const size_t tile = (size_t)KT * 1024;
+    int stages = 3;
+    while (stages > 2 && xbytes + stages * tile > (size_t)pmax[dev]) stages--;
+    if (xbytes + stages * tile > (size_t)pmax[dev]) return IQ_ERR_UNSUPPORTED;
+    const size_t smem = xbytes + stages * tile;
+    const int grid = std::min(RT, dev_info().sms);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    IQ_CUDA(cudaLaunchKernelEx(&cfg, k_matvec_rows_pipe, out, (const uint4 *)P.planes, packed_res(P), x, P.M, P.N,
+                               P.Kp, add, nrm_w, (int)xbytes, stages));
+    IQ_CHECK_LAUNCH();
+    return IQ_OK;
 }
 
 int launch_matvec_rows(int64_t *out, const Packed &P, const int64_t *x, cudaStream_t s, int add,

@@ -100,3 +100,79 @@ k_matvec_rows_smem(int64_t *__restrict__ out, const uint4 *__restrict__ planes, 
 
 }  // namespace iq
 
+namespace iq {
+
+// Up to a few row tiles per CTA (more tiles than one wave of CTAs): CTA c
+// takes row tiles c, c + G, c + 2G, ... through a ring of `stages`
+// shared-memory slots of one whole row tile each (KT x 1 KB), refilled by the
+// bulk-copy engine as soon as the CTA has consumed a slot; the first `stages`
+// tiles are requested before the dependency wait. The digits of x are staged
+// once per CTA for all its tiles. 8 warps split each tile's column tiles; the
+// rows are reduced and written as in k_matvec_rows (S = 1).
+__global__ void __launch_bounds__(256, 1)
+k_matvec_rows_pipe(int64_t *__restrict__ out, const uint4 *__restrict__ planes, const PackedRes R,
+                   const int64_t *__restrict__ xg, int M, int N, int Kp, int add, const int64_t *__restrict__ nrm_w,
+                   int wsm_off, int stages) {
+    extern __shared__ __align__(128) unsigned char wsm_raw[];
+    unsigned char *xd = wsm_raw;
+    __shared__ __align__(16) unsigned long long wpart[8][16][2];
+    __shared__ __align__(16) unsigned long long cpart[8][16][2];
+    __shared__ __align__(8) uint64_t full[4];
+    constexpr int TS = 64;
+    const int ld = Kp + 16;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
+    const int KT = Kp / 32, RT = (M + 15) / 16;
+    const uint32_t tile_bytes = (uint32_t)KT * TS * 16;
+    const int G = gridDim.x, ntiles = (int)blockIdx.x < RT ? (RT - 1 - (int)blockIdx.x) / G + 1 : 0;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; s++) mbar_init(&full[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    auto request = [&](int i) {   // tile i of this CTA into slot i % stages
+        const int s = i % stages, rt = (int)blockIdx.x + i * G;
+        mbar_expect_tx(&full[s], tile_bytes);
+        const unsigned char *src = reinterpret_cast<const unsigned char *>(planes + (size_t)rt * KT * TS);
+        unsigned char *dst = wsm_raw + wsm_off + (size_t)s * tile_bytes;
+        for (uint32_t off = 0; off < tile_bytes; off += 32768u)
+            bulk_g2s(dst + off, src + off, min(32768u, tile_bytes - off), &full[s]);
+    };
+    if (threadIdx.x == 0)
+        for (int i = 0; i < stages && i < ntiles; i++) request(i);
+    RowPre pre = {};
+    if (threadIdx.x < 16 && ntiles > 0 && (int)(blockIdx.x * 16 + threadIdx.x) < M)
+        pre = row_pre(blockIdx.x * 16 + threadIdx.x, R);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    i128 xs = 0;
+    stage_digits(xd, ld, xg, N, Kp, nrm_w, &xs);
+    const unsigned char *xb = xd + g * ld + 4 * t;
+    bool ok = true;
+    for (int i = 0; i < ntiles; i++) {
+        const int s = i % stages, rt = (int)blockIdx.x + i * G;
+        int c[3][4];
+#pragma unroll
+        for (int p = 0; p < 3; p++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) c[p][q] = 0;
+        if (ok && !mbar_wait(&full[s], (uint32_t)(i / stages) & 1u)) ok = false;
+        if (ok) {
+            const uint4 *wsm = reinterpret_cast<const uint4 *>(wsm_raw + wsm_off + (size_t)s * tile_bytes);
+            for (int j = warp; j < KT; j += 8) {
+                const uint4 *tile = wsm + (size_t)j * TS + lane;
+                const uint4 w2[2] = {tile[0], tile[32]};
+                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(xb + j * 32);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t *>(xb + j * 32 + 16);
+                mma_tile_bf(c, w2, b0, b1);
+            }
+        }
+        i128 r0 = 0, r1 = 0;
+        fold_planes(c, t, r0, r1);
+        // every warp is done with slot s once rows_tile_end's barriers pass
+        rows_tile_end(r0, r1, rt, (int)blockIdx.x, pre, 1, 0, M, add, out, R, xd, ld, xg, xs, &wpart[0][0][0],
+                      &cpart[0][0][0]);
+        if (threadIdx.x == 0 && ok && i + stages < ntiles) request(i + stages);
+    }
+}
+
+}  // namespace iq
