@@ -587,6 +587,13 @@ def run_model_workload(args):
     ms = m.decode_steps_timed(pos0, dec)
     clocks = clk.stop()
     ms = _max_over_ranks(dist, ms)
+    if getattr(args, "profile_step", False):
+        # one decode step inside a profiler range (ncu --profile-from-start off)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        m.decode_steps_timed(pos0, 1)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
     # e2e decode through generate(): prompt in, tokens out (host buffers)
     e2e = None
     if wl == "cfg0":
@@ -599,11 +606,11 @@ def run_model_workload(args):
     tok_s = B * dec / (ms / 1e3)
     d, L, V, it = cfg["dim"], cfg["n_layers"], cfg["vocab"], cfg["inter"]
     kvd = cfg["n_kv_heads"] * cfg["head_dim"]
-    wbytes = 8 * (L * (d * (d + 2 * kvd) + d * d + 3 * d * it) + V * d)
-    kv_bytes = 8 * 2 * L * kvd * (pos0 + dec / 2) * B
+    wbytes, _ = m.weight_bytes()   # this rank's packed weight bytes read per decode step
+    kv_bytes = 8 * 2 * L * kvd * (pos0 + dec / 2) * B / world
     peak, peak_kind = measured_peak()
     step_s = ms / 1e3 / dec
-    ach = (wbytes / world + kv_bytes / world) / step_s / 1e9  # per GPU
+    ach = (wbytes + kv_bytes) / step_s / 1e9  # per GPU
     line = {
         "metric": {"cfg0": "TinyLlama greedy decode tokens/s (B=1), bit-exact",
                    "cfg3": "TinyLlama batch-64 decode tokens/s after 2048-token prefills, bit-exact",
@@ -616,7 +623,9 @@ def run_model_workload(args):
         "prefill_s": t_prefill, "prefill_tokens_per_s": B * plen / t_prefill, "load_s": t_load,
         "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
                      "peak_source": peak_kind, "kernel": "decode step (all kernels)",
-                     "bytes_per_step_per_gpu": (wbytes + kv_bytes) / world, "traffic": None},
+                     "bytes_per_step_per_gpu": wbytes + kv_bytes,
+                     "bytes_note": "packed weight bytes (iq_model_weight_bytes) + int64 KV reads",
+                     "traffic": None},
         "gpu_launches": None, "clocks": clocks,
     }
     if e2e:
@@ -672,6 +681,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
     ap.add_argument("--headline-only", action="store_true",
                     help="config 1 only (no config-0 decode / config-2 GEMM extras)")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="model workloads: run one extra decode step inside cudaProfilerStart/Stop")
     ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg0", "cfg2", "cfg3", "cfg4"],
                     help="cfg1 (default, the headline): M=1 matvec microbench")
     args = ap.parse_args()

@@ -69,15 +69,29 @@ __device__ __forceinline__ i128 d_sdiv128_64(i128 a, int64_t b) {
     return (na != nb) ? (i128)((u128)0 - q) : (i128)q;
 }
 
-// fp_div (fp_math.h:508-524): sign-magnitude |a| << 48, truncating divide.
+// fp_div (fp_math.h:508-524): sign-magnitude |a| << 48, truncating divide,
+// q = floor(|a| 2^48 / |b|) with the sign of a b.
+// Fast path: a double estimate of the quotient (three roundings of relative
+// size 2^-53 each: |a|, |b| and the quotient) is within 3/8 of the exact value
+// while it is below 2^50, so its truncation is q - 1, q or q + 1; one exact
+// remainder r = |a| 2^48 - q' |b| (|r| < 2 |b| < 2^62, so its low 64 bits are
+// exact) picks q. Larger quotients or divisors take the 128 / 64 long division.
 // b == 0 never occurs on the reference path (its callers guard it); 0 is returned.
 __device__ __forceinline__ int64_t d_div(int64_t a, int64_t b) {
     if (b == 0) return 0;
     uint64_t ma = a < 0 ? (uint64_t)0 - (uint64_t)a : (uint64_t)a;
     uint64_t mb = b < 0 ? (uint64_t)0 - (uint64_t)b : (uint64_t)b;
-    // |a| << 48 as (hi, lo): hi < 2^47 so the 128/64 division has hi < mb or not.
-    u128 q = d_udiv128_64((u128)ma << 48, mb);
-    uint64_t ql = (uint64_t)q;
+    uint64_t ql;
+    const double qd = (double)ma * 281474976710656.0 / (double)mb;   // 2^48 |a| / |b|
+    if (qd < 1125899906842624.0 && mb < (1ull << 61)) {              // 2^50
+        ql = (uint64_t)qd;
+        const int64_t r = (int64_t)((ma << 48) - ql * mb);
+        if (r < 0) ql--;
+        else if ((uint64_t)r >= mb) ql++;
+    } else {
+        // |a| << 48 as (hi, lo): hi < 2^47 so the 128/64 division has hi < mb or not.
+        ql = (uint64_t)d_udiv128_64((u128)ma << 48, mb);
+    }
     return ((a < 0) != (b < 0)) ? (int64_t)((uint64_t)0 - ql) : (int64_t)ql;
 }
 

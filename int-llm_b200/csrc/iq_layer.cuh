@@ -262,6 +262,17 @@ struct KVView {
         // (2q + 1) M >= 0: the division by 2^b is a floor, i.e. a shift
         return (int64_t)(((i128)(2 * q + 1) * M) >> bits) - M;
     }
+    // elements elem .. elem + 3 of vector vec (elem a multiple of 4)
+    __device__ __forceinline__ void at4(size_t elem, size_t vec, int64_t (&e)[4]) const {
+        if (!k8 && !v16) {
+            const longlong2 *p = reinterpret_cast<const longlong2 *>(x + elem);
+            const longlong2 a = p[0], c = p[1];
+            e[0] = a.x; e[1] = a.y; e[2] = c.x; e[3] = c.y;
+            return;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) e[i] = at(elem + i, vec);
+    }
 };
 
 // kv_pack_vector (llama_int.c:1197-1218) for the rows' K and V at their
@@ -397,6 +408,150 @@ k_attn_scores(int64_t *__restrict__ sc, int64_t *__restrict__ mx, const int64_t 
     }
 }
 
+// One m16n8k32 integer MMA, D += A B, A (16 x 32, row) and B (32 x 8, col)
+// bytes unsigned or signed (AS, BS).
+template <bool AS, bool BS>
+__device__ __forceinline__ void mma_s32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+#define IQ_MMA_S32(TA, TB)                                                                               \
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32." TA "." TB ".s32 "                             \
+                 "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"                                 \
+                 : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])                                        \
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1))
+    if (AS && BS) IQ_MMA_S32("s8", "s8");
+    else if (AS) IQ_MMA_S32("s8", "u8");
+    else if (BS) IQ_MMA_S32("u8", "s8");
+    else IQ_MMA_S32("u8", "u8");
+#undef IQ_MMA_S32
+}
+
+// Byte planes of four consecutive int64 (two's complement, little endian):
+// o[i] holds byte i of e[0], e[1], e[2], e[3] in its bytes 0..3.
+__device__ __forceinline__ void byte_planes4(const int64_t (&e)[4], uint32_t (&o)[8]) {
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+        const uint32_t w0 = (uint32_t)((uint64_t)e[0] >> (32 * half)), w1 = (uint32_t)((uint64_t)e[1] >> (32 * half));
+        const uint32_t w2 = (uint32_t)((uint64_t)e[2] >> (32 * half)), w3 = (uint32_t)((uint64_t)e[3] >> (32 * half));
+        const uint32_t x01 = __byte_perm(w0, w1, 0x5140), x23 = __byte_perm(w2, w3, 0x5140);
+        const uint32_t y01 = __byte_perm(w0, w1, 0x7362), y23 = __byte_perm(w2, w3, 0x7362);
+        o[4 * half + 0] = __byte_perm(x01, x23, 0x5410);
+        o[4 * half + 1] = __byte_perm(x01, x23, 0x7632);
+        o[4 * half + 2] = __byte_perm(y01, y23, 0x5410);
+        o[4 * half + 3] = __byte_perm(y01, y23, 0x7632);
+    }
+}
+
+// Phase 1 on the int8 tensor cores: the same scores as k_attn_scores.
+// Each int64 is 7 unsigned bytes and a signed top byte, x = sum_i x_i 2^(8i),
+// so q . k = sum_(i,j) 2^(8(i+j)) sum_d q_i k_j. The (7, 7) pair only adds
+// multiples of 2^112 and is dropped: (q . k >> 48) mod 2^64, the value the
+// reference keeps, depends on q . k mod 2^112 alone. The pairs of each
+// diagonal s = i + j accumulate into one s32 (at most 8 pairs x hd terms of
+// |byte product| < 2^16: < 2^27 for hd <= 256) and the 14 diagonals are
+// recombined in 128 bits.
+// A warp takes 16-position tiles (MMA rows: keys) against 8 query heads (MMA
+// columns; a kv group of more than 8 heads takes several passes, missing heads
+// read as zero). K and Q fragments come straight from global memory into
+// registers and are transposed to byte planes with byte permutes; the raw K of
+// the warp's next (tile, 32-wide d step) is loaded before the MMAs of the
+// current one, so the loads overlap the tensor work. 8 warps x ATT_TC_TPW
+// tiles = ATT_TC_POS positions per CTA; no shared memory.
+#define ATT_TC_TPW 2
+#define ATT_TC_POS (128 * ATT_TC_TPW)
+__global__ void __launch_bounds__(256)
+k_attn_scores_tc(int64_t *__restrict__ sc, int64_t *__restrict__ mx, const int64_t *__restrict__ qkv,
+                 const KVView kv, const int *__restrict__ pos_arr, const int *__restrict__ seq_arr,
+                 int nh, int nkv, int hd, int max_seq, int Tcap, int64_t scale) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
+    const int g = blockIdx.y, b = blockIdx.z;
+    const int T = pos_arr[b] + 1;
+    const int tbase = blockIdx.x * ATT_TC_POS + warp * 16;   // tile k of this warp: tbase + 128 k
+    if (tbase >= T) return;   // warp-uniform; the kernel has no CTA-wide barrier
+    const int ntile = min(ATT_TC_TPW, (T - tbase + 127) / 128);
+    const int grp = nh / nkv, dim = nh * hd, kvd = nkv * hd, KS = hd / 32;
+    const int64_t *qb = qkv + (size_t)b * (dim + 2 * kvd) + (size_t)g * grp * hd;
+    const size_t vbase = (size_t)seq_arr[b] * max_seq;
+    for (int n0 = 0; n0 < grp; n0 += 8) {
+        const int hq = n0 + gq;
+        const int U = ntile * KS;
+        int64_t raw[4][4];
+        auto load_k = [&](int u) {   // a0..a3 of unit u: rows gq, gq + 8 x columns tq*4, tq*4 + 16
+            const int t0 = tbase + 128 * (u / KS), ks = (u % KS) * 32;
+#pragma unroll
+            for (int f = 0; f < 4; f++) {
+                const int row = t0 + gq + ((f & 1) ? 8 : 0), d = ks + tq * 4 + (f >> 1) * 16;
+                raw[f][0] = raw[f][1] = raw[f][2] = raw[f][3] = 0;
+                if (row < T) {
+                    const size_t vec = (vbase + row) * nkv + g;
+                    kv.at4(vec * hd + d, vec, raw[f]);
+                }
+            }
+        };
+        load_k(0);
+        int acc[14][4];
+        for (int u = 0; u < U; u++) {
+            const int ks = (u % KS) * 32, t0 = tbase + 128 * (u / KS);
+            if (ks == 0) {
+#pragma unroll
+                for (int s = 0; s < 14; s++) acc[s][0] = acc[s][1] = acc[s][2] = acc[s][3] = 0;
+            }
+            uint32_t A[4][8], B[2][8];
+#pragma unroll
+            for (int f = 0; f < 4; f++) byte_planes4(raw[f], A[f]);
+            if (u + 1 < U) load_k(u + 1);
+#pragma unroll
+            for (int f = 0; f < 2; f++) {   // b0, b1: rows (d) tq*4, tq*4 + 16 x column (head) hq
+                int64_t e[4] = {0, 0, 0, 0};
+                if (hq < grp) {
+                    const longlong2 *p =
+                        reinterpret_cast<const longlong2 *>(qb + (size_t)hq * hd + ks + tq * 4 + f * 16);
+                    const longlong2 x = p[0], y = p[1];
+                    e[0] = x.x; e[1] = x.y; e[2] = y.x; e[3] = y.y;
+                }
+                byte_planes4(e, B[f]);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    if (i + j > 13) continue;
+                    if (i == 7) mma_s32<true, false>(acc[i + j], A[0][i], A[1][i], A[2][i], A[3][i], B[0][j], B[1][j]);
+                    else if (j == 7) mma_s32<false, true>(acc[i + j], A[0][i], A[1][i], A[2][i], A[3][i], B[0][j], B[1][j]);
+                    else mma_s32<false, false>(acc[i + j], A[0][i], A[1][i], A[2][i], A[3][i], B[0][j], B[1][j]);
+                }
+            if (ks + 32 < hd) continue;
+            // c0, c1: position t0 + gq, heads n0 + 2 tq + {0, 1}; c2, c3: position t0 + gq + 8
+            int64_t hmax[2] = {INT64_MIN, INT64_MIN};
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                uint64_t G0 = 0, G1 = 0, G2 = 0;   // diagonals 0-4, 5-9, 10-13 (|G| < 2^61)
+#pragma unroll
+                for (int s = 0; s < 5; s++) G0 += (uint64_t)(int64_t)acc[s][c] << (8 * s);
+#pragma unroll
+                for (int s = 5; s < 10; s++) G1 += (uint64_t)(int64_t)acc[s][c] << (8 * (s - 5));
+#pragma unroll
+                for (int s = 10; s < 14; s++) G2 += (uint64_t)(int64_t)acc[s][c] << (8 * (s - 10));
+                const u128 dot = (u128)(i128)(int64_t)G0 + ((u128)(i128)(int64_t)G1 << 40) +
+                                 ((u128)(i128)(int64_t)G2 << 80);
+                const int pos = t0 + gq + (c < 2 ? 0 : 8), head = n0 + 2 * tq + (c & 1);
+                if (pos < T && head < grp) {
+                    const int64_t v = d_mul((int64_t)(uint64_t)(dot >> 48), scale);
+                    sc[((size_t)b * nh + g * grp + head) * Tcap + pos] = v;
+                    hmax[c & 1] = max(hmax[c & 1], v);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 2; k++) {
+                int64_t v = hmax[k];
+                for (int m = 4; m <= 16; m <<= 1) v = max(v, (int64_t)__shfl_xor_sync(0xffffffffu, v, m));
+                const int head = n0 + 2 * tq + k;
+                if (gq == 0 && head < grp && v != INT64_MIN)
+                    atomicMax((long long *)&mx[(size_t)b * nh + g * grp + head], (long long)v);
+            }
+        }
+    }
+}
+
 // shared memory of k_attn_scores: q sums, q limbs, key tile of int2 (int64 units)
 __host__ __device__ constexpr size_t att_scores_smem(int grp, int hd) {
     return ((size_t)2 * grp + (3 * (size_t)grp * hd + 1) / 2 + (size_t)ATT_TILE * (hd + 1)) * 8;
@@ -422,7 +577,24 @@ k_attn_exp(int64_t *__restrict__ sc, const int64_t *__restrict__ mx, uint64_t *_
 }
 
 // phase 3: p_t = fp_div(e_t, S) (if S > 0) for the tile, then int64 partial
-// sums of fp_mul(p_t, v_t[d]) added atomically into out (wrapping, exact)
+// sums of fp_mul(p_t, v_t[d]) added atomically into out (wrapping, exact).
+//
+// Limb form of the per-term floor (SPT > 0): with 0 <= p < 2^49 (p is a
+// probability, at most 2^48) and R_t = (p_t v_t) mod 2^48 >= 0,
+//   sum_t fp_mul(p_t, v_t) = (sum_t p_t v_t - sum_t R_t) / 2^48   exactly,
+// since every p v - R is 2^48 floor(p v / 2^48). The exact sum of products is
+// taken in four 32 x 32 -> 64 partial sums, p = p0 + 2^25 p1 (p0 < 2^25,
+// p1 < 2^24), v = vl + 2^32 vh (vl unsigned, vh signed):
+//   A = sum p0 vl, B = sum p1 vl, C = sum p0 vh, D = sum p1 vh,
+//   sum p v = A + 2^25 B + 2^32 C + 2^57 D,
+// all int64-exact over one 64-position tile; R_t is the low 48 bits of the
+// 64-bit product. Thread slots: with grp*hd >= 256 a thread owns one d and
+// SPT heads (d = tid % hd, heads tid / hd + k * 256 / hd), sharing each v load
+// across them; with fewer slots, 256 / (grp*hd) position groups split the tile
+// and each adds its own partial sum. A tile holding a p outside [0, 2^49)
+// (never produced by fp_div of a softmax numerator) takes the direct
+// fp_mul loop (SPT == 0 is that loop for every tile).
+template <int SPT>
 __global__ void __launch_bounds__(256)
 k_attn_pv(int64_t *__restrict__ out, const int64_t *__restrict__ sc, const uint64_t *__restrict__ sm_,
           const KVView kv, const int *__restrict__ pos_arr, const int *__restrict__ seq_arr,
@@ -433,8 +605,9 @@ k_attn_pv(int64_t *__restrict__ out, const int64_t *__restrict__ sc, const uint6
     if (t0 >= T) return;
     const int nt = min(ATT_TILE, T - t0);
     const int grp = nh / nkv, dim = nh * hd;
-    int64_t *ps = smem;                // [grp][ATT_TILE]
-    int64_t *vt = ps + grp * ATT_TILE; // [ATT_TILE][hd]
+    int4 *ps = reinterpret_cast<int4 *>(smem);                 // [grp][ATT_TILE] {p0, p1, lo32(p), p >> 32}
+    int64_t *vt = smem + 2 * grp * ATT_TILE;                  // [ATT_TILE][hd]
+    int bad = 0;
     for (int e = threadIdx.x; e < grp * ATT_TILE; e += blockDim.x) {
         const int hh = e / ATT_TILE, tt = e % ATT_TILE;
         int64_t p = 0;
@@ -444,22 +617,75 @@ k_attn_pv(int64_t *__restrict__ out, const int64_t *__restrict__ sc, const uint6
             const int64_t S = (int64_t)sm_[(size_t)b * nh + h];
             if (S > 0) p = d_div(p, S);
         }
-        ps[e] = p;
+        bad |= (uint64_t)p >= (1ull << 49);
+        ps[e] = make_int4((int)(p & 0x1FFFFFF), (int)((uint64_t)p >> 25), (int)(uint32_t)p, (int)(p >> 32));
     }
     const size_t vb0 = ((size_t)seq_arr[b] * max_seq + t0) * nkv + g;
     for (int e = threadIdx.x; e < nt * hd; e += blockDim.x) {
         const size_t vec = vb0 + (size_t)(e / hd) * nkv;
         vt[e] = kv.at(vec * hd + e % hd, vec);
     }
-    __syncthreads();
-    for (int e = threadIdx.x; e < grp * hd; e += blockDim.x) {
-        const int hh = e / hd, dd = e % hd;
-        const int64_t *p = ps + hh * ATT_TILE;
-        uint64_t acc = 0;
-        for (int tt = 0; tt < nt; tt++) acc += (uint64_t)d_mul(p[tt], vt[tt * hd + dd]);
-        atomicAdd((unsigned long long *)&out[(size_t)b * dim + (size_t)(g * grp + hh) * hd + dd],
-                  (unsigned long long)acc);
+    if (SPT == 0 || __syncthreads_or(bad)) {
+        __syncthreads();
+        for (int e = threadIdx.x; e < grp * hd; e += blockDim.x) {
+            const int hh = e / hd, dd = e % hd;
+            const int4 *pp = ps + hh * ATT_TILE;
+            uint64_t acc = 0;
+            for (int tt = 0; tt < nt; tt++) {
+                const int64_t p = (int64_t)(uint32_t)pp[tt].z | ((int64_t)pp[tt].w << 32);
+                acc += (uint64_t)d_mul(p, vt[tt * hd + dd]);
+            }
+            atomicAdd((unsigned long long *)&out[(size_t)b * dim + (size_t)(g * grp + hh) * hd + dd],
+                      (unsigned long long)acc);
+        }
+        return;
     }
+    if constexpr (SPT > 0) {
+        const int nslots = grp * hd, tid = threadIdx.x;
+        const int pg_n = nslots >= 256 ? 1 : 256 / nslots;            // position groups
+        const int slot = nslots >= 256 ? tid : tid % nslots, pg = nslots >= 256 ? 0 : tid / nslots;
+        const int dd = slot % hd, h0 = slot / hd, hstep = 256 / hd;
+        uint64_t A[SPT], B[SPT], Rs[SPT];
+        int64_t C[SPT], D[SPT];
+#pragma unroll
+        for (int k = 0; k < SPT; k++) { A[k] = B[k] = Rs[k] = 0; C[k] = D[k] = 0; }
+        const int2 *vcol = reinterpret_cast<const int2 *>(vt) + dd;
+#pragma unroll 2
+        for (int tt = pg; tt < nt; tt += pg_n) {
+            const int2 v = vcol[tt * hd];
+#pragma unroll
+            for (int k = 0; k < SPT; k++) {
+                const int4 p = ps[(h0 + k * hstep) * ATT_TILE + tt];
+                asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(A[k]) : "r"(p.x), "r"(v.x));
+                asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(B[k]) : "r"(p.y), "r"(v.x));
+                asm("mad.wide.s32 %0, %1, %2, %0;" : "+l"(C[k]) : "r"(p.x), "r"(v.y));
+                asm("mad.wide.s32 %0, %1, %2, %0;" : "+l"(D[k]) : "r"(p.y), "r"(v.y));
+                const uint64_t lo = ((uint64_t)(uint32_t)p.w << 32 | (uint32_t)p.z) *
+                                    ((uint64_t)(uint32_t)v.y << 32 | (uint32_t)v.x);
+                Rs[k] += lo & 0xFFFFFFFFFFFFull;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < SPT; k++) {
+            const u128 sum = (u128)A[k] + ((u128)B[k] << 25) + ((u128)(i128)C[k] << 32) +
+                             ((u128)(i128)D[k] << 57) - (u128)Rs[k];
+            const uint64_t part = (uint64_t)(sum >> 48);
+            atomicAdd((unsigned long long *)&out[(size_t)b * dim + (size_t)(g * grp + h0 + k * hstep) * hd + dd],
+                      (unsigned long long)part);
+        }
+    }
+}
+
+// the k_attn_pv instance for (grp, hd): SPT = grp*hd / 256 slots per thread
+// when hd divides 256 and the slots fill the CTA evenly, else 0 (direct loop)
+__host__ __device__ constexpr int att_pv_spt(int grp, int hd) {
+    return (hd <= 0 || 256 % hd) ? 0
+           : (grp * hd >= 256) ? ((grp * hd) % 256 == 0 && grp * hd / 256 <= 8 && ((grp * hd / 256) & (grp * hd / 256 - 1)) == 0
+                                      ? grp * hd / 256 : 0)
+           : (256 % (grp * hd) == 0 ? 1 : 0);
+}
+__host__ __device__ constexpr size_t att_pv_smem(int grp, int hd) {
+    return ((size_t)2 * grp * ATT_TILE + (size_t)ATT_TILE * hd) * 8;
 }
 
 // SwiGLU: out[i] = fp_mul(fp_silu(gate[i]), up[i]) with gu = [gate | up] (llama_int.c:1549-1552)

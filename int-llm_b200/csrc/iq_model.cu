@@ -96,6 +96,8 @@ struct iq_model {
     size_t attn_smem = 0;
     size_t gqa_smem = 0;  // k_attention_gqa shared memory (0 = use k_attention)
     int hpc = 1;          // query heads per attention CTA
+    int att_scores_tc = 0;   // scores on the int8 tensor cores (k_attn_scores_tc)
+    int att_pv_spt = 0;   // k_attn_pv instance (att_pv_spt())
     int att_phased = 1;   // phased attention (k_attn_*), else one CTA per (row, head)
     int64_t *asc = nullptr, *amx = nullptr;  // phased-attention scratch: scores, maxima
     uint64_t *asum = nullptr;                // and sums
@@ -129,6 +131,16 @@ struct iq_model {
     int dec_grid = 0;
     size_t dec_smem = 0;
 };
+
+static const void *att_pv_kernel(int spt) {
+    switch (spt) {
+        case 1: return (const void *)k_attn_pv<1>;
+        case 2: return (const void *)k_attn_pv<2>;
+        case 4: return (const void *)k_attn_pv<4>;
+        case 8: return (const void *)k_attn_pv<8>;
+        default: return (const void *)k_attn_pv<0>;
+    }
+}
 
 static int dalloc(void **p, size_t bytes) {
     cudaError_t e = cudaMalloc(p, bytes ? bytes : 8);
@@ -378,16 +390,30 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
             k_attn_init<<<(int)std::min<int64_t>((n + 255) / 256, 4096), 256, 0, s>>>(att_out, m->amx, m->asum, R,
                                                                                    S.nh_l, hd);
             IQ_CHECK_LAUNCH();
-            k_attn_scores<<<dim3(grid_t, S.nkv_l, R), 256, m->att_s1, s>>>(m->asc, m->amx, m->qkv, kview, pos,
-                                                                            seq, S.nh_l, S.nkv_l, hd, c.max_seq_len,
-                                                                            c.max_seq_len, m->att_scale);
+            if (m->att_scores_tc)
+                k_attn_scores_tc<<<dim3((c.max_seq_len + ATT_TC_POS - 1) / ATT_TC_POS, S.nkv_l, R), 256, 0, s>>>(
+                    m->asc, m->amx, m->qkv, kview, pos, seq, S.nh_l, S.nkv_l, hd, c.max_seq_len, c.max_seq_len,
+                    m->att_scale);
+            else
+                k_attn_scores<<<dim3(grid_t, S.nkv_l, R), 256, m->att_s1, s>>>(m->asc, m->amx, m->qkv, kview, pos,
+                                                                                seq, S.nh_l, S.nkv_l, hd,
+                                                                                c.max_seq_len, c.max_seq_len,
+                                                                                m->att_scale);
             IQ_CHECK_LAUNCH();
             k_attn_exp<<<dim3((c.max_seq_len + 255) / 256, S.nh_l, R), 256, 0, s>>>(m->asc, m->amx, m->asum, pos,
                                                                                    S.nh_l, c.max_seq_len);
             IQ_CHECK_LAUNCH();
-            k_attn_pv<<<dim3(grid_t, S.nkv_l, R), 256, m->att_s3, s>>>(att_out, m->asc, m->asum, vview, pos, seq,
-                                                                        S.nh_l, S.nkv_l, hd, c.max_seq_len,
-                                                                        c.max_seq_len);
+            const dim3 gpv(grid_t, S.nkv_l, R);
+#define IQ_PV(SPT) k_attn_pv<SPT><<<gpv, 256, m->att_s3, s>>>(att_out, m->asc, m->asum, vview, pos, seq, S.nh_l, \
+                                                          S.nkv_l, hd, c.max_seq_len, c.max_seq_len)
+            switch (m->att_pv_spt) {
+                case 1: IQ_PV(1); break;
+                case 2: IQ_PV(2); break;
+                case 4: IQ_PV(4); break;
+                case 8: IQ_PV(8); break;
+                default: IQ_PV(0);
+            }
+#undef IQ_PV
         } else if (m->gqa_smem && !att_short)
             k_attention_gqa<<<dim3(S.nh_l / m->hpc, R), 256, m->gqa_smem, s>>>(
                 att_out, m->qkv, m->kc[l], m->vc[l], pos, seq, S.nh_l, S.nkv_l, hd, c.max_seq_len, c.max_seq_len,
@@ -825,7 +851,9 @@ IQ_API int iq_model_create_tp(const iq_config *cfg, int max_batch, int device, i
         static int att_env = getenv("IQ_ATT") ? atoi(getenv("IQ_ATT")) : 1;
         const size_t grp = (size_t)sh.nh_l / sh.nkv_l, hd = c.head_dim;
         m->att_s1 = att_scores_smem((int)grp, (int)hd);
-        m->att_s3 = (grp * ATT_TILE + (size_t)ATT_TILE * hd) * 8;
+        m->att_s3 = att_pv_smem((int)grp, (int)hd);
+        m->att_pv_spt = getenv("IQ_PV_DIRECT") ? 0 : att_pv_spt((int)grp, (int)hd);
+        m->att_scores_tc = !getenv("IQ_SCORES_DIRECT") && hd % 32 == 0 && hd <= 256;
         // the phased scores use 32-bit limb dots, exact for head_dim <= 256
         m->att_phased = att_env == 1 && hd <= 256 && m->att_s1 <= 200 * 1024 && m->att_s3 <= 200 * 1024;
         if (m->att_phased) {
@@ -834,7 +862,8 @@ IQ_API int iq_model_create_tp(const iq_config *cfg, int max_batch, int device, i
                 (rc = dalloc((void **)&m->asum, n * 8))) { iq_model_destroy(m); return rc; }
             e = cudaFuncSetAttribute(k_attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->att_s1);
             if (e == cudaSuccess)
-                e = cudaFuncSetAttribute(k_attn_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->att_s3);
+                e = cudaFuncSetAttribute(att_pv_kernel(m->att_pv_spt), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)m->att_s3);
             if (e != cudaSuccess) { iq_model_destroy(m); return cuda_fail(e); }
         }
     }

@@ -181,6 +181,54 @@ def test_fp_ports_random_vs_oracle(fn):
     assert (host(do) == want).all()
 
 
+def test_fp_div_fast_path_edges_vs_oracle():
+    """fp_div's estimate-and-correct path at its edges: quotients near 2^50 (the
+    switch to the long division), divisors near 2^61, exact quotients (remainder
+    0), remainders of |b| - 1, softmax-like numerators over sums, and the
+    extreme magnitudes (INT64_MIN, +-1)."""
+    import torch
+    rng = np.random.default_rng(77)
+    M = (1 << 63) - 1
+    xs, ys = [], []
+    for _ in range(3000):   # quotient near 2^50 +- a little
+        b = int(rng.integers(1, 1 << 40))
+        q = (1 << 50) + int(rng.integers(-4, 5))
+        a = (q * b) >> 48
+        for da in (-1, 0, 1):
+            if 0 <= a + da <= M:
+                xs.append(a + da); ys.append(b)
+    for _ in range(3000):   # divisors near 2^61
+        b = (1 << 61) + int(rng.integers(-8, 9))
+        a = int(rng.integers(0, M))
+        xs.append(a); ys.append(b)
+    for _ in range(3000):   # exact quotients and remainders of b - 1
+        b = int(rng.integers(1, 1 << 55))
+        q = int(rng.integers(0, 1 << 49))
+        n = q * b            # = a << 48 exactly when 2^48 divides n
+        a = n >> 48
+        xs += [a, a + 1, max(a - 1, 0)]; ys += [b, b, b]
+    for _ in range(3000):   # softmax numerators e <= 2^48 over sums up to ~2^60
+        S = int(rng.integers(1 << 48, 1 << 60))
+        e = int(rng.integers(0, (1 << 48) + 1))
+        xs.append(e); ys.append(S)
+    ext = [-(1 << 63), M, 1, -1, 0, 1 << 48, -(1 << 48), 3, (1 << 62) + 7]
+    for a in ext:
+        for b in ext:
+            if b != 0:
+                xs.append(a); ys.append(b)
+    x = np.array(xs, dtype=np.int64)
+    y = np.array(ys, dtype=np.int64)
+    sg = rng.integers(0, 4, x.size)
+    x = np.where(sg & 1, -x, x).astype(np.int64)   # INT64_MIN stays INT64_MIN
+    y = np.where(sg & 2, -y, y).astype(np.int64)
+    want = orc.fp_vec(1, x, y)
+    do = torch.empty(x.size, dtype=torch.int64, device="cuda")
+    iq.fp_dev(1, dev(x), dev(y), do, x.size)
+    got = host(do)
+    bad = np.nonzero(got != want)[0]
+    assert bad.size == 0, [(int(x[i]), int(y[i]), int(got[i]), int(want[i])) for i in bad[:5]]
+
+
 def test_rmsnorm_softmax_vs_oracle():
     import torch
     rng = np.random.default_rng(1)
