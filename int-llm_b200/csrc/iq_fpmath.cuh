@@ -165,10 +165,17 @@ __device__ __forceinline__ int64_t d_inv_sqrt(int64_t x) {
 
 // ---- exp / log --------------------------------------------------------
 
+// fp_mul(r, r) (fp_math.h:491-506) from the unsigned square of |r|: r r = |r|^2,
+// so the low 64 bits of |r|^2 >> 48 are the same value.
+__device__ __forceinline__ int64_t d_sqr(int64_t r) {
+    const uint64_t m = r < 0 ? (uint64_t)0 - (uint64_t)r : (uint64_t)r;
+    return (int64_t)(((m * m) >> 48) | (__umul64hi(m, m) << 16));
+}
+
 // fp_exp_dyadic (fp_math.h:714-720)
 __device__ __forceinline__ int64_t d_exp_dyadic(int64_t x, int k) {
     int64_t r = IQ_ONE + (x >> k);
-    for (int i = 0; i < k; i++) r = d_mul(r, r);
+    for (int i = 0; i < k; i++) r = d_sqr(r);
     return r;
 }
 

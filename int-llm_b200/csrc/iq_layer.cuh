@@ -458,7 +458,10 @@ __device__ __forceinline__ void byte_planes4(const int64_t (&e)[4], uint32_t (&o
 // tiles = ATT_TC_POS positions per CTA; no shared memory.
 #define ATT_TC_TPW 2
 #define ATT_TC_POS (128 * ATT_TC_TPW)
-__global__ void __launch_bounds__(256)
+#ifndef IQ_SC_MINB
+#define IQ_SC_MINB 1
+#endif
+__global__ void __launch_bounds__(256, IQ_SC_MINB)
 k_attn_scores_tc(int64_t *__restrict__ sc, int64_t *__restrict__ mx, const int64_t *__restrict__ qkv,
                  const KVView kv, const int *__restrict__ pos_arr, const int *__restrict__ seq_arr,
                  int nh, int nkv, int hd, int max_seq, int Tcap, int64_t scale) {
@@ -674,6 +677,196 @@ k_attn_pv(int64_t *__restrict__ out, const int64_t *__restrict__ sc, const uint6
                       (unsigned long long)part);
         }
     }
+}
+
+// Phase 3 with the products on the int8 tensor cores. Same result as
+// k_attn_pv: per (row, head, d), sum_t fp_mul(p_t, v_t[d]) =
+// (sum_t p_t v_t - sum_t R_t) / 2^48 with R_t = (p_t v_t) mod 2^48, over any set
+// of positions. The exact sum of products is taken in byte planes (p: 7
+// unsigned bytes, as 0 <= p < 2^49; v: 7 unsigned and a signed top byte) with
+// one m16n8k32 MMA per plane pair (A = values, 16 d x 32 positions; B =
+// probabilities, 32 positions x 8 heads), the pairs of each diagonal summed in
+// s32; every pair has i + j <= 13, all needed mod 2^112. R_t is taken on the
+// CUDA cores from 32-bit pieces: w = lo(p) lo(v) (64-bit) and the low 16 bits
+// of hi(w) + lo(p) hi(v) + hi(p) lo(v) (the bits 32..47). Both parts of each
+// (head, d) meet in shared memory as four int64 partial sums weighted 2^0,
+// 2^32, 2^64, 2^96 (each far from overflow), then the exact shift by 48.
+// A CTA takes PV_CH positions of one (row, kv group) in 64-position sub-tiles;
+// the host launches it when (hd / 16) x ceil(grp / 8) output blocks divide the
+// 8 warps and att_pv_spt(grp, hd) > 0.
+#define PV_CH 256
+#ifndef IQ_PV_XMMA
+#define IQ_PV_XMMA 0
+#endif
+#ifndef IQ_PV_XR
+#define IQ_PV_XR 0
+#endif
+#ifndef IQ_PV_MINB
+#define IQ_PV_MINB 2
+#endif
+template <int HB>
+__global__ void __launch_bounds__(256, IQ_PV_MINB)
+k_attn_pv_tc(int64_t *__restrict__ out, const int64_t *__restrict__ sc, const uint64_t *__restrict__ sm_,
+             const KVView kv, const int *__restrict__ pos_arr, const int *__restrict__ seq_arr,
+             int nh, int nkv, int hd, int max_seq, int Tcap) {
+    extern __shared__ __align__(16) int64_t smem[];
+    const int g = blockIdx.y, b = blockIdx.z, T = pos_arr[b] + 1, c0 = blockIdx.x * PV_CH;
+    if (c0 >= T) return;
+    const int nt = min(PV_CH, T - c0);
+    const int grp = nh / nkv, dim = nh * hd, nslots = grp * hd, vld = hd + 2, tid = threadIdx.x;
+    int64_t *ps = smem;                                        // [grp][PV_CH] probabilities
+    int64_t *vt = ps + (size_t)grp * PV_CH;                    // [64][hd + 1] values of one sub-tile
+    long long *gacc = reinterpret_cast<long long *>(vt + 64 * vld);   // [4][nslots]
+    for (int e = tid; e < 4 * nslots; e += 256) gacc[e] = 0;
+    int bad = 0;
+    for (int e = tid; e < grp * PV_CH; e += 256) {
+        const int hh = e / PV_CH, tt = e % PV_CH;
+        int64_t p = 0;
+        if (tt < nt) {
+            const int h = g * grp + hh;
+            p = sc[((size_t)b * nh + h) * Tcap + c0 + tt];
+            const int64_t S = (int64_t)sm_[(size_t)b * nh + h];
+            if (S > 0) p = d_div(p, S);
+        }
+        bad |= (uint64_t)p >= (1ull << 49);
+        ps[e] = p;
+    }
+    bad = __syncthreads_or(bad);
+    const size_t vb0 = ((size_t)seq_arr[b] * max_seq + c0) * nkv + g;   // vector of position c0, head g
+    auto stage_v = [&](int st0, int snt) {
+        __syncthreads();   // the previous sub-tile is consumed
+        for (int e = tid * 4; e < 64 * hd; e += 1024) {
+            const int t = e / hd, d = e % hd;
+            int64_t v4[4] = {0, 0, 0, 0};
+            if (t < snt) {
+                const size_t vec = vb0 + (size_t)(st0 + t) * nkv;
+                kv.at4(vec * hd + d, vec, v4);
+            }
+            longlong2 *dst = reinterpret_cast<longlong2 *>(vt + t * vld + d);
+            dst[0] = make_longlong2(v4[0], v4[1]);
+            dst[1] = make_longlong2(v4[2], v4[3]);
+        }
+        __syncthreads();
+    };
+    if (bad) {   // a probability outside [0, 2^49): the direct per-term loop for this chunk
+        for (int st0 = 0; st0 < nt; st0 += 64) {
+            const int snt = min(64, nt - st0);
+            stage_v(st0, snt);
+            for (int e = tid; e < nslots; e += 256) {
+                const int hh = e / hd, dd = e % hd;
+                uint64_t acc = 0;
+                for (int tt = 0; tt < snt; tt++) acc += (uint64_t)d_mul(ps[hh * PV_CH + st0 + tt], vt[tt * vld + dd]);
+                atomicAdd((unsigned long long *)&out[(size_t)b * dim + (size_t)g * nslots + e], (unsigned long long)acc);
+            }
+        }
+        return;
+    }
+    const int warp = tid >> 5, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
+    const int ndt = hd / 16, OB = ndt * ((grp + 7) / 8), WB = 8 / OB;
+    const int ob = warp % OB, wsub = warp / OB, d0 = (ob % ndt) * 16, n0 = (ob / ndt) * 8;
+    // R slots: HB heads x 2 adjacent d per thread, position pairs split over pg_n groups
+    const int nthr = nslots / (2 * HB), pg_n = 256 / nthr, r = tid % nthr, pg = tid / nthr;
+    const int dd = (r % (hd / 2)) * 2, h0 = (r / (hd / 2)) * HB;
+    int acc[14][4];
+#pragma unroll
+    for (int s = 0; s < 14; s++) acc[s][0] = acc[s][1] = acc[s][2] = acc[s][3] = 0;
+    uint64_t Rs[HB][2];
+#pragma unroll
+    for (int k = 0; k < HB; k++) Rs[k][0] = Rs[k][1] = 0;
+    const int hq = n0 + gq;
+    for (int st0 = 0; st0 < nt; st0 += 64) {
+        const int snt = min(64, nt - st0);
+        stage_v(st0, snt);
+        for (int ks = wsub; ks < 2 && ks * 32 < snt && !IQ_PV_XMMA; ks += WB) {
+            uint32_t A[4][8], B[2][8];
+#pragma unroll
+            for (int f = 0; f < 4; f++) {   // a0..a3: rows (d) d0 + gq (+8) x columns (t) tq*4 (+16)
+                const int d = d0 + gq + ((f & 1) ? 8 : 0), t = ks * 32 + tq * 4 + (f >> 1) * 16;
+                const int64_t e[4] = {vt[t * vld + d], vt[(t + 1) * vld + d], vt[(t + 2) * vld + d],
+                                      vt[(t + 3) * vld + d]};
+                byte_planes4(e, A[f]);
+            }
+#pragma unroll
+            for (int f = 0; f < 2; f++) {   // b0, b1: rows (t) tq*4 (+16) x column (head) hq
+                int64_t e[4] = {0, 0, 0, 0};
+                if (hq < grp) {
+                    const longlong2 *p = reinterpret_cast<const longlong2 *>(ps + (size_t)hq * PV_CH + st0 + ks * 32 +
+                                                                             tq * 4 + f * 16);
+                    const longlong2 x = p[0], y = p[1];
+                    e[0] = x.x; e[1] = x.y; e[2] = y.x; e[3] = y.y;
+                }
+                byte_planes4(e, B[f]);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int j = 0; j < 7; j++) {
+                    if (i == 7) mma_s32<true, false>(acc[i + j], A[0][i], A[1][i], A[2][i], A[3][i], B[0][j], B[1][j]);
+                    else mma_s32<false, false>(acc[i + j], A[0][i], A[1][i], A[2][i], A[3][i], B[0][j], B[1][j]);
+                }
+        }
+        // R_t for this thread's (head, d) slots, two positions per step
+        const int64_t *prow = ps + (size_t)h0 * PV_CH + st0;
+#pragma unroll 2
+        for (int tt = 2 * pg; tt < snt && !IQ_PV_XR; tt += 2 * pg_n) {
+            const longlong2 va = *reinterpret_cast<const longlong2 *>(vt + tt * vld + dd);
+            const longlong2 vb = *reinterpret_cast<const longlong2 *>(vt + (tt + 1) * vld + dd);
+            const uint64_t v[2][2] = {{(uint64_t)va.x, (uint64_t)va.y}, {(uint64_t)vb.x, (uint64_t)vb.y}};
+#pragma unroll
+            for (int k = 0; k < HB; k++) {
+                const longlong2 pp = *reinterpret_cast<const longlong2 *>(prow + k * PV_CH + tt);
+                const uint64_t p2[2] = {(uint64_t)pp.x, (uint64_t)pp.y};
+#pragma unroll
+                for (int u = 0; u < 2; u++) {
+                    const uint32_t plo = (uint32_t)p2[u], phi = (uint32_t)(p2[u] >> 32);
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+                        const uint32_t vlo = (uint32_t)v[u][e], vhi = (uint32_t)(v[u][e] >> 32);
+                        const uint64_t w = (uint64_t)plo * vlo;
+                        const uint32_t hi = ((uint32_t)(w >> 32) + plo * vhi + phi * vlo) & 0xFFFFu;
+                        Rs[k][e] += ((uint64_t)hi << 32) | (uint32_t)w;
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < HB; k++)
+#pragma unroll
+        for (int e = 0; e < 2; e++)
+            atomicAdd((unsigned long long *)&gacc[(h0 + k) * hd + dd + e], (unsigned long long)(0 - Rs[k][e]));
+    // c0, c1: d = d0 + gq, heads n0 + 2 tq + {0, 1}; c2, c3: d + 8
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        const int head = n0 + 2 * tq + (c & 1), d = d0 + gq + (c < 2 ? 0 : 8);
+        if (head >= grp) continue;
+        uint64_t G[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int s = 0; s < 14; s++) G[s >> 2] += (uint64_t)(int64_t)acc[s][c] << (8 * (s & 3));
+        const int sl = head * hd + d;
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+            if (G[q]) atomicAdd((unsigned long long *)&gacc[q * nslots + sl], (unsigned long long)G[q]);
+    }
+    __syncthreads();
+    for (int e = tid; e < nslots; e += 256) {
+        const u128 X = (u128)(i128)gacc[e] + ((u128)(i128)gacc[nslots + e] << 32) +
+                       ((u128)(i128)gacc[2 * nslots + e] << 64) + ((u128)(i128)gacc[3 * nslots + e] << 96);
+        atomicAdd((unsigned long long *)&out[(size_t)b * dim + (size_t)g * nslots + e], (unsigned long long)(X >> 48));
+    }
+}
+
+// shared memory of k_attn_pv_tc, and whether (grp, hd) can take it
+__host__ __device__ constexpr size_t att_pv_tc_smem(int grp, int hd) {
+    return ((size_t)grp * PV_CH + (size_t)64 * (hd + 2) + (size_t)4 * grp * hd) * 8;
+}
+// heads per thread of the R part (0: the kernel does not apply): the MMA output
+// blocks (hd / 16) x ceil(grp / 8) divide the 8 warps and the R threads
+// grp * hd / (2 HB) divide 256
+__host__ __device__ constexpr int att_pv_tc_hb(int grp, int hd) {
+    return (hd % 32 != 0 || hd / 16 * ((grp + 7) / 8) > 8 || 8 % (hd / 16 * ((grp + 7) / 8)) != 0) ? 0
+           : (grp >= 2 && grp % 2 == 0 && 256 % (grp * hd / 4) == 0) ? 2
+           : (256 % (grp * hd / 2) == 0 && grp * hd / 2 <= 256) ? 1 : 0;
 }
 
 // the k_attn_pv instance for (grp, hd): SPT = grp*hd / 256 slots per thread

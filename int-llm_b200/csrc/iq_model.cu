@@ -96,6 +96,8 @@ struct iq_model {
     size_t attn_smem = 0;
     size_t gqa_smem = 0;  // k_attention_gqa shared memory (0 = use k_attention)
     int hpc = 1;          // query heads per attention CTA
+    int att_pv_tc = 0;       // phase 3 on the tensor cores (k_attn_pv_tc<att_pv_tc>), 0: off
+    size_t att_s3tc = 0;
     int att_scores_tc = 0;   // scores on the int8 tensor cores (k_attn_scores_tc)
     int att_pv_spt = 0;   // k_attn_pv instance (att_pv_spt())
     int att_phased = 1;   // phased attention (k_attn_*), else one CTA per (row, head)
@@ -140,6 +142,10 @@ static const void *att_pv_kernel(int spt) {
         case 8: return (const void *)k_attn_pv<8>;
         default: return (const void *)k_attn_pv<0>;
     }
+}
+
+static const void *att_pv_tc_kernel(int hb) {
+    return hb == 2 ? (const void *)k_attn_pv_tc<2> : (const void *)k_attn_pv_tc<1>;
 }
 
 static int dalloc(void **p, size_t bytes) {
@@ -406,7 +412,13 @@ static int enqueue_rows(iq_model *m, int R, const int *tok, const int *pos, cons
             const dim3 gpv(grid_t, S.nkv_l, R);
 #define IQ_PV(SPT) k_attn_pv<SPT><<<gpv, 256, m->att_s3, s>>>(att_out, m->asc, m->asum, vview, pos, seq, S.nh_l, \
                                                           S.nkv_l, hd, c.max_seq_len, c.max_seq_len)
-            switch (m->att_pv_spt) {
+            const dim3 gtc((c.max_seq_len + PV_CH - 1) / PV_CH, S.nkv_l, R);
+#define IQ_PVTC(SPT) k_attn_pv_tc<SPT><<<gtc, 256, m->att_s3tc, s>>>(att_out, m->asc, m->asum, vview, pos, seq, \
+                                                                   S.nh_l, S.nkv_l, hd, c.max_seq_len, c.max_seq_len)
+            if (m->att_pv_tc == 2) IQ_PVTC(2);
+            else if (m->att_pv_tc == 1) IQ_PVTC(1);
+#undef IQ_PVTC
+            else switch (m->att_pv_spt) {
                 case 1: IQ_PV(1); break;
                 case 2: IQ_PV(2); break;
                 case 4: IQ_PV(4); break;
@@ -854,6 +866,8 @@ IQ_API int iq_model_create_tp(const iq_config *cfg, int max_batch, int device, i
         m->att_s3 = att_pv_smem((int)grp, (int)hd);
         m->att_pv_spt = getenv("IQ_PV_DIRECT") ? 0 : att_pv_spt((int)grp, (int)hd);
         m->att_scores_tc = !getenv("IQ_SCORES_DIRECT") && hd % 32 == 0 && hd <= 256;
+        m->att_s3tc = att_pv_tc_smem((int)grp, (int)hd);
+        m->att_pv_tc = getenv("IQ_PV_NOTC") || m->att_s3tc > 200 * 1024 ? 0 : att_pv_tc_hb((int)grp, (int)hd);
         // the phased scores use 32-bit limb dots, exact for head_dim <= 256
         m->att_phased = att_env == 1 && hd <= 256 && m->att_s1 <= 200 * 1024 && m->att_s3 <= 200 * 1024;
         if (m->att_phased) {
@@ -864,6 +878,9 @@ IQ_API int iq_model_create_tp(const iq_config *cfg, int max_batch, int device, i
             if (e == cudaSuccess)
                 e = cudaFuncSetAttribute(att_pv_kernel(m->att_pv_spt), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)m->att_s3);
+            if (e == cudaSuccess && m->att_pv_tc)
+                e = cudaFuncSetAttribute(att_pv_tc_kernel(m->att_pv_tc), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)m->att_s3tc);
             if (e != cudaSuccess) { iq_model_destroy(m); return cuda_fail(e); }
         }
     }
