@@ -770,9 +770,9 @@ k_attn_pv_tc(int64_t *__restrict__ out, const int64_t *__restrict__ sc, const ui
     int acc[14][4];
 #pragma unroll
     for (int s = 0; s < 14; s++) acc[s][0] = acc[s][1] = acc[s][2] = acc[s][3] = 0;
-    uint64_t Rs[HB][2];
+    uint32_t Rl[HB][2], Rh[HB][2];   // sum_t R_t of each slot as (low, high) 32-bit words
 #pragma unroll
-    for (int k = 0; k < HB; k++) Rs[k][0] = Rs[k][1] = 0;
+    for (int k = 0; k < HB; k++) Rl[k][0] = Rl[k][1] = Rh[k][0] = Rh[k][1] = 0;
     const int hq = n0 + gq;
     for (int st0 = 0; st0 < nt; st0 += 64) {
         const int snt = min(64, nt - st0);
@@ -821,10 +821,17 @@ k_attn_pv_tc(int64_t *__restrict__ out, const int64_t *__restrict__ sc, const ui
                     const uint32_t plo = (uint32_t)p2[u], phi = (uint32_t)(p2[u] >> 32);
 #pragma unroll
                     for (int e = 0; e < 2; e++) {
+                        // R = lo(p) lo(v) mod 2^32 + 2^32 ((hi(lo(p) lo(v)) + lo(p) hi(v) + hi(p) lo(v)) mod 2^16)
                         const uint32_t vlo = (uint32_t)v[u][e], vhi = (uint32_t)(v[u][e] >> 32);
-                        const uint64_t w = (uint64_t)plo * vlo;
-                        const uint32_t hi = ((uint32_t)(w >> 32) + plo * vhi + phi * vlo) & 0xFFFFu;
-                        Rs[k][e] += ((uint64_t)hi << 32) | (uint32_t)w;
+                        asm("{\n\t.reg .u32 wh, t;\n\t"
+                            "mul.hi.u32 wh, %2, %3;\n\t"
+                            "mad.lo.u32 t, %2, %4, wh;\n\t"
+                            "mad.lo.u32 t, %5, %3, t;\n\t"
+                            "and.b32 t, t, 65535;\n\t"
+                            "mad.lo.cc.u32 %0, %2, %3, %0;\n\t"
+                            "addc.u32 %1, %1, t;\n\t}"
+                            : "+r"(Rl[k][e]), "+r"(Rh[k][e])
+                            : "r"(plo), "r"(vlo), "r"(vhi), "r"(phi));
                     }
                 }
             }
@@ -834,7 +841,8 @@ k_attn_pv_tc(int64_t *__restrict__ out, const int64_t *__restrict__ sc, const ui
     for (int k = 0; k < HB; k++)
 #pragma unroll
         for (int e = 0; e < 2; e++)
-            atomicAdd((unsigned long long *)&gacc[(h0 + k) * hd + dd + e], (unsigned long long)(0 - Rs[k][e]));
+            atomicAdd((unsigned long long *)&gacc[(h0 + k) * hd + dd + e],
+                      (unsigned long long)(0 - (((uint64_t)Rh[k][e] << 32) | Rl[k][e])));
     // c0, c1: d = d0 + gq, heads n0 + 2 tq + {0, 1}; c2, c3: d + 8
 #pragma unroll
     for (int c = 0; c < 4; c++) {
