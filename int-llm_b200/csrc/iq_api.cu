@@ -707,15 +707,22 @@ static int stream_bytes(cudaStream_t s, size_t bytes, uint8_t **out) {
     return IQ_OK;
 }
 
-// Split-K factor for a grid of `tiles` output tiles: enough CTAs for ~2 per SM.
+// Split-K factor: the ks in 1..16 (each split keeping >= IQ_GEMM_MINKB K blocks,
+// default 8: the per-plane epilogue fold is a fixed cost per CTA) that
+// minimises waves x K blocks per split, i.e. the time of the longest SM with
+// one CTA per SM; ties go to the smaller ks (less partial traffic).
 static int gemm_ksplit(const PackedTC &P, int R) {
+    static const int minkb = getenv("IQ_GEMM_MINKB") ? std::max(1, atoi(getenv("IQ_GEMM_MINKB"))) : 8;
     const int Rpad = (R + TC_BR - 1) / TC_BR * TC_BR;
-    const int tiles = (P.Mpad / TC_BM) * (Rpad / TC_BR), KBall = P.Kpad / TC_BK;
-    if (tiles >= dev_info().sms) return 1;  // the grid already fills the GPU
-    int ks = (dev_info().sms + tiles - 1) / tiles;
-    // each split keeps >= 8 K blocks: the per-plane epilogue fold is a fixed cost
-    // per CTA, so thin splits would make it, not the MMAs, the bottleneck
-    return std::max(1, std::min(ks, std::min(KBall / 8, 16)));
+    const int tiles = (P.Mpad / TC_BM) * (Rpad / TC_BR), KBall = P.Kpad / TC_BK, sms = dev_info().sms;
+    if (tiles >= 2 * sms) return 1;   // two or more waves: the tile count already balances
+    int best = 1;
+    long best_cost = (long)((tiles + sms - 1) / sms) * KBall;
+    for (int ks = 2; ks <= 16 && KBall / ks >= minkb; ks++) {
+        const long cost = (long)((tiles * ks + sms - 1) / sms) * ((KBall + ks - 1) / ks);
+        if (cost * 20 < best_cost * 19) { best = ks; best_cost = cost; }   // > 5% better
+    }
+    return best;
 }
 // bytes of split-K partial scratch launch_gemm_tc needs for (P, R)
 size_t gemm_tc_part_bytes(const PackedTC &P, int R) {

@@ -271,7 +271,7 @@ static int model_alloc(iq_model *m) {
         size_t kpad = (kmax + TC_BK - 1) / TC_BK * TC_BK, rpad = ((size_t)B + TC_BR - 1) / TC_BR * TC_BR;
         DALLOC(m->digits, rpad * 8 * kpad);
         // split-K partials: KS * Rpad * Mpad * 16 with KS * tiles <= 2 * SMs + tiles
-        m->gpart_bytes = (size_t)(4 * dev_info().sms + 8) * TC_BM * TC_BR * 16;
+        m->gpart_bytes = (size_t)(8 * dev_info().sms + 8) * TC_BM * TC_BR * 16;
         DALLOC(m->gpart, m->gpart_bytes);
     }
     // pinned ints: [0, B) results, then (max_seq + 2) slots of 2*NB (token, pos)
