@@ -920,6 +920,18 @@ IQ_API int iq_model_create(const iq_config *cfg, int max_batch, int device, iq_m
 IQ_API int iq_model_destroy(iq_model *m) {
     if (!m) return IQ_ERR_ARG;
     cudaSetDevice(m->dev);
+    if (m->failed && m->s) {
+        // an aborted collective may still hold the stream: wait a bounded time;
+        // if it never drains, the device buffers are left to the process exit
+        // (cudaFree would wait for the device, i.e. forever)
+        const int64_t t0 = ms_now();
+        while (cudaStreamQuery(m->s) == cudaErrorNotReady && ms_now() - t0 < 10000)
+            std::this_thread::sleep_for(std::chrono::milliseconds(1));
+        if (cudaStreamQuery(m->s) == cudaErrorNotReady) {
+            delete m;
+            return IQ_ERR_TIMEOUT;
+        }
+    }
     if (m->s) cudaStreamSynchronize(m->s);
     if (m->graph) cudaGraphExecDestroy(m->graph);
     if (m->graph_s) cudaGraphExecDestroy(m->graph_s);

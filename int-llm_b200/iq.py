@@ -396,8 +396,8 @@ class Model:
 
     def close(self):
         if self.h:
-            _call("iq_model_destroy", self.h)
-            self.h = ctypes.c_void_p()
+            h, self.h = self.h, ctypes.c_void_p()   # the handle is gone even when destroy reports an error
+            _call("iq_model_destroy", h)
 
     def __del__(self):
         try:

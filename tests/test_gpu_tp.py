@@ -77,8 +77,16 @@ def _rank_leave(rank, world, nid, q):
     """Rank 1 finishes one generate and leaves between steps (no collective in
     flight); rank 0's next generate finds no peer and must return an error
     within its timeout instead of blocking forever."""
+    import faulthandler
+    import sys
+    import time
     import torch
+    faulthandler.dump_traceback_later(200, exit=False)   # names the call if anything blocks
     torch.cuda.set_device(rank)
+    t0 = time.time()
+
+    def note(what):
+        print(f"[rank {rank} +{time.time() - t0:.1f}s] {what}", file=sys.stderr, flush=True)
     try:
         g = json.load(open(os.path.join(GOLD, "tiny_model.json")))
         c = g["config"]
@@ -90,18 +98,25 @@ def _rank_leave(rank, world, nid, q):
             q.put((rank, toks == g["tokens"][:len(toks)], "left"))
             os._exit(0)   # leaves without destroying its communicator
         iq.lib().iq_model_set_timeout(m.h, 3000)
+        note("peer gone; generate")
         try:
             m.generate(np.array(g["prompt"]), 8)
             status = 0
         except iq.IQError as e:
             status = e.status
+        note(f"generate returned {status}")
         try:
             m.generate(np.array(g["prompt"]), 8)
             after = 0
         except iq.IQError as e:
             after = e.status
-        m.close()
+        note(f"second generate returned {after}")
         q.put((rank, status in (-4, -5) and after == -7, (status, after)))
+        try:   # a failed model's destroy is bounded too (IQ_ERR_TIMEOUT if the stream never drains)
+            m.close()
+        except iq.IQError as e:
+            note(f"close returned {e.status}")
+        note("closed")
     except Exception as e:
         q.put((rank, False, repr(e)))
 
