@@ -354,6 +354,14 @@ IQ_API int iq_model_set_kv_packed(iq_model *m, int k_bits, int v_bits);
  * without a GPU (scenario 0: completes; 1: communicator error; 2: never
  * completes; 3: stream error) and reports whether it aborted. */
 IQ_API int iq_model_set_timeout(iq_model *m, int64_t ms);
+/* Host-side liveness of the other tensor-parallel ranks (a store, heartbeat or
+ * process table the host keeps): fn(ctx) is called at the start of every call
+ * that launches work on a model with tp_size > 1; nonzero means a peer left,
+ * and the call returns IQ_ERR_NCCL before enqueueing anything (no collective
+ * is ever posted towards the missing rank); the model then refuses further
+ * work (IQ_ERR_STATE) and iq_model_destroy aborts its communicator. fn NULL:
+ * no check (the default; the bounded wait above still applies). */
+IQ_API int iq_model_set_peer_check(iq_model *m, int (*fn)(void *ctx), void *ctx);
 IQ_API int iq_selftest_watchdog(int scenario, int *aborted, int *polls);
 IQ_API int iq_model_decode_info(iq_model *m, int *persistent, int *grid);
 /* Diagnostics of the persistent kernel: microseconds per grid barrier with

@@ -112,7 +112,9 @@ struct iq_model {
     std::vector<bool> loaded_layer;
     // persistent decode kernel (k_decode_token) for batch 1 without tensor
     // parallelism: requested mode, and its state once prepared
-    bool failed = false;        // the communicator was aborted: the model is unusable
+    bool failed = false;        // the communicator was aborted or a peer left: the model is unusable
+    int (*peer_check)(void *) = nullptr;   // host-side liveness of the other ranks (nonzero: one left)
+    void *peer_ctx = nullptr;
     int64_t timeout_ms = 60000; // bounded host waits under tensor parallelism
     bool want_logits = false;   // decode steps also gather the full logits (TP; hashing callers)
     int kv_kbits = 0, kv_vbits = 0;   // packed KV cache (K and V code widths); 0 = exact
@@ -681,6 +683,20 @@ static bool model_ready(iq_model *m) {
     return true;
 }
 
+// Entry gate of every call that launches work: IQ_ERR_ARG / IQ_ERR_STATE as
+// model_ready, and, under tensor parallelism, the host-side peer check before
+// anything is enqueued: a rank that left between steps is found here, so no
+// collective is ever launched towards it (IQ_ERR_NCCL; the model is failed).
+static int model_gate(iq_model *m) {
+    if (!m) return IQ_ERR_ARG;
+    if (int g_ = model_gate(m)) return g_;
+    if (m->sh.P > 1 && m->peer_check && m->peer_check(m->peer_ctx)) {
+        m->failed = true;
+        return IQ_ERR_NCCL;
+    }
+    return IQ_OK;
+}
+
 // ----------------------------------------------------------- host helpers
 
 static int h2d(void *dst, const void *src, size_t bytes) {
@@ -935,7 +951,10 @@ IQ_API int iq_model_destroy(iq_model *m) {
     if (m->s) cudaStreamSynchronize(m->s);
     if (m->graph) cudaGraphExecDestroy(m->graph);
     if (m->graph_s) cudaGraphExecDestroy(m->graph_s);
-    if (m->comm) ncclCommDestroy(m->comm);
+    if (m->comm) {
+        if (m->failed) ncclCommAbort(m->comm);   // a peer left: no collective to complete
+        else ncclCommDestroy(m->comm);
+    }
     void *bufs[] = {m->embed, m->fnorm, m->lm, m->rcos, m->rsin, m->hidden, m->normed, m->qkv, m->att,
                     m->gu, m->act, m->logits, m->att_l, m->proj_l, m->act_l, m->logits_l, m->gath,
                     m->proj_full, m->d_tok, m->d_pos, m->d_arg, m->d_hist, m->racc, m->digits, m->gpart, m->asc, m->amx, m->asum, m->d_seq,
@@ -1106,7 +1125,7 @@ static int enqueue_prefill(iq_model *m, int sq, const int *prompt, int L, std::v
 }
 
 IQ_API int iq_forward(iq_model *m, int token, int pos, int64_t *logits, int *argmax_out) {
-    if (!model_ready(m)) return m ? IQ_ERR_STATE : IQ_ERR_ARG;
+    if (int g_ = model_gate(m)) return g_;
     if (token < 0 || token >= m->c.vocab_size || pos < 0 || pos >= m->c.max_seq_len) return IQ_ERR_RANGE;
     IQ_CUDA(cudaSetDevice(m->dev));
     IQ_WAIT(m);
@@ -1148,7 +1167,7 @@ static int run_step(iq_model *m, int B, int tmax) {
 IQ_API int iq_generate(iq_model *m, const int *prompt, int plen, int max_new, int *out, int *n_out,
                        uint64_t *logit_hash) {
     if (!m || !prompt || !out || !n_out || plen < 1 || max_new < 1) return IQ_ERR_ARG;
-    if (!model_ready(m)) return IQ_ERR_STATE;
+    if (int g_ = model_gate(m)) return g_;
     const iq_config &c = m->c;
     *n_out = -1;
     for (int i = 0; i < plen; i++)
@@ -1201,7 +1220,7 @@ IQ_API int iq_generate(iq_model *m, const int *prompt, int plen, int max_new, in
 
 IQ_API int iq_generate_sampled(iq_model *m, const int *prompt, int plen, int max_new, int64_t temperature,
                                int top_k, int64_t top_p, uint64_t seed, int *out, int *n_out, uint64_t *logit_hash) {
-    if (!model_ready(m)) return m ? IQ_ERR_STATE : IQ_ERR_ARG;
+    if (int g_ = model_gate(m)) return g_;
     IQ_CUDA(cudaSetDevice(m->dev));
     SampleState st{};
     st.temperature = temperature;
@@ -1224,7 +1243,7 @@ IQ_API int iq_generate_sampled(iq_model *m, const int *prompt, int plen, int max
 IQ_API int iq_generate_batch(iq_model *m, const int *prompts, int plen, int max_new, int *out, int *n_out,
                              uint64_t *logit_hashes) {
     if (!m || !prompts || !out || !n_out || plen < 1 || max_new < 1) return IQ_ERR_ARG;
-    if (!model_ready(m)) return IQ_ERR_STATE;
+    if (int g_ = model_gate(m)) return g_;
     const iq_config &c = m->c;
     const int B = m->max_batch;
     for (int i = 0; i < B * plen; i++)
@@ -1354,6 +1373,13 @@ IQ_API int iq_model_set_kv_packed(iq_model *m, int k_bits, int v_bits) {
     return iq_model_reset(m);
 }
 
+IQ_API int iq_model_set_peer_check(iq_model *m, int (*fn)(void *ctx), void *ctx) {
+    if (!m) return IQ_ERR_ARG;
+    m->peer_check = fn;
+    m->peer_ctx = ctx;
+    return IQ_OK;
+}
+
 IQ_API int iq_model_set_timeout(iq_model *m, int64_t ms) {
     if (!m || ms < 1) return IQ_ERR_ARG;
     m->timeout_ms = ms;
@@ -1439,7 +1465,7 @@ IQ_API int iq_model_decode_stamps(iq_model *m, int64_t *out, int n) {
 
 IQ_API int iq_model_decode_info(iq_model *m, int *persistent, int *grid) {
     if (!m || !persistent || !grid) return IQ_ERR_ARG;
-    if (!model_ready(m)) return IQ_ERR_STATE;
+    if (int g_ = model_gate(m)) return g_;
     IQ_CUDA(cudaSetDevice(m->dev));
     int rc = dec_prepare(m);
     if (rc) return rc;
@@ -1450,7 +1476,7 @@ IQ_API int iq_model_decode_info(iq_model *m, int *persistent, int *grid) {
 
 IQ_API int iq_model_weight_bytes(iq_model *m, int64_t *decode_bytes, int64_t *gemm_bytes) {
     if (!m || !decode_bytes || !gemm_bytes) return IQ_ERR_ARG;
-    if (!model_ready(m)) return IQ_ERR_STATE;
+    if (int g_ = model_gate(m)) return g_;
     int64_t d = packed_bytes(m->plm), g = 0;
     for (const std::vector<Packed> *v : {&m->pqkv, &m->po, &m->pgu, &m->pdown})
         for (const Packed &P : *v) d += packed_bytes(P);
@@ -1464,7 +1490,7 @@ IQ_API int iq_model_weight_bytes(iq_model *m, int64_t *decode_bytes, int64_t *ge
 
 IQ_API int iq_decode_steps_timed(iq_model *m, int pos0, int steps, float *ms) {
     if (!m || !ms || steps < 1 || pos0 < 0 || pos0 + steps > m->c.max_seq_len) return IQ_ERR_ARG;
-    if (!model_ready(m)) return IQ_ERR_STATE;
+    if (int g_ = model_gate(m)) return g_;
     IQ_CUDA(cudaSetDevice(m->dev));
     int rc;
     std::vector<int> tok(m->max_batch), pos(m->max_batch, pos0);

@@ -82,6 +82,7 @@ SIGNATURES = {
     "iq_model_weight_bytes": (_I, [_P, _P, _P]),
     "iq_model_set_decode": (_I, [_P, _I]),
     "iq_model_set_timeout": (_I, [_P, _I64]),
+    "iq_model_set_peer_check": (_I, [_P, _P, _P]),
     "iq_model_set_kv_packed": (_I, [_P, _I, _I]),
     "iq_selftest_watchdog": (_I, [_I, _P, _P]),
     "iq_model_decode_info": (_I, [_P, _P, _P]),
@@ -462,6 +463,18 @@ class Model:
     def set_attention(self, short_max):
         """Contexts up to short_max use the single-kernel attention (0 = phased only)."""
         _call("iq_model_set_attention", self.h, short_max)
+
+    PEER_CHECK = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p)
+
+    def set_peer_check(self, fn):
+        """fn() -> bool, True when another tensor-parallel rank has left; checked
+        before every call that launches work (iq_model_set_peer_check)."""
+        self._peer_cb = self.PEER_CHECK(lambda _ctx: 1 if fn() else 0) if fn else None
+        _call("iq_model_set_peer_check", self.h,
+              ctypes.cast(self._peer_cb, ctypes.c_void_p) if fn else None, None)
+
+    def set_timeout(self, ms):
+        _call("iq_model_set_timeout", self.h, int(ms))
 
     def set_kv_packed(self, k_bits, v_bits):
         """The reference's --kv-packed KbVb cache (0, 0 = exact)."""

@@ -73,10 +73,12 @@ def test_tp2_generate_matches_goldens():
     assert res == {0: (True, None), 1: (True, None)}, res
 
 
-def _rank_leave(rank, world, nid, q):
+def _rank_leave(rank, world, nid, q, gone):
     """Rank 1 finishes one generate and leaves between steps (no collective in
-    flight); rank 0's next generate finds no peer and must return an error
-    within its timeout instead of blocking forever."""
+    flight) after marking itself gone in a host-side store (an Event); rank 0
+    learns of it from its peer check before its next launch, so its generate
+    returns IQ_ERR_NCCL having posted no collective, and the model then refuses
+    work (IQ_ERR_STATE)."""
     import faulthandler
     import sys
     import time
@@ -96,8 +98,11 @@ def _rank_leave(rank, world, nid, q):
         toks, _ = m.generate(np.array(g["prompt"]), 8)
         if rank == 1:
             q.put((rank, toks == g["tokens"][:len(toks)], "left"))
+            gone.set()
             os._exit(0)   # leaves without destroying its communicator
-        iq.lib().iq_model_set_timeout(m.h, 3000)
+        m.set_timeout(3000)
+        m.set_peer_check(gone.is_set)
+        gone.wait(60)
         note("peer gone; generate")
         try:
             m.generate(np.array(g["prompt"]), 8)
@@ -111,7 +116,7 @@ def _rank_leave(rank, world, nid, q):
         except iq.IQError as e:
             after = e.status
         note(f"second generate returned {after}")
-        q.put((rank, status in (-4, -5) and after == -7, (status, after)))
+        q.put((rank, status == -5 and after == -7, (status, after)))
         try:   # a failed model's destroy is bounded too (IQ_ERR_TIMEOUT if the stream never drains)
             m.close()
         except iq.IQError as e:
@@ -121,12 +126,11 @@ def _rank_leave(rank, world, nid, q):
         q.put((rank, False, repr(e)))
 
 
-def test_tp2_peer_leaving_between_steps_times_out_cleanly():
-    """Failure detection without a GPU fault: the surviving rank's collective
-    is ended by the library's bounded wait (ncclCommAbort after the timeout or
-    on NCCL's asynchronous error), the call returns IQ_ERR_TIMEOUT or
-    IQ_ERR_NCCL, and the model refuses further work (IQ_ERR_STATE). NVLS is
-    off in both ranks."""
+def test_tp2_peer_leaving_between_steps_fails_cleanly():
+    """Failure detection without a GPU fault: a rank leaves between steps, the
+    surviving rank learns of it on the host before its next launch (the peer
+    check), its call returns IQ_ERR_NCCL without posting a collective, and the
+    model refuses further work (IQ_ERR_STATE). NVLS is off in both ranks."""
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -135,13 +139,14 @@ def test_tp2_peer_leaving_between_steps_times_out_cleanly():
     nid = iq.nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_leave, args=(r, 2, nid, q)) for r in range(2)]
+    gone = ctx.Event()
+    procs = [ctx.Process(target=_rank_leave, args=(r, 2, nid, q, gone)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
     try:
         for _ in procs:
-            r, ok, info = q.get(timeout=300)
+            r, ok, info = q.get(timeout=240)
             res[r] = (ok, info)
     finally:
         for p in procs:
