@@ -17,6 +17,8 @@ GOLD = os.path.join(os.path.dirname(__file__), "golden")
 
 
 def _rank(rank, world, ids, q):
+    import faulthandler
+    faulthandler.dump_traceback_later(150, exit=False)   # names the call if anything blocks
     import torch
     torch.cuda.set_device(rank)
     try:
@@ -63,7 +65,7 @@ def test_tp2_generate_matches_goldens():
     res = {}
     try:
         for _ in procs:
-            r, ok, err = q.get(timeout=600)
+            r, ok, err = q.get(timeout=240)
             res[r] = (ok, err)
     finally:
         for p in procs:
@@ -80,10 +82,10 @@ def _rank_leave(rank, world, nid, q, gone):
     returns IQ_ERR_NCCL having posted no collective, and the model then refuses
     work (IQ_ERR_STATE)."""
     import faulthandler
+    faulthandler.dump_traceback_later(200, exit=False)   # names the call if anything blocks
     import sys
     import time
     import torch
-    faulthandler.dump_traceback_later(200, exit=False)   # names the call if anything blocks
     torch.cuda.set_device(rank)
     t0 = time.time()
 
