@@ -118,7 +118,7 @@ def _rank_leave(rank, world, nid, q, gone):
         except iq.IQError as e:
             after = e.status
         note(f"second generate returned {after}")
-        q.put((rank, status == -5 and after == -7, (status, after)))
+        q.put((rank, status == -4 and after == -7, (status, after)))   # IQ_ERR_NCCL, IQ_ERR_STATE
         try:   # a failed model's destroy is bounded too (IQ_ERR_TIMEOUT if the stream never drains)
             m.close()
         except iq.IQError as e:
