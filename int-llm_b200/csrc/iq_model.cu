@@ -689,7 +689,7 @@ static bool model_ready(iq_model *m) {
 // collective is ever launched towards it (IQ_ERR_NCCL; the model is failed).
 static int model_gate(iq_model *m) {
     if (!m) return IQ_ERR_ARG;
-    if (int g_ = model_gate(m)) return g_;
+    if (!model_ready(m)) return IQ_ERR_STATE;
     if (m->sh.P > 1 && m->peer_check && m->peer_check(m->peer_ctx)) {
         m->failed = true;
         return IQ_ERR_NCCL;

@@ -18,6 +18,7 @@ GOLD = os.path.join(os.path.dirname(__file__), "golden")
 
 def _rank(rank, world, ids, q):
     import faulthandler
+    faulthandler.enable()                                # a crash prints its stack too
     faulthandler.dump_traceback_later(150, exit=False)   # names the call if anything blocks
     import torch
     torch.cuda.set_device(rank)
@@ -82,6 +83,7 @@ def _rank_leave(rank, world, nid, q, gone):
     returns IQ_ERR_NCCL having posted no collective, and the model then refuses
     work (IQ_ERR_STATE)."""
     import faulthandler
+    faulthandler.enable()                                # a crash prints its stack too
     faulthandler.dump_traceback_later(200, exit=False)   # names the call if anything blocks
     import sys
     import time
