@@ -707,7 +707,7 @@ static int stream_bytes(cudaStream_t s, size_t bytes, uint8_t **out) {
     return IQ_OK;
 }
 
-// Split-K factor: the ks in 1..16 (each split keeping >= IQ_GEMM_MINKB K blocks,
+// Split-K factor for decode-sized batches: the ks in 1..16 (each split keeping >= IQ_GEMM_MINKB K blocks,
 // default 8: the per-plane epilogue fold is a fixed cost per CTA) that
 // minimises waves x K blocks per split, i.e. the time of the longest SM with
 // one CTA per SM; ties go to the smaller ks (less partial traffic).
@@ -715,7 +715,10 @@ static int gemm_ksplit(const PackedTC &P, int R) {
     static const int minkb = getenv("IQ_GEMM_MINKB") ? std::max(1, atoi(getenv("IQ_GEMM_MINKB"))) : 8;
     const int Rpad = (R + TC_BR - 1) / TC_BR * TC_BR;
     const int tiles = (P.Mpad / TC_BM) * (Rpad / TC_BR), KBall = P.Kpad / TC_BK, sms = dev_info().sms;
-    if (tiles >= 2 * sms) return 1;   // two or more waves: the tile count already balances
+    // a full wave of tiles at prefill-sized batches: the partials' traffic outweighs
+    // the balance (measured: config-2 down 0.146 -> 0.184 ms at ks = 4); two or
+    // more waves: the tile count already balances
+    if ((tiles >= sms && Rpad > 128) || tiles >= 2 * sms) return 1;
     int best = 1;
     long best_cost = (long)((tiles + sms - 1) / sms) * KBall;
     for (int ks = 2; ks <= 16 && KBall / ks >= minkb; ks++) {

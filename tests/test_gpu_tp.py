@@ -102,6 +102,8 @@ def _rank_leave(rank, world, nid, q, gone):
         toks, _ = m.generate(np.array(g["prompt"]), 8)
         if rank == 1:
             q.put((rank, toks == g["tokens"][:len(toks)], "left"))
+            q.close()
+            q.join_thread()   # the message is in the pipe and the queue's lock released before _exit
             gone.set()
             os._exit(0)   # leaves without destroying its communicator
         m.set_timeout(3000)
