@@ -178,3 +178,161 @@ def test_bf16_form_dot_identity():
             res += x * (w - (v << 24))
         got = ((acc - (U << 63) - (X << 22)) << 24) + res
         assert got & M128 == want, trial
+
+
+# ---- tensor-core attention and fp_div (exact Python integers) -------------
+
+M64 = (1 << 64) - 1
+
+
+def _bytes_signed_top(x):
+    """7 unsigned bytes and a signed top byte: x = sum_i b_i 2^(8i)."""
+    u = x & M64
+    b = [(u >> (8 * i)) & 0xFF for i in range(8)]
+    if b[7] >= 128:
+        b[7] -= 256
+    return b
+
+
+def _fp_mul(a, b):
+    return ((a * b) >> 48) & M64
+
+
+def test_score_diagonals_mod_2_112():
+    """k_attn_scores_tc: sum over diagonals s = i + j <= 13 of 2^(8s) sum_d q_i k_j,
+    each diagonal within int32, recombined in three int64 groups, gives the
+    reference's (q . k >> 48) mod 2^64 (the (7, 7) pair only adds multiples of 2^112)."""
+    rng = random.Random(5)
+    for hd in (32, 64, 128, 256):
+        for _ in range(40):
+            mode = rng.randrange(3)
+            def val():
+                if mode == 0:
+                    return rng.randrange(-(1 << 63), 1 << 63)
+                if mode == 1:
+                    return rng.choice([-(1 << 63), (1 << 63) - 1, -1, 0, 1])
+                return rng.randrange(-(1 << 52), 1 << 52)
+            q = [val() for _ in range(hd)]
+            k = [val() for _ in range(hd)]
+            want = (sum(a * b for a, b in zip(q, k)) >> 48) & M64
+            qb = [_bytes_signed_top(a) for a in q]
+            kb = [_bytes_signed_top(b) for b in k]
+            D = [0] * 14
+            for i in range(8):
+                for j in range(8):
+                    if i + j > 13:
+                        continue
+                    D[i + j] += sum(kb[d][i] * qb[d][j] for d in range(hd))
+            assert all(-(1 << 31) <= v < (1 << 31) for v in D)
+            G0 = sum(D[s] << (8 * s) for s in range(5))
+            G1 = sum(D[s] << (8 * (s - 5)) for s in range(5, 10))
+            G2 = sum(D[s] << (8 * (s - 10)) for s in range(10, 14))
+            assert all(-(1 << 61) <= g < (1 << 61) for g in (G0, G1, G2))
+            dot = (G0 + (G1 << 40) + (G2 << 80)) % (1 << 128)
+            assert (dot >> 48) & M64 == want
+
+
+def _r_pieces(p, v):
+    """R = (p v) mod 2^48 from 32-bit pieces, as k_attn_pv_tc's PTX block:
+    lo(p) lo(v) mod 2^32 + 2^32 ((hi(lo(p) lo(v)) + lo(p) hi(v) + hi(p) lo(v)) mod 2^16)."""
+    vu = v & M64
+    plo, phi, vlo, vhi = p & 0xFFFFFFFF, p >> 32, vu & 0xFFFFFFFF, vu >> 32
+    w = plo * vlo
+    hi = ((w >> 32) + plo * vhi + phi * vlo) & 0xFFFF
+    return (w & 0xFFFFFFFF) + (hi << 32)
+
+
+def test_pv_floor_identity_and_remainder_pieces():
+    """k_attn_pv_tc: sum_t fp_mul(p_t, v_t) = (sum p v - sum R) / 2^48 mod 2^64 with
+    R_t = (p_t v_t) mod 2^48 from 32-bit pieces; the products' byte-plane diagonals
+    (p: 7 unsigned bytes, v: signed top) in int32; the four int64 limb sums
+    weighted 2^0, 2^32, 2^64, 2^96 recombine to the same value."""
+    rng = random.Random(9)
+    for T in (1, 7, 64, 256):
+        for _ in range(30):
+            ps = [rng.choice([0, 1 << 48, rng.randrange(0, (1 << 48) + 1), rng.randrange(0, 1 << 40)])
+                  for _ in range(T)]
+            vs = [rng.choice([rng.randrange(-(1 << 63), 1 << 63), rng.randrange(-(1 << 50), 1 << 50),
+                              -(1 << 63), (1 << 63) - 1]) for _ in range(T)]
+            want = sum(_fp_mul(p, v) for p, v in zip(ps, vs)) & M64
+            for p, v in zip(ps, vs):
+                assert _r_pieces(p, v) == (p * v) % (1 << 48)
+            Rsum = sum(_r_pieces(p, v) for p, v in zip(ps, vs))
+            assert Rsum < 1 << 56
+            pb = [[(p >> (8 * j)) & 0xFF for j in range(7)] for p in ps]
+            vb = [_bytes_signed_top(v) for v in vs]
+            D = [0] * 14
+            for i in range(8):
+                for j in range(7):
+                    D[i + j] += sum(vb[t][i] * pb[t][j] for t in range(T))
+            assert all(-(1 << 31) <= x < (1 << 31) for x in D)
+            G = [0, 0, 0, 0]
+            for s in range(14):
+                G[s >> 2] += D[s] << (8 * (s & 3))
+            G[0] -= Rsum
+            assert all(-(1 << 63) <= g < (1 << 63) for g in G)
+            X = (G[0] + (G[1] << 32) + (G[2] << 64) + (G[3] << 96)) % (1 << 128)
+            assert X % (1 << 48) == 0
+            assert (X >> 48) & M64 == want
+
+
+def _fp_div_ref(a, b):
+    ma, mb = abs(a), abs(b)
+    q = ((ma << 48) // mb) & M64
+    return q if (a < 0) == (b < 0) else (-q) & M64
+
+
+def _fp_div_fast(a, b):
+    """The device fp_div: a double estimate of |a| 2^48 / |b| corrected by one
+    exact remainder step while it is below 2^50 and |b| < 2^61."""
+    ma, mb = abs(a) & M64, abs(b) & M64
+    qd = float(ma) * 281474976710656.0 / float(mb)
+    if qd < 2.0 ** 50 and mb < (1 << 61):
+        q = int(qd)
+        r = ((ma << 48) - q * mb) & M64
+        if r >= 1 << 63:
+            r -= 1 << 64
+        if r < 0:
+            q -= 1
+        elif r >= mb:
+            q += 1
+    else:
+        q = ((ma << 48) // mb) & M64
+    return q if (a < 0) == (b < 0) else (-q) & M64
+
+
+def test_fp_div_estimate_and_correct():
+    rng = random.Random(13)
+    cases = []
+    for _ in range(20000):
+        b = rng.randrange(1, 1 << rng.randrange(1, 63))
+        k = rng.randrange(4)
+        if k == 0:
+            a = ((1 << 50) + rng.randrange(-4, 5)) * b >> 48
+        elif k == 1:
+            a = (rng.randrange(0, 1 << 49) * b >> 48) + rng.randrange(-1, 2)
+        elif k == 2:
+            b = (1 << 61) + rng.randrange(-8, 9)
+            a = rng.randrange(0, 1 << 63)
+        else:
+            a = rng.randrange(0, 1 << rng.randrange(1, 64))
+        cases.append((max(0, min(a, (1 << 63) - 1)), b))
+    ext = [-(1 << 63), (1 << 63) - 1, 1, -1, 1 << 48, 3]
+    for a in ext:
+        for b in ext:
+            cases.append((a, b))
+    for a, b in cases:
+        for sa, sb in ((1, 1), (-1, 1), (1, -1), (-1, -1)):
+            x, y = sa * a, sb * b
+            if not (-(1 << 63) <= x < (1 << 63) and -(1 << 63) <= y < (1 << 63)) or y == 0:
+                continue
+            assert _fp_div_fast(x, y) == _fp_div_ref(x, y), (x, y)
+
+
+def test_unsigned_square_equals_fp_mul_r_r():
+    """fp_exp's squarings: fp_mul(r, r) from the unsigned square of |r|."""
+    rng = random.Random(17)
+    for _ in range(20000):
+        r = rng.randrange(-(1 << 63), 1 << 63)
+        m = abs(r) & M64
+        assert (((m * m) >> 48) & M64) == (((r * r) >> 48) & M64)
